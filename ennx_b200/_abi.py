@@ -1,0 +1,105 @@
+"""ctypes binding of the C ABI in ``include/ennx_b200.h``.
+
+The shared library is built in-tree (``ennx_b200/_lib/libennx_b200.so``) by
+``ennx_b200.build``.  There is no CPU fallback: if the library is missing or
+the device is not sm_100, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libennx_b200.so"
+
+OK, INVALID_ARGUMENT, OVERFLOW, CUDA_ERROR, TIMEOUT, UNSUPPORTED = range(6)
+EPI_BF16, EPI_F32, EPI_SWIGLU, EPI_ROWSCALE, EPI_LSE = range(5)
+
+
+class EnnxB200Error(RuntimeError):
+    """A status other than ENNX_B200_OK returned by the C ABI."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class EnnxB200ValueError(EnnxB200Error, ValueError):
+    """INVALID_ARGUMENT / OVERFLOW: the reference raises ValueError for these
+    (rust/crates/ennx-py/src/py_weights.rs:27-29)."""
+
+
+class DenseLeaf(ctypes.Structure):
+    _fields_ = [("key", ctypes.c_uint64), ("offset", ctypes.c_size_t), ("len", ctypes.c_size_t),
+                ("scale", ctypes.c_float)]
+
+
+class DenseTerm(ctypes.Structure):
+    _fields_ = [("seed", ctypes.c_uint64), ("coefficient", ctypes.c_float)]
+
+
+class DenseView(ctypes.Structure):
+    _fields_ = [("key", ctypes.c_uint64), ("start", ctypes.c_uint64), ("scale", ctypes.c_float)]
+
+
+class GemmParams(ctypes.Structure):
+    _fields_ = [("m", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
+                ("lda", ctypes.c_int64), ("ldb", ctypes.c_int64), ("ldc", ctypes.c_int64),
+                ("groups", ctypes.c_int32), ("b_group_rows", ctypes.c_int32),
+                ("group_offsets", ctypes.c_void_p), ("epilogue", ctypes.c_int32),
+                ("alpha", ctypes.c_float), ("residual", ctypes.c_void_p), ("ldr", ctypes.c_int64),
+                ("row_scale", ctypes.c_void_p), ("targets", ctypes.c_void_p),
+                ("lse_partial", ctypes.c_void_p), ("target_logit", ctypes.c_void_p)]
+
+
+_P = ctypes.c_void_p
+_SZ = ctypes.c_size_t
+_I32 = ctypes.c_int32
+_U32 = ctypes.c_uint32
+_U64 = ctypes.c_uint64
+_F32 = ctypes.c_float
+
+SIGNATURES = {
+    "ennx_b200_abi_version": (_U32, []),
+    "ennx_b200_last_error": (ctypes.c_char_p, []),
+    "ennx_b200_device_check": (_I32, []),
+    "ennx_b200_device_status": (_I32, [_P]),
+    "ennx_b200_dense_apply_f32": (_I32, [_P, _SZ, _P, _SZ, _P, _SZ, _P, _P, _P]),
+    "ennx_b200_dense_apply_bf16": (_I32, [_P, _SZ, _P, _SZ, _P, _SZ, _P, _P]),
+    "ennx_b200_check_bf16": (_I32, [_P, _SZ, _P, _P]),
+    "ennx_b200_dense_linear_f32": (_I32, [_P, _SZ, _P, _SZ, _P, DenseView, DenseView, _P, _SZ, _P, _P]),
+    "ennx_b200_perturb_bf16": (_I32, [_P, _SZ, _U64, _U32, _U32, _F32, _P, _P, _P]),
+    "ennx_b200_gemm_bf16": (_I32, [_P, _P, _P, _P, _P]),
+}
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the in-tree library (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise EnnxB200Error(CUDA_ERROR, f"{LIB_PATH} is missing: run `python -m ennx_b200.build`")
+        L = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(L, name, None)
+            if fn is None:
+                continue
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def check(status: int, what: str = "") -> None:
+    if status == OK:
+        return
+    msg = lib().ennx_b200_last_error().decode(errors="replace")
+    text = f"{what}: {msg}" if what else msg
+    if status in (INVALID_ARGUMENT, OVERFLOW):
+        raise EnnxB200ValueError(status, text)
+    raise EnnxB200Error(status, text)
+
+
+def call(name: str, *args) -> None:
+    check(getattr(lib(), name)(*args), name)

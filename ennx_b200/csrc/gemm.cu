@@ -1,0 +1,388 @@
+// gemm.cu -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
+//
+// C = A . B^T, A [M, K] and B [N, K] bf16 with K contiguous ("K-major"), fp32
+// accumulation in tensor memory.  One CTA per SM loops over 128x256 output
+// tiles:
+//   warp 0      TMA producer: 64-wide K slices of A (128x64) and B (256x64)
+//               into a 4-stage ring of 128B-swizzled shared-memory tiles;
+//   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators)
+//               and issues tcgen05.mma (M=128, N=256, K=16) from one thread;
+//               tcgen05.commit frees a ring slot / publishes an accumulator;
+//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from their TMEM
+//               lane quarter, fused epilogue math, 16-byte global stores.
+// The two accumulators let tile i's epilogue overlap tile i+1's main loop.
+// No cluster, no multicast: every CTA loads its own tiles.
+//
+// Grouped mode runs several independent problems that share A/C rows
+// segments and use different B row blocks (MoE experts, antithetic
+// candidates) in one launch.
+//
+// The reference has no GEMM (its only contraction is the fp32 GEMV of
+// cuda/kernels/src/lib.rs:2359-2423); this kernel is the B200 replacement of
+// the "linear" operator for M > 1 (rust/crates/ennx/src/dense/linear.rs:484).
+#include <string.h>
+
+#include "common.cuh"
+
+namespace ennx {
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+constexpr int B_BYTES = BN * BK * 2;  // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int MAX_GROUPS = 256;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 4096 /*barriers, tables*/;
+constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN);
+
+struct Args {
+  int M, N, K;
+  int groups, rows_per_group, b_group_rows;
+  const int* group_offsets;
+  int epi;
+  float alpha;
+  void* C;
+  long long ldc;
+  const uint16_t* R;
+  long long ldr;
+  const float* row_scale;
+  const int* targets;
+  float2* lse;
+  float* tlogit;
+  int n_tiles;
+  int* err;
+};
+
+struct Smem {  // lives after the stage ring
+  uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+  int total_tiles;
+  int row0[MAX_GROUPS + 1];       // first A/C row of each group
+  int tile0[MAX_GROUPS + 1];      // first tile index of each group
+};
+
+struct TileInfo {
+  int g, mt, nt, row0, rows;
+};
+
+__device__ __forceinline__ TileInfo decode_tile(const Smem& s, const Args& a, int tile) {
+  int lo = 0, hi = a.groups - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (s.tile0[mid] <= tile) lo = mid; else hi = mid - 1;
+  }
+  TileInfo t;
+  t.g = lo;
+  t.row0 = s.row0[lo];
+  t.rows = s.row0[lo + 1] - s.row0[lo];
+  int mtiles = (t.rows + BM - 1) / BM;
+  int local = tile - s.tile0[lo];
+  t.mt = local % mtiles;
+  t.nt = local / mtiles;
+  return t;
+}
+
+__device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* ring = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  Smem& s = *reinterpret_cast<Smem*>(ring + STAGES * STAGE_BYTES);
+  uint8_t* sA = ring;
+  uint8_t* sB = ring + STAGES * A_BYTES;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < STAGES; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], 4); }
+    s.abort_flag = 0;
+    // group table: row offsets (device table or uniform split) and tile prefix
+    int tiles = 0;
+    for (int g = 0; g < a.groups; ++g) {
+      int r0 = a.group_offsets ? a.group_offsets[g] : g * a.rows_per_group;
+      int r1 = a.group_offsets ? a.group_offsets[g + 1] : (g + 1) * a.rows_per_group;
+      s.row0[g] = r0;
+      s.row0[g + 1] = r1;
+      s.tile0[g] = tiles;
+      int rows = r1 - r0;
+      tiles += (rows > 0 ? (rows + BM - 1) / BM : 0) * a.n_tiles;
+    }
+    s.tile0[a.groups] = tiles;
+    s.total_tiles = tiles;
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
+  if (warp == 1) { tmem_alloc(&s.tmem_base, TMEM_COLS); tmem_relinquish(); }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+  const int total = s.total_tiles;
+  const int KB = a.K / BK;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < total && !*(volatile int*)&s.abort_flag; tile += gridDim.x) {
+        TileInfo t = decode_tile(s, a, tile);
+        int arow = t.row0 + t.mt * BM;
+        int brow = t.g * a.b_group_rows + t.nt * BN;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&s.empty[stage], phase ^ 1u, a.err)) { s.abort_flag = 1; break; }
+          mbar_arrive_expect_tx(&s.full[stage], STAGE_BYTES);
+          tma_load_2d(sA + stage * A_BYTES, &tmA, &s.full[stage], kb * BK, arow);
+          tma_load_2d(sB + stage * B_BYTES, &tmB, &s.full[stage], kb * BK, brow);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < total && !*(volatile int*)&s.abort_flag; tile += gridDim.x, ++it) {
+        int acc = it & 1;
+        uint32_t acc_phase = (it >> 1) & 1;
+        if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1u, a.err)) { s.abort_flag = 1; break; }
+        tc_fence_after();
+        uint32_t d = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&s.full[stage], phase, a.err)) { s.abort_flag = 1; ok = false; break; }
+          tc_fence_after();
+          uint32_t abase = smem_u32(sA + stage * A_BYTES);
+          uint32_t bbase = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16(d, smem_desc_sw128(abase + k * 32), smem_desc_sw128(bbase + k * 32), IDESC,
+                     (kb | k) != 0);
+          umma_commit(&s.empty[stage]);
+          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+        }
+        if (!ok) break;
+        umma_commit(&s.tfull[acc]);
+      }
+    }
+  } else {
+    // epilogue warps 2..5; TMEM lane quarter = warp % 4
+    const int q = warp & 3;
+    const int r_in_tile = q * 32 + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+      int acc = it & 1;
+      uint32_t acc_phase = (it >> 1) & 1;
+      if (!mbar_wait(&s.tfull[acc], acc_phase, a.err)) { s.abort_flag = 1; break; }
+      tc_fence_after();
+      TileInfo t = decode_tile(s, a, tile);
+      const int mrow = t.mt * BM + r_in_tile;
+      const bool row_ok = mrow < t.rows;
+      const long long grow = (long long)t.row0 + mrow;
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
+      uint32_t v[32];
+
+      if (a.epi == ENNX_B200_EPI_SWIGLU) {
+        uint16_t* C = (uint16_t*)a.C;
+        for (int c = 0; c < BN / 2; c += 32) {
+          uint32_t u[32];
+          tmem_ld32(tbase + c, v);
+          tmem_ld32(tbase + c + BN / 2, u);
+          tmem_ld_wait();
+          int col0 = t.nt * (BN / 2) + c;
+          int ncols = a.N / 2;
+          if (row_ok) {
+            uint16_t* dst = C + grow * a.ldc + col0;
+            uint32_t pk[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              float g0 = __uint_as_float(v[2 * j]) * a.alpha, g1 = __uint_as_float(v[2 * j + 1]) * a.alpha;
+              float u0 = __uint_as_float(u[2 * j]) * a.alpha, u1 = __uint_as_float(u[2 * j + 1]) * a.alpha;
+              pk[j] = pack_bf16x2(silu(g0) * u0, silu(g1) * u1);
+            }
+            if (col0 + 32 <= ncols) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) st_global_v4(dst + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+            } else {
+              for (int j = 0; j < 32 && col0 + j < ncols; ++j) dst[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
+            }
+          }
+        }
+      } else if (a.epi == ENNX_B200_EPI_LSE) {
+        float m = -INFINITY, ssum = 0.0f, tl = 0.0f;
+        int tgt = row_ok ? a.targets[grow] : -1;
+        bool have_t = false;
+        for (int c = 0; c < BN; c += 32) {
+          tmem_ld32(tbase + c, v);
+          tmem_ld_wait();
+          int col0 = t.nt * BN + c;
+          float cm = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(v[j]) * a.alpha;
+            bool ok = col0 + j < a.N;
+            if (ok) cm = fmaxf(cm, x);
+            if (col0 + j == tgt) { tl = x; have_t = true; }
+          }
+          if (cm > -INFINITY) {
+            float nm = fmaxf(m, cm);
+            float acc_s = ssum * __expf(m - nm);
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < a.N) acc_s += __expf(__uint_as_float(v[j]) * a.alpha - nm);
+            ssum = acc_s;
+            m = nm;
+          }
+        }
+        if (row_ok) {
+          a.lse[grow * a.n_tiles + t.nt] = make_float2(m, ssum);
+          if (have_t) a.tlogit[grow] = tl;
+        }
+      } else {
+        const float rs = (a.epi == ENNX_B200_EPI_ROWSCALE && row_ok) ? a.row_scale[grow] : a.alpha;
+        for (int c = 0; c < BN; c += 32) {
+          tmem_ld32(tbase + c, v);
+          tmem_ld_wait();
+          int col0 = t.nt * BN + c;
+          if (!row_ok || col0 >= a.N) continue;
+          bool full = col0 + 32 <= a.N;
+          if (a.epi == ENNX_B200_EPI_F32) {
+            float* dst = (float*)a.C + grow * a.ldc + col0;
+            if (full) {
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                float x0 = __uint_as_float(v[4 * j]) * rs, x1 = __uint_as_float(v[4 * j + 1]) * rs;
+                float x2 = __uint_as_float(v[4 * j + 2]) * rs, x3 = __uint_as_float(v[4 * j + 3]) * rs;
+                st_global_v4(dst + 4 * j, __float_as_uint(x0), __float_as_uint(x1), __float_as_uint(x2),
+                             __float_as_uint(x3));
+              }
+            } else {
+              for (int j = 0; col0 + j < a.N; ++j) dst[j] = __uint_as_float(v[j]) * rs;
+            }
+          } else {
+            uint16_t* dst = (uint16_t*)a.C + grow * a.ldc + col0;
+            float x[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(v[j]) * rs;
+            if (a.R) {
+              const uint16_t* rp = a.R + grow * a.ldr + col0;
+              if (full) {
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  uint4 rv = *reinterpret_cast<const uint4*>(rp + 8 * j);
+                  uint32_t w4[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                  for (int h = 0; h < 4; ++h) {
+                    x[8 * j + 2 * h] += bf16_to_f32((uint16_t)(w4[h] & 0xffffu));
+                    x[8 * j + 2 * h + 1] += bf16_to_f32((uint16_t)(w4[h] >> 16));
+                  }
+                }
+              } else {
+                for (int j = 0; col0 + j < a.N; ++j) x[j] += bf16_to_f32(rp[j]);
+              }
+            }
+            if (full) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+                st_global_v4(dst + 8 * j, pack_bf16x2(x[8 * j], x[8 * j + 1]), pack_bf16x2(x[8 * j + 2], x[8 * j + 3]),
+                             pack_bf16x2(x[8 * j + 4], x[8 * j + 5]), pack_bf16x2(x[8 * j + 6], x[8 * j + 7]));
+            } else {
+              for (int j = 0; col0 + j < a.N; ++j) dst[j] = f32_to_bf16_rne(x[j]);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s.tempty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+bool g_attr_set[64];
+
+}  // namespace
+}  // namespace ennx
+
+using namespace ennx;
+
+extern "C" int32_t ennx_b200_gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint16_t* B,
+                                       void* C, void* stream) {
+  cudaStream_t st = (cudaStream_t)stream;
+  if (!p || !A || !B) return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: null argument");
+  const int M = p->m, N = p->n, K = p->k;
+  const int G = p->groups < 1 ? 1 : p->groups;
+  if (M <= 0 || N <= 0 || K <= 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: empty problem %dx%dx%d", M, N, K);
+  if (K % BK != 0) return set_error(ENNX_B200_UNSUPPORTED, "gemm: K=%d must be a multiple of %d", K, BK);
+  if (G > MAX_GROUPS) return set_error(ENNX_B200_UNSUPPORTED, "gemm: at most %d groups", MAX_GROUPS);
+  if (!p->group_offsets && M % G != 0)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: M=%d not divisible into %d uniform groups", M, G);
+  if (p->lda < K || p->ldb < K || p->lda % 8 || p->ldb % 8)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: lda/ldb must be >= K and multiples of 8");
+  const int epi = p->epilogue;
+  if (epi < 0 || epi > ENNX_B200_EPI_LSE) return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: unknown epilogue %d", epi);
+  if (epi == ENNX_B200_EPI_SWIGLU && N % BN != 0)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: SwiGLU needs N a multiple of %d", BN);
+  if (epi == ENNX_B200_EPI_LSE && (!p->targets || !p->lse_partial || !p->target_logit))
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: LSE epilogue needs targets, lse_partial, target_logit");
+  if (epi == ENNX_B200_EPI_ROWSCALE && !p->row_scale)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: ROWSCALE epilogue needs row_scale");
+  if (epi != ENNX_B200_EPI_LSE) {
+    if (!C) return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: null C");
+    long long out_cols = epi == ENNX_B200_EPI_SWIGLU ? N / 2 : N;
+    if (p->ldc < out_cols || (((uintptr_t)C) & 15u) || (p->ldc * (epi == ENNX_B200_EPI_F32 ? 4 : 2)) % 16)
+      return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: C must be 16-byte aligned with ldc >= %lld and 16-byte rows",
+                       out_cols);
+  }
+  if (p->residual && (p->ldr % 8 || ((uintptr_t)p->residual & 15u)))
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: residual must be 16-byte aligned with ldr %% 8 == 0");
+
+  const long long b_rows = (long long)(G - 1) * p->b_group_rows + N;
+  CUtensorMap ta, tb;
+  ENNX_TRY(make_tmap_2d_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)p->lda, BK, BM));
+  ENNX_TRY(make_tmap_2d_bf16(&tb, B, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, BK, BN));
+
+  Args a;
+  a.M = M; a.N = N; a.K = K;
+  a.groups = G;
+  a.rows_per_group = p->group_offsets ? 0 : M / G;
+  a.b_group_rows = p->b_group_rows;
+  a.group_offsets = p->group_offsets;
+  a.epi = epi;
+  a.alpha = p->alpha == 0.0f ? 1.0f : p->alpha;
+  a.C = C; a.ldc = p->ldc;
+  a.R = p->residual; a.ldr = p->ldr;
+  a.row_scale = p->row_scale;
+  a.targets = p->targets;
+  a.lse = (float2*)p->lse_partial;
+  a.tlogit = p->target_logit;
+  a.n_tiles = (N + BN - 1) / BN;
+  a.err = device_error_word();
+  if (!a.err) return set_error(ENNX_B200_CUDA_ERROR, "gemm: no device error word");
+
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!g_attr_set[dev]) {
+    ENNX_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+              "gemm: set smem");
+    g_attr_set[dev] = true;
+  }
+  long long tiles_bound = ((long long)M / BM + G) * a.n_tiles;
+  int grid = sm_count();
+  if (tiles_bound < grid) grid = (int)tiles_bound;
+  gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, a);
+  ENNX_LAUNCH_CHECK("gemm launch");
+  return ENNX_B200_OK;
+}

@@ -1,0 +1,146 @@
+// runtime.cu -- error reporting, device bookkeeping and tensor-map encoding.
+#include <cudaTypedefs.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+
+namespace ennx {
+
+static thread_local std::string g_last_error;
+
+int32_t set_error(int32_t code, const char* fmt, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int32_t check_cuda(cudaError_t e, const char* what) {
+  return set_error(ENNX_B200_CUDA_ERROR, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+static constexpr int kMaxDevices = 64;
+static std::mutex g_mu;
+static int* g_err_word[kMaxDevices];
+static int g_sms[kMaxDevices];
+
+static int current_device() {
+  int d = 0;
+  cudaGetDevice(&d);
+  return d;
+}
+
+int* device_error_word() {
+  int d = current_device();
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_err_word[d]) {
+    int* p = nullptr;
+    if (cudaMalloc(&p, sizeof(int)) != cudaSuccess) return nullptr;
+    cudaMemset(p, 0, sizeof(int));
+    g_err_word[d] = p;
+  }
+  return g_err_word[d];
+}
+
+int32_t consume_device_error(cudaStream_t stream) {
+  int* w = device_error_word();
+  if (!w) return set_error(ENNX_B200_CUDA_ERROR, "could not allocate the device error word");
+  ENNX_CUDA(cudaStreamSynchronize(stream), "stream synchronize");
+  int host = 0;
+  ENNX_CUDA(cudaMemcpy(&host, w, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
+  if (host != 0) {
+    cudaMemset(w, 0, sizeof(int));
+    if (host == ENNX_B200_TIMEOUT)
+      return set_error(ENNX_B200_TIMEOUT, "a device wait exceeded its bound; the kernel returned early");
+    return set_error(host, "device kernel reported status %d", host);
+  }
+  return ENNX_B200_OK;
+}
+
+static void* g_stage[kMaxDevices];
+static size_t g_stage_bytes[kMaxDevices];
+
+void* staging(size_t bytes) {
+  int d = current_device();
+  if (g_stage_bytes[d] < bytes) {
+    if (g_stage[d]) {
+      cudaDeviceSynchronize();
+      cudaFree(g_stage[d]);
+    }
+    size_t cap = bytes < 4096 ? 4096 : bytes * 2;
+    g_stage[d] = nullptr;
+    g_stage_bytes[d] = 0;
+    if (cudaMalloc(&g_stage[d], cap) != cudaSuccess) return nullptr;
+    g_stage_bytes[d] = cap;
+  }
+  return g_stage[d];
+}
+
+int sm_count() {
+  int d = current_device();
+  if (g_sms[d] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, d);
+    g_sms[d] = n > 0 ? n : 148;
+  }
+  return g_sms[d];
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int32_t make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                          uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer) {
+  if (!g_encode) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    ENNX_CUDA(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q),
+              "cudaGetDriverEntryPoint(cuTensorMapEncodeTiled)");
+    if (q != cudaDriverEntryPointSuccess || !fn)
+      return set_error(ENNX_B200_CUDA_ERROR, "cuTensorMapEncodeTiled is not available from the driver");
+    g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+  }
+  if (((uintptr_t)base & 15u) != 0 || (row_stride_elems * 2) % 16 != 0)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "TMA operand must be 16-byte aligned with a 16-byte row stride");
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (%d) for %llux%llu box %ux%u",
+                     (int)r, (unsigned long long)inner, (unsigned long long)outer, box_inner, box_outer);
+  return ENNX_B200_OK;
+}
+
+}  // namespace ennx
+
+extern "C" {
+
+uint32_t ennx_b200_abi_version(void) { return ENNX_B200_ABI_VERSION; }
+
+const char* ennx_b200_last_error(void) { return ennx::g_last_error.c_str(); }
+
+int32_t ennx_b200_device_check(void) {
+  int d = 0;
+  ENNX_CUDA(cudaGetDevice(&d), "cudaGetDevice");
+  cudaDeviceProp p;
+  ENNX_CUDA(cudaGetDeviceProperties(&p, d), "cudaGetDeviceProperties");
+  if (p.major != 10 || p.minor != 0)
+    return ennx::set_error(ENNX_B200_UNSUPPORTED, "device %d is sm_%d%d; this library is built for sm_100a", d,
+                           p.major, p.minor);
+  return ENNX_B200_OK;
+}
+
+int32_t ennx_b200_device_status(void* stream) { return ennx::consume_device_error((cudaStream_t)stream); }
+
+}  // extern "C"

@@ -1,0 +1,74 @@
+"""torch-facing wrappers over the C ABI (device memory and streams from torch).
+
+Every function here launches a kernel of ``libennx_b200.so``; none has a CPU
+path.  Tensors must live on the current CUDA device.
+"""
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _abi
+
+
+def _ptr(t: torch.Tensor | None):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream():
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def _check_dev(*ts):
+    for t in ts:
+        if t is not None and not t.is_cuda:
+            raise ValueError("ennx_b200 operates on CUDA tensors only")
+
+
+def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, *, epilogue: int = _abi.EPI_BF16,
+         alpha: float = 1.0, groups: int = 1, b_group_rows: int = 0, group_offsets: torch.Tensor | None = None,
+         residual: torch.Tensor | None = None, row_scale: torch.Tensor | None = None,
+         targets: torch.Tensor | None = None, lse_partial: torch.Tensor | None = None,
+         target_logit: torch.Tensor | None = None, n: int | None = None) -> torch.Tensor | None:
+    """C = A . B^T on tcgen05 (see ``ennx_b200_gemm_bf16``).
+
+    a: [M, K] bf16; b: [rows, K] bf16 where rows >= (groups-1)*b_group_rows + N.
+    ``n`` defaults to b.shape[0] when there is one B block."""
+    _check_dev(a, b, out, residual, row_scale, targets, group_offsets)
+    if a.dtype != torch.bfloat16 or b.dtype != torch.bfloat16:
+        raise ValueError("gemm operands must be bfloat16")
+    M, K = a.shape
+    N = n if n is not None else b.shape[0]
+    if out is None and epilogue != _abi.EPI_LSE:
+        cols = N // 2 if epilogue == _abi.EPI_SWIGLU else N
+        out = torch.empty(M, cols, device=a.device,
+                          dtype=torch.float32 if epilogue == _abi.EPI_F32 else torch.bfloat16)
+    p = _abi.GemmParams(
+        m=M, n=N, k=K, lda=a.stride(0), ldb=b.stride(0), ldc=0 if out is None else out.stride(0),
+        groups=groups, b_group_rows=b_group_rows,
+        group_offsets=None if group_offsets is None else group_offsets.data_ptr(),
+        epilogue=epilogue, alpha=alpha,
+        residual=None if residual is None else residual.data_ptr(),
+        ldr=0 if residual is None else residual.stride(0),
+        row_scale=None if row_scale is None else row_scale.data_ptr(),
+        targets=None if targets is None else targets.data_ptr(),
+        lse_partial=None if lse_partial is None else lse_partial.data_ptr(),
+        target_logit=None if target_logit is None else target_logit.data_ptr())
+    _abi.call("ennx_b200_gemm_bf16", ctypes.byref(p), _ptr(a), _ptr(b), _ptr(out), _stream())
+    return out
+
+
+def perturb_bf16(w: torch.Tensor, seed: int, pair: int, tensor: int, sigma: float,
+                 plus: torch.Tensor | None = None, minus: torch.Tensor | None = None):
+    """(W + sigma*eps, W - sigma*eps) with Philox noise keyed by (seed, pair, tensor, element)."""
+    _check_dev(w)
+    plus = torch.empty_like(w) if plus is None else plus
+    _abi.call("ennx_b200_perturb_bf16", _ptr(w), w.numel(), seed, pair, tensor, sigma, _ptr(plus), _ptr(minus),
+              _stream())
+    return plus, minus
+
+
+def device_status() -> None:
+    """Synchronise and raise if any kernel recorded a bounded-wait timeout."""
+    _abi.call("ennx_b200_device_status", _stream())

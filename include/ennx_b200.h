@@ -1,0 +1,163 @@
+/*
+ * ennx_b200.h -- C ABI of the B200-native (sm_100a) model-evaluation hot path.
+ *
+ * Drop-in boundary for the GPU path of Kvutza/ennx.  Conventions follow the
+ * reference's existing C ABI (zig/include/ennx.h:11-65: int32 status, POD
+ * structs, size_t counts) and the public surface of its `ennx-cuda` crate
+ * (cuda/src/lib.rs:13-27, 1084-1430).  Each entry point names the reference
+ * interface it replaces.  Citations are file:line inside Kvutza/ennx.
+ *
+ * Common rules
+ *   - Every pointer argument documented "device" is a CUDA device pointer on
+ *     the current device; the caller owns it (zero copy).  Pointers documented
+ *     "host" are read before the call returns.
+ *   - `stream` is a cudaStream_t passed as void* (NULL = legacy default stream).
+ *     Calls are asynchronous on `stream` unless documented "synchronises".
+ *   - Status codes below; on failure a description is available from
+ *     ennx_b200_last_error() (thread-local).  Nothing aborts the process.
+ *   - Device kernels never trap or spin forever: every wait is bounded and a
+ *     timeout is reported as ENNX_B200_TIMEOUT by the next synchronising call
+ *     or by ennx_b200_device_status().
+ *   - Handles / workspaces are not thread-safe; use one per thread and device.
+ */
+#ifndef ENNX_B200_H
+#define ENNX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ENNX_B200_ABI_VERSION 1u
+
+#if defined(__GNUC__)
+#define ENNX_B200_API __attribute__((visibility("default")))
+#else
+#define ENNX_B200_API
+#endif
+
+enum {
+    ENNX_B200_OK = 0,               /* == ENNX_OK (zig/include/ennx.h:12) */
+    ENNX_B200_INVALID_ARGUMENT = 1, /* == ENNX_INVALID_ARGUMENT (zig/include/ennx.h:13) */
+    ENNX_B200_OVERFLOW = 2,         /* "perturbation overflowed" (dense/bf16.rs:254) */
+    ENNX_B200_CUDA_ERROR = 3,
+    ENNX_B200_TIMEOUT = 4,          /* a bounded device wait expired */
+    ENNX_B200_UNSUPPORTED = 5       /* device is not sm_100 or shape outside the kernels' contract */
+};
+
+/* Same layout as ennx_dense_leaf / ennx_dense_term / ennx_dense_view
+ * (zig/include/ennx.h:16-32) and DenseLeaf/DenseTerm/DenseView
+ * (rust/crates/ennx/src/dense.rs:24-48, dense/linear.rs:14-20). */
+typedef struct { uint64_t key; size_t offset; size_t len; float scale; } ennx_b200_dense_leaf;
+typedef struct { uint64_t seed; float coefficient; } ennx_b200_dense_term;
+typedef struct { uint64_t key; uint64_t start; float scale; } ennx_b200_dense_view;
+
+/* ---- library ---------------------------------------------------------- */
+
+/* Replaces ennx_abi_version (zig/include/ennx.h:34). Returns ENNX_B200_ABI_VERSION. */
+ENNX_B200_API uint32_t ennx_b200_abi_version(void);
+/* Thread-local description of the last failure ("" if none). */
+ENNX_B200_API const char* ennx_b200_last_error(void);
+/* ENNX_B200_OK if the current device is an sm_100 part this library was built for. */
+ENNX_B200_API int32_t ennx_b200_device_check(void);
+/* Synchronises `stream`, then returns and clears the device error word
+ * (ENNX_B200_TIMEOUT if any kernel gave up on a bounded wait). */
+ENNX_B200_API int32_t ennx_b200_device_status(void* stream);
+
+/* ---- seeded dense perturbation (the existing CUDA drop-in) ------------- */
+
+/* out = base + scale * sum(c_i * sign_i), with the one-ulp rule.  Replaces
+ * `dense_apply` (cuda/src/lib.rs:1084-1124; CPU ennx_dense_apply_f32,
+ * zig/include/ennx.h:36-44).  base/out: device float[num_values];
+ * leaves/terms: host.  out_changed (host, nullable) receives num_values on
+ * success.  Synchronises; ENNX_B200_OVERFLOW if any output is non-finite. */
+ENNX_B200_API int32_t ennx_b200_dense_apply_f32(const float* base, size_t num_values,
+                                  const ennx_b200_dense_leaf* leaves, size_t num_leaves,
+                                  const ennx_b200_dense_term* terms, size_t num_terms,
+                                  float* out, size_t* out_changed, void* stream);
+
+/* BF16 materialisation with per-tile overflow status and rollback to base.
+ * Replaces Bf16Engine::materialize (cuda/src/lib.rs:1211-1252).
+ * base/out: device uint16 (bf16 bits)[num_values].  Synchronises; on
+ * overflow out is restored to base and ENNX_B200_OVERFLOW is returned. */
+ENNX_B200_API int32_t ennx_b200_dense_apply_bf16(const uint16_t* base, size_t num_values,
+                                   const ennx_b200_dense_leaf* leaves, size_t num_leaves,
+                                   const ennx_b200_dense_term* terms, size_t num_terms,
+                                   uint16_t* out, void* stream);
+
+/* *all_finite (host) = 1 iff every bf16 value is finite.  Replaces the
+ * check_bf16 kernel path (cuda/kernels/src/lib.rs:2311-2354).  Synchronises. */
+ENNX_B200_API int32_t ennx_b200_check_bf16(const uint16_t* values, size_t num_values, int32_t* all_finite,
+                             void* stream);
+
+/* Fused perturbed GEMV y = W~ x (+ b~).  Replaces DenseLinearEngine::eval
+ * (cuda/src/lib.rs:1339-1429) and ennx_dense_linear_f32
+ * (zig/include/ennx.h:55-65), same argument order.  input/weight/bias/out:
+ * device (bias nullable); terms: host.  Asynchronous. */
+ENNX_B200_API int32_t ennx_b200_dense_linear_f32(const float* input, size_t columns, const float* weight,
+                                   size_t rows, const float* bias,
+                                   ennx_b200_dense_view weight_view, ennx_b200_dense_view bias_view,
+                                   const ennx_b200_dense_term* terms, size_t num_terms, float* out,
+                                   void* stream);
+
+/* ---- population noise (no reference counterpart: the reference draws
+ *      Rademacher signs; BASELINE asks for Philox Gaussian noise) --------- */
+
+/* out_plus = bf16(W + sigma*eps), out_minus = bf16(W - sigma*eps) (nullable),
+ * eps = Philox4x32-10 Box-Muller normal of (seed, pair, tensor, element).
+ * w/out_*: device bf16 bits[n].  Asynchronous. */
+ENNX_B200_API int32_t ennx_b200_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair,
+                               uint32_t tensor, float sigma, uint16_t* out_plus,
+                               uint16_t* out_minus, void* stream);
+
+/* ---- dense contractions ------------------------------------------------ */
+
+enum {
+    ENNX_B200_EPI_BF16 = 0,     /* C[bf16] = alpha*acc (+ residual)               */
+    ENNX_B200_EPI_F32 = 1,      /* C[f32]  = alpha*acc                            */
+    ENNX_B200_EPI_SWIGLU = 2,   /* C[bf16, N/2 cols] = silu(gate) * up, see below */
+    ENNX_B200_EPI_ROWSCALE = 3, /* C[bf16] = row_scale[r] * acc                   */
+    ENNX_B200_EPI_LSE = 4       /* per-row logsumexp partials + target logit      */
+};
+
+/* C = A . B^T with A [M, K] and B [N, K] bf16 row-major (K contiguous), fp32
+ * accumulation on tcgen05 tensor cores (TMEM accumulators, TMA-fed).
+ * The reference has no GEMM; the nearest operator is the fused linear
+ * (dense/linear.rs:484-519: C[m,:] = linear(A[m,:], B)).
+ *
+ * Grouping: rows of A/C are split into `groups` contiguous segments; group g
+ * uses rows [g*b_group_rows, g*b_group_rows + N) of B (b_group_rows = 0: all
+ * groups share rows [0, N)).
+ * Segment bounds come from `group_offsets` (device int32[groups+1]) or, when
+ * it is NULL, from equal segments of M/groups rows.
+ *
+ * Epilogues: EPI_SWIGLU expects B's rows in blocks of 256 = [128 gate rows |
+ * 128 up rows]; output column j of block b is silu(g)*u of row 128b+j.
+ * EPI_LSE writes lse_partial[r * ceil(N/256) + tile] = (max, sum exp(x-max))
+ * as float2 and target_logit[r] = acc[r, targets[r]].
+ * Requirements: K % 64 == 0, K >= 64, lda/ldb % 8 == 0, 16-byte aligned A/B. */
+typedef struct {
+    int32_t m, n, k;
+    int64_t lda, ldb, ldc;   /* elements */
+    int32_t groups;          /* >= 1 */
+    int32_t b_group_rows;    /* B row stride between groups (0: shared B) */
+    const int32_t* group_offsets; /* device, nullable */
+    int32_t epilogue;
+    float alpha;
+    const uint16_t* residual; /* EPI_BF16: device bf16 [M, ldr] added after alpha*acc; nullable */
+    int64_t ldr;
+    const float* row_scale;   /* EPI_ROWSCALE: device float[M] */
+    const int32_t* targets;   /* EPI_LSE: device int32[M] */
+    float* lse_partial;       /* EPI_LSE: device float2[M, ceil(N/256)] */
+    float* target_logit;      /* EPI_LSE: device float[M] */
+} ennx_b200_gemm_params;
+
+ENNX_B200_API int32_t ennx_b200_gemm_bf16(const ennx_b200_gemm_params* params, const uint16_t* a,
+                            const uint16_t* b, void* c, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ENNX_B200_H */

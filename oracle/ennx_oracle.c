@@ -1,0 +1,540 @@
+/*
+ * ennx_oracle.c -- CPU restatement of the reference's model-evaluation math.
+ *
+ * TEST INFRASTRUCTURE ONLY: the checker for the CUDA path, never the product.
+ * Compiled with -ffp-contract=off so that every "a + b*c" rounds twice, as the
+ * reference's Rust code does (Rust never contracts to FMA unless mul_add is
+ * written out).  Citations are file:line inside the Kvutza/ennx repository.
+ */
+#include "ennx_oracle.h"
+
+#include <math.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------------ */
+/* Perturbation family                                                      */
+/* ------------------------------------------------------------------------ */
+
+/* splitmix64 finaliser; rust/crates/ennx/src/dense.rs:428-433 */
+uint64_t eo_mix64(uint64_t x) {
+    uint64_t v = x + 0x9e3779b97f4a7c15ull;
+    v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+    v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
+    return v ^ (v >> 31);
+}
+
+/* Rademacher direction of (seed, leaf key, element); dense.rs:397-405 */
+float eo_dense_sign(uint64_t seed, uint64_t key, uint64_t element) {
+    uint64_t leaf = eo_mix64(key ^ 0xd6e8feb86659fd93ull);
+    uint64_t coord = eo_mix64(element ^ 0xa0761d6478bd642full);
+    return (eo_mix64(seed ^ leaf ^ coord) & 1ull) ? 1.0f : -1.0f;
+}
+
+/* FNV-1a 64 over the tensor name bytes; dense.rs:51-58 */
+uint64_t eo_tensor_key(const char* name) {
+    uint64_t key = 1469598103934665603ull;
+    for (const unsigned char* p = (const unsigned char*)name; *p; ++p)
+        key = (key ^ (uint64_t)*p) * 1099511628211ull;
+    return key;
+}
+
+static uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+/* one-ulp step toward the dominant direction, kept finite; dense.rs:407-426 */
+float eo_dense_next(float value, int positive) {
+    if (value == 0.0f) return u2f(positive ? 1u : 0x80000001u);
+    int grows = (value > 0.0f) == (positive != 0);
+    float cand = u2f(grows ? f2u(value) + 1u : f2u(value) - 1u);
+    if (isfinite(cand)) return cand;
+    return u2f(grows ? f2u(value) - 1u : f2u(value) + 1u);
+}
+
+/* dense/bf16.rs:266-268 */
+float eo_bf16_decode(uint16_t v) { return u2f((uint32_t)v << 16); }
+
+/* round-to-nearest-even encode; dense/bf16.rs:270-273 */
+uint16_t eo_bf16_encode(float v) {
+    uint32_t bits = f2u(v);
+    return (uint16_t)((bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16);
+}
+
+/* dense/bf16.rs:275-292 */
+uint16_t eo_bf16_next(uint16_t v, int positive) {
+    if ((v & 0x7fffu) == 0) return positive ? 1u : 0x8001u;
+    int grows = ((v & 0x8000u) == 0) == (positive != 0);
+    uint16_t cand = grows ? (uint16_t)(v + 1u) : (uint16_t)(v - 1u);
+    if (isfinite(eo_bf16_decode(cand))) return cand;
+    return grows ? (uint16_t)(v - 1u) : (uint16_t)(v + 1u);
+}
+
+/* Sum of coefficient*direction plus the dominant term's direction; the inner
+ * loop shared by dense.rs:367-379, dense/bf16.rs:239-251, linear.rs:530-541. */
+static float term_sum(const eo_term* terms, size_t nt, uint64_t key, uint64_t element,
+                      int* positive) {
+    float sum = 0.0f, strongest = 0.0f;
+    *positive = 1;
+    for (size_t t = 0; t < nt; ++t) {
+        float c = terms[t].coefficient;
+        if (c == 0.0f) continue;
+        float dir = eo_dense_sign(terms[t].seed, key, element);
+        float prod = c * dir;
+        sum = sum + prod;
+        if (fabsf(c) > strongest) {
+            strongest = fabsf(c);
+            *positive = (c > 0.0f) == (dir > 0.0f);
+        }
+    }
+    return sum;
+}
+
+/* dense.rs:191-240 (validate_leaves / dense_validate) */
+static int leaves_valid(const eo_leaf* leaves, size_t nl, size_t n) {
+    if (!leaves || nl == 0) return 0;
+    size_t end = 0;
+    for (size_t i = 0; i < nl; ++i) {
+        if (leaves[i].offset != end || leaves[i].len == 0) return 0;
+        if (!isfinite(leaves[i].scale) || leaves[i].scale <= 0.0f) return 0;
+        end += leaves[i].len;
+    }
+    return end == n;
+}
+
+static double coefficient_of(const eo_term* terms, size_t nt, uint64_t seed) {
+    double c = 0.0;
+    for (size_t i = 0; i < nt; ++i)
+        if (terms[i].seed == seed) c += (double)terms[i].coefficient;
+    return c;
+}
+
+/* dense.rs:258-265 (has_direction) */
+static int has_direction(const eo_term* terms, size_t nt) {
+    for (size_t i = 0; i < nt; ++i) {
+        int seen = 0;
+        for (size_t j = 0; j < i; ++j) if (terms[j].seed == terms[i].seed) seen = 1;
+        if (!seen && coefficient_of(terms, nt, terms[i].seed) != 0.0) return 1;
+    }
+    return 0;
+}
+
+static int terms_valid(const eo_term* terms, size_t nt) {
+    for (size_t i = 0; i < nt; ++i) if (!isfinite(terms[i].coefficient)) return 0;
+    return 1;
+}
+
+/* fp32 dense perturbation; dense.rs:361-395 */
+int32_t eo_dense_apply_f32(const float* base, size_t n, const eo_leaf* leaves, size_t nl,
+                           const eo_term* terms, size_t nt, float* out, size_t* changed) {
+    if (!base || !out || n == 0) return EO_INVALID_ARGUMENT;
+    for (size_t i = 0; i < n; ++i) if (!isfinite(base[i])) return EO_INVALID_ARGUMENT;
+    if (!leaves_valid(leaves, nl, n) || !terms_valid(terms, nt) || !has_direction(terms, nt))
+        return EO_INVALID_ARGUMENT;
+    size_t count = 0;
+    for (size_t l = 0; l < nl; ++l) {
+        for (size_t local = 0; local < leaves[l].len; ++local) {
+            size_t idx = leaves[l].offset + local;
+            int positive;
+            float sum = term_sum(terms, nt, leaves[l].key, local, &positive);
+            float step = leaves[l].scale * sum;
+            float cand = base[idx] + step;
+            float v;
+            if (sum == 0.0f || cand == base[idx]) v = eo_dense_next(base[idx], positive);
+            else if (isfinite(cand)) v = cand;
+            else return EO_OVERFLOW;
+            out[idx] = v;
+            count += (v != base[idx]);
+        }
+    }
+    if (changed) *changed = count;
+    return EO_OK;
+}
+
+/* BF16 dense perturbation; dense/bf16.rs:228-264 */
+int32_t eo_dense_apply_bf16(const uint16_t* base, size_t n, const eo_leaf* leaves, size_t nl,
+                            const eo_term* terms, size_t nt, uint16_t* out) {
+    if (!base || !out || n == 0) return EO_INVALID_ARGUMENT;
+    for (size_t i = 0; i < n; ++i) if (!isfinite(eo_bf16_decode(base[i]))) return EO_INVALID_ARGUMENT;
+    if (!leaves_valid(leaves, nl, n) || !terms_valid(terms, nt) || !has_direction(terms, nt))
+        return EO_INVALID_ARGUMENT;
+    for (size_t l = 0; l < nl; ++l) {
+        for (size_t local = 0; local < leaves[l].len; ++local) {
+            size_t idx = leaves[l].offset + local;
+            int positive;
+            float sum = term_sum(terms, nt, leaves[l].key, local, &positive);
+            float step = leaves[l].scale * sum;
+            float value = eo_bf16_decode(base[idx]) + step;
+            if (!isfinite(value)) {
+                memcpy(out, base, n * sizeof(uint16_t)); /* roll back, bf16.rs:139-142 */
+                return EO_OVERFLOW;
+            }
+            uint16_t cand = eo_bf16_encode(value);
+            out[idx] = (sum == 0.0f || cand == base[idx]) ? eo_bf16_next(base[idx], positive) : cand;
+        }
+    }
+    return EO_OK;
+}
+
+/* closed-form squared distance between two term sets; dense.rs:341-358 */
+int32_t eo_dense_dist2(const eo_leaf* leaves, size_t nl, const eo_term* left, size_t nleft,
+                       const eo_term* right, size_t nright, double* out) {
+    if (!out || !leaves || nl == 0) return EO_INVALID_ARGUMENT;
+    double energy = 0.0;
+    for (size_t i = 0; i < nl; ++i) {
+        if (leaves[i].len == 0 || !(leaves[i].scale > 0.0f)) return EO_INVALID_ARGUMENT;
+        energy += (double)leaves[i].len * (double)leaves[i].scale * (double)leaves[i].scale;
+    }
+    double dist = 0.0;
+    size_t total = nleft + nright;
+    for (size_t i = 0; i < total; ++i) {
+        uint64_t seed = i < nleft ? left[i].seed : right[i - nleft].seed;
+        int seen = 0;
+        for (size_t j = 0; j < i; ++j) {
+            uint64_t s = j < nleft ? left[j].seed : right[j - nleft].seed;
+            if (s == seed) seen = 1;
+        }
+        if (seen) continue;
+        double d = coefficient_of(left, nleft, seed) - coefficient_of(right, nright, seed);
+        dist += d * d;
+    }
+    *out = energy * dist;
+    return EO_OK;
+}
+
+/* per-element perturbation used by the fused linear; linear.rs:522-548 */
+static int perturbed_value(float base, eo_view view, uint64_t element, const eo_term* terms,
+                           size_t nt, float* out) {
+    int positive;
+    float sum = term_sum(terms, nt, view.key, view.start + element, &positive);
+    float step = view.scale * sum;
+    float cand = base + step;
+    if (sum == 0.0f || cand == base) *out = eo_dense_next(base, positive);
+    else if (isfinite(cand)) *out = cand;
+    else return 0;
+    return 1;
+}
+
+/* fused perturbed GEMV with a serial fma chain per row; linear.rs:484-519 */
+int32_t eo_dense_linear_f32(const float* input, size_t columns, const float* weight, size_t rows,
+                            const float* bias, eo_view weight_view, eo_view bias_view,
+                            const eo_term* terms, size_t nt, float* out) {
+    if (!input || !weight || !out || columns == 0 || rows == 0 || nt == 0) return EO_INVALID_ARGUMENT;
+    if (!terms_valid(terms, nt) || !has_direction(terms, nt)) return EO_INVALID_ARGUMENT;
+    if (!(weight_view.scale > 0.0f) || !isfinite(weight_view.scale)) return EO_INVALID_ARGUMENT;
+    if (bias && (!(bias_view.scale > 0.0f) || !isfinite(bias_view.scale))) return EO_INVALID_ARGUMENT;
+    for (size_t r = 0; r < rows; ++r) {
+        float sum = 0.0f;
+        for (size_t c = 0; c < columns; ++c) {
+            size_t idx = r * columns + c;
+            float w;
+            if (!perturbed_value(weight[idx], weight_view, idx, terms, nt, &w)) return EO_OVERFLOW;
+            sum = fmaf(input[c], w, sum);
+        }
+        if (bias) {
+            float b;
+            if (!perturbed_value(bias[r], bias_view, r, terms, nt, &b)) return EO_OVERFLOW;
+            sum = sum + b;
+        }
+        if (!isfinite(sum)) return EO_OVERFLOW;
+        out[r] = sum;
+    }
+    return EO_OK;
+}
+
+/* packed-code hash of the CUDA trial path; cuda/kernels/src/lib.rs:150-158 */
+uint32_t eo_trial_hash(uint32_t seed_low, uint32_t seed_high, uint32_t element) {
+    uint32_t v = seed_low ^ (element * 0x9e3779b9u);
+    v ^= v >> 16;
+    v *= 0x7feb352du;
+    v ^= seed_high;
+    v *= 0x846ca68bu;
+    return v ^ (v >> 15);
+}
+
+/* integer-code step with reflection at the code range; lib.rs:230-258 */
+uint32_t eo_perturb_code(uint32_t code, uint32_t seed_low, uint32_t seed_high, uint32_t element,
+                         uint32_t bits, uint32_t whole, uint32_t threshold) {
+    uint32_t random = eo_trial_hash(seed_low, seed_high, element);
+    uint32_t amount = whole + (uint32_t)((random >> 1) < (threshold >> 1));
+    if (amount == 0) return code;
+    uint32_t max_code = (1u << bits) - 1u;
+    if ((random & 1u) == 0) {
+        if (code >= amount) return code - amount;
+        uint32_t up = code + amount;
+        return up < max_code ? up : max_code;
+    }
+    if (code + amount <= max_code) return code + amount;
+    return code >= amount ? code - amount : 0u;
+}
+
+/* ------------------------------------------------------------------------ */
+/* Population noise: Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11) with  */
+/* Box-Muller.  Builder-defined -- the reference draws Rademacher signs.     */
+/* ------------------------------------------------------------------------ */
+
+void eo_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) {
+    uint32_t c0 = ctr[0], c1 = ctr[1], c2 = ctr[2], c3 = ctr[3];
+    uint32_t k0 = key[0], k1 = key[1];
+    for (int round = 0; round < 10; ++round) {
+        uint64_t p0 = (uint64_t)0xD2511F53u * c0;
+        uint64_t p1 = (uint64_t)0xCD9E8D57u * c2;
+        uint32_t n0 = (uint32_t)(p1 >> 32) ^ c1 ^ k0;
+        uint32_t n1 = (uint32_t)p1;
+        uint32_t n2 = (uint32_t)(p0 >> 32) ^ c3 ^ k1;
+        uint32_t n3 = (uint32_t)p0;
+        c0 = n0; c1 = n1; c2 = n2; c3 = n3;
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
+}
+
+/* Box-Muller on the top 24 bits of two Philox words; computed in double so
+ * the oracle is the exactly rounded value the device approximates. */
+static void box_muller(uint32_t a, uint32_t b, float* z0, float* z1) {
+    float u1 = ((float)(a >> 8) + 0.5f) * 5.9604644775390625e-08f; /* 2^-24 */
+    float u2 = (float)(b >> 8) * 5.9604644775390625e-08f;
+    double r = sqrt(-2.0 * log((double)u1));
+    double th = 2.0 * M_PI * (double)u2;
+    *z0 = (float)(r * cos(th));
+    *z1 = (float)(r * sin(th));
+}
+
+/* Four N(0,1) draws for element block `block` (elements 4*block .. 4*block+3)
+ * of tensor `tensor`, antithetic pair `pair`, population seed `seed`. */
+void eo_noise4(uint64_t seed, uint32_t pair, uint32_t tensor, uint64_t block, float out[4]) {
+    uint32_t ctr[4] = {(uint32_t)block, (uint32_t)(block >> 32), tensor, pair};
+    uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
+    uint32_t x[4];
+    eo_philox4x32_10(ctr, key, x);
+    box_muller(x[0], x[1], &out[0], &out[1]);
+    box_muller(x[2], x[3], &out[2], &out[3]);
+}
+
+/* W~ = bf16(W + sign * (sigma * eps)), two fp32 roundings then RNE. */
+void eo_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor,
+                     float sigma, int sign, uint16_t* out) {
+    float z[4];
+    for (size_t i = 0; i < n; ++i) {
+        if ((i & 3) == 0 || i == 0) eo_noise4(seed, pair, tensor, i >> 2, z);
+        float step = sigma * z[i & 3];
+        float v = sign >= 0 ? eo_bf16_decode(w[i]) + step : eo_bf16_decode(w[i]) - step;
+        out[i] = eo_bf16_encode(v);
+    }
+}
+
+/* ------------------------------------------------------------------------ */
+/* Forward math                                                             */
+/* ------------------------------------------------------------------------ */
+
+/* x * rsqrt(mean(x^2) + eps) * w; kda_moe.metal:536-554 (fp64 accumulate). */
+void eo_rmsnorm(const float* x, const float* w, size_t rows, size_t width, float eps, float* out) {
+    for (size_t r = 0; r < rows; ++r) {
+        double ss = 0.0;
+        for (size_t i = 0; i < width; ++i) ss += (double)x[r * width + i] * x[r * width + i];
+        double inv = 1.0 / sqrt(ss / (double)width + (double)eps);
+        for (size_t i = 0; i < width; ++i)
+            out[r * width + i] = (float)((double)x[r * width + i] * inv * (double)w[i]);
+    }
+}
+
+/* Router logits with the fixed fp32 reduction tree the CUDA router uses, so
+ * that the logits -- and therefore the routing indices -- are bit-identical.
+ * Lane l of 32 owns elements {256*j + 8*l + u}; it runs a serial fmaf chain
+ * over j then u; the 32 partials are combined by an xor butterfly with
+ * offsets 16, 8, 4, 2, 1.  The math is kda_moe.metal:585-595. */
+void eo_router_logits(const uint16_t* x, const uint16_t* w, size_t tokens, size_t hidden,
+                      size_t experts, float* logits) {
+    for (size_t t = 0; t < tokens; ++t) {
+        for (size_t e = 0; e < experts; ++e) {
+            float p[32];
+            for (int l = 0; l < 32; ++l) {
+                float acc = 0.0f;
+                for (size_t j = 0; j < hidden / 256; ++j)
+                    for (int u = 0; u < 8; ++u) {
+                        size_t i = 256 * j + 8 * (size_t)l + (size_t)u;
+                        acc = fmaf(eo_bf16_decode(x[t * hidden + i]), eo_bf16_decode(w[e * hidden + i]), acc);
+                    }
+                p[l] = acc;
+            }
+            for (int off = 16; off >= 1; off >>= 1) {
+                float q[32];
+                for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ off];
+                memcpy(p, q, sizeof(p));
+            }
+            logits[t * experts + e] = p[0];
+        }
+    }
+}
+
+/* Top-k by insertion with strict '>' (ties keep the lower expert index), then
+ * a max-subtracted softmax over the k kept logits; kda_moe.metal:596-621. */
+void eo_router_topk(const float* logits, size_t tokens, size_t experts, size_t k,
+                    int32_t* index, float* gate) {
+    for (size_t t = 0; t < tokens; ++t) {
+        float val[64];
+        int32_t idx[64];
+        for (size_t r = 0; r < k; ++r) { val[r] = -INFINITY; idx[r] = 0; }
+        for (size_t e = 0; e < experts; ++e) {
+            float s = logits[t * experts + e];
+            for (size_t r = 0; r < k; ++r) {
+                if (s > val[r]) {
+                    for (size_t m = k - 1; m > r; --m) { val[m] = val[m - 1]; idx[m] = idx[m - 1]; }
+                    val[r] = s; idx[r] = (int32_t)e;
+                    break;
+                }
+            }
+        }
+        double den = 0.0, ex[64];
+        for (size_t r = 0; r < k; ++r) { ex[r] = exp((double)val[r] - (double)val[0]); den += ex[r]; }
+        for (size_t r = 0; r < k; ++r) {
+            index[t * k + r] = idx[r];
+            gate[t * k + r] = (float)(ex[r] / den);
+        }
+    }
+}
+
+static double softplus_d(double x) { return (x > 0 ? x : 0.0) + log1p(exp(-fabs(x))); }
+
+/* g = max(-exp(decay_h) * softplus(raw + time_bias), -5), beta = sigmoid(raw_beta);
+ * kda_moe.metal:869-895. */
+void eo_kda_gate_beta(const float* raw_gate, const float* raw_beta, const float* decay,
+                      const float* time_bias, size_t tokens, size_t heads, size_t head_width,
+                      float* gate, float* beta) {
+    size_t width = heads * head_width;
+    for (size_t t = 0; t < tokens; ++t) {
+        for (size_t j = 0; j < width; ++j) {
+            size_t h = j / head_width;
+            double raw = (double)raw_gate[t * width + j] + (double)time_bias[j];
+            double g = -exp((double)decay[h]) * softplus_d(raw);
+            gate[t * width + j] = (float)(g < -5.0 ? -5.0 : g);
+        }
+        for (size_t h = 0; h < heads; ++h)
+            beta[t * heads + h] = (float)(1.0 / (1.0 + exp(-(double)raw_beta[t * heads + h])));
+    }
+}
+
+/* per-head L2 normalisation with max(|x|, 1e-6); kda_moe.metal:510-534 */
+void eo_l2norm_heads(float* x, size_t groups, size_t width) {
+    for (size_t gi = 0; gi < groups; ++gi) {
+        double ss = 0.0;
+        for (size_t i = 0; i < width; ++i) ss += (double)x[gi * width + i] * x[gi * width + i];
+        double n = sqrt(ss);
+        double inv = 1.0 / (n > 1e-6 ? n : 1e-6);
+        for (size_t i = 0; i < width; ++i) x[gi * width + i] = (float)(x[gi * width + i] * inv);
+    }
+}
+
+/* Serial gated delta rule with per-key-channel decay, fp32 state, in the
+ * reference's operation order; kda_moe.metal:167-225.  q,k: [B,T,H,dk],
+ * v: [B,T,H,dv], g: [B,T,H,dk], beta: [B,T,H], state: [B,H,dk,dv] in/out,
+ * out: [B,T,H,dv] scaled by 1/sqrt(dk). */
+void eo_kda_recurrence(const float* q, const float* k, const float* v, const float* g,
+                       const float* beta, size_t batch, size_t length, size_t heads,
+                       size_t dk, size_t dv, float* state, float* out) {
+    float scale = 1.0f / sqrtf((float)dk);
+    for (size_t b = 0; b < batch; ++b)
+        for (size_t h = 0; h < heads; ++h) {
+            float* S = state + (b * heads + h) * dk * dv;
+            for (size_t t = 0; t < length; ++t) {
+                size_t qk = ((b * length + t) * heads + h) * dk;
+                size_t vo = ((b * length + t) * heads + h) * dv;
+                float rate = beta[(b * length + t) * heads + h];
+                for (size_t i = 0; i < dk; ++i) {
+                    float d = expf(g[qk + i]);
+                    for (size_t j = 0; j < dv; ++j) S[i * dv + j] *= d;
+                }
+                for (size_t j = 0; j < dv; ++j) {
+                    float read = 0.0f;
+                    for (size_t i = 0; i < dk; ++i) read += k[qk + i] * S[i * dv + j];
+                    float upd = rate * (v[vo + j] - read);
+                    for (size_t i = 0; i < dk; ++i) S[i * dv + j] += k[qk + i] * upd;
+                    float res = 0.0f;
+                    for (size_t i = 0; i < dk; ++i) res += q[qk + i] * S[i * dv + j];
+                    out[vo + j] = res * scale;
+                }
+            }
+        }
+}
+
+/* per-head RMSNorm * norm, then * sigmoid(gate); kda_moe.metal:898-921 */
+void eo_kda_postprocess(const float* o, const float* gate, const float* norm, size_t tokens,
+                        size_t heads, size_t width, float eps, float* out) {
+    for (size_t t = 0; t < tokens; ++t)
+        for (size_t h = 0; h < heads; ++h) {
+            const float* x = o + (t * heads + h) * width;
+            double ss = 0.0;
+            for (size_t i = 0; i < width; ++i) ss += (double)x[i] * x[i];
+            double inv = 1.0 / sqrt(ss / (double)width + (double)eps);
+            for (size_t i = 0; i < width; ++i) {
+                size_t j = (t * heads + h) * width + i;
+                double val = (double)x[i] * inv * (double)norm[i];
+                out[j] = (float)(val / (1.0 + exp(-(double)gate[j])));
+            }
+        }
+}
+
+/* Rotary embedding, rotate-half (NeoX) pairing (i, i + dim/2), position = s.
+ * No reference counterpart.  x: [B, S, H, dim], in place. */
+void eo_rope(float* x, size_t batch, size_t seq, size_t heads, size_t dim, double theta) {
+    size_t half = dim / 2;
+    for (size_t b = 0; b < batch; ++b)
+        for (size_t s = 0; s < seq; ++s)
+            for (size_t h = 0; h < heads; ++h) {
+                float* p = x + ((b * seq + s) * heads + h) * dim;
+                for (size_t i = 0; i < half; ++i) {
+                    double inv = pow(theta, -2.0 * (double)i / (double)dim);
+                    double a = (double)s * inv, c = cos(a), sn = sin(a);
+                    double x1 = p[i], x2 = p[i + half];
+                    p[i] = (float)(x1 * c - x2 * sn);
+                    p[i + half] = (float)(x2 * c + x1 * sn);
+                }
+            }
+}
+
+/* Causal grouped-query attention, softmax scale 1/sqrt(dim), fp64 accumulate.
+ * q: [B,S,Hq,dim], k,v: [B,S,Hkv,dim], out: [B,S,Hq,dim].  No reference
+ * counterpart. */
+void eo_gqa_attention(const float* q, const float* k, const float* v, size_t batch, size_t seq,
+                      size_t hq, size_t hkv, size_t dim, float* out) {
+    double scale = 1.0 / sqrt((double)dim);
+    double* p = (double*)malloc(seq * sizeof(double));
+    size_t group = hq / hkv;
+    for (size_t b = 0; b < batch; ++b)
+        for (size_t h = 0; h < hq; ++h) {
+            size_t kh = h / group;
+            for (size_t t = 0; t < seq; ++t) {
+                const float* qr = q + ((b * seq + t) * hq + h) * dim;
+                double mx = -INFINITY;
+                for (size_t s = 0; s <= t; ++s) {
+                    const float* kr = k + ((b * seq + s) * hkv + kh) * dim;
+                    double dot = 0.0;
+                    for (size_t i = 0; i < dim; ++i) dot += (double)qr[i] * kr[i];
+                    p[s] = dot * scale;
+                    if (p[s] > mx) mx = p[s];
+                }
+                double den = 0.0;
+                for (size_t s = 0; s <= t; ++s) { p[s] = exp(p[s] - mx); den += p[s]; }
+                float* orow = out + ((b * seq + t) * hq + h) * dim;
+                for (size_t i = 0; i < dim; ++i) {
+                    double acc = 0.0;
+                    for (size_t s = 0; s <= t; ++s) acc += p[s] * v[((b * seq + s) * hkv + kh) * dim + i];
+                    orow[i] = (float)(acc / den);
+                }
+            }
+        }
+    free(p);
+}
+
+/* per-row logsumexp(logits) - logits[target]; no reference counterpart. */
+void eo_cross_entropy_rows(const float* logits, const int32_t* targets, size_t rows,
+                           size_t vocab, double* loss) {
+    for (size_t r = 0; r < rows; ++r) {
+        const float* x = logits + r * vocab;
+        double mx = -INFINITY;
+        for (size_t i = 0; i < vocab; ++i) if (x[i] > mx) mx = x[i];
+        double s = 0.0;
+        for (size_t i = 0; i < vocab; ++i) s += exp((double)x[i] - mx);
+        loss[r] = mx + log(s) - (double)x[targets[r]];
+    }
+}

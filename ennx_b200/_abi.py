@@ -51,6 +51,27 @@ class GemmParams(ctypes.Structure):
                 ("lse_partial", ctypes.c_void_p), ("target_logit", ctypes.c_void_p)]
 
 
+class ModelConfig(ctypes.Structure):
+    _fields_ = [("layers", ctypes.c_int32), ("hidden", ctypes.c_int32), ("vocab", ctypes.c_int32),
+                ("attn_period", ctypes.c_int32), ("q_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
+                ("kda_heads", ctypes.c_int32), ("gate_rank", ctypes.c_int32), ("experts", ctypes.c_int32),
+                ("top_k", ctypes.c_int32), ("expert_width", ctypes.c_int32), ("rms_eps", ctypes.c_float),
+                ("rope_theta", ctypes.c_float)]
+
+
+LAYER_FIELDS = ("attn_norm", "w_qkv", "w_ctl", "w_forget", "w_ogate", "decay", "time_bias", "out_norm", "w_o",
+                "moe_norm", "w_router", "w_gate_up", "w_down")
+
+
+class LayerWeights(ctypes.Structure):
+    _fields_ = [(f, ctypes.c_void_p) for f in LAYER_FIELDS]
+
+
+class ModelWeights(ctypes.Structure):
+    _fields_ = [("embedding", ctypes.c_void_p), ("final_norm", ctypes.c_void_p),
+                ("layers", ctypes.POINTER(LayerWeights))]
+
+
 _P = ctypes.c_void_p
 _SZ = ctypes.c_size_t
 _I32 = ctypes.c_int32
@@ -69,6 +90,15 @@ SIGNATURES = {
     "ennx_b200_dense_linear_f32": (_I32, [_P, _SZ, _P, _SZ, _P, DenseView, DenseView, _P, _SZ, _P, _P]),
     "ennx_b200_perturb_bf16": (_I32, [_P, _SZ, _U64, _U32, _U32, _F32, _P, _P, _P]),
     "ennx_b200_gemm_bf16": (_I32, [_P, _P, _P, _P, _P]),
+    "ennx_b200_rmsnorm_bf16": (_I32, [_P, _P, ctypes.c_int64, _I32, _F32, _P, _P]),
+    "ennx_b200_moe_route": (_I32, [_P, _P, ctypes.c_int64, _I32, _I32, _I32, _P, _P, _P, _P]),
+    "ennx_b200_moe_workspace_size": (_SZ, [ctypes.c_int64, _I32, _I32, _I32, _I32]),
+    "ennx_b200_moe_layer": (_I32, [_P, _P, _P, _P, ctypes.c_int64, _I32, _I32, _I32, _I32, _P, _P, _P, _P, _P,
+                                   _SZ, _P]),
+    "ennx_b200_gqa_attention": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _F32, _P]),
+    "ennx_b200_kda_chunked": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P]),
+    "ennx_b200_population_workspace_size": (_SZ, [_P, _I32, _I32]),
+    "ennx_b200_population_forward": (_I32, [_P, _P, _U64, _F32, _I32, _I32, _P, _I32, _I32, _P, _P, _SZ, _P]),
 }
 
 _lib = None

@@ -28,7 +28,11 @@ int32_t check_cuda(cudaError_t e, const char* what);
     cudaError_t _e = (expr);                                           \
     if (_e != cudaSuccess) return ::ennx::check_cuda(_e, what);        \
   } while (0)
-#define ENNX_LAUNCH_CHECK(what) ENNX_CUDA(cudaGetLastError(), what)
+#define ENNX_LAUNCH_CHECK(what)                 \
+  do {                                          \
+    ::ennx::note_launch(1);                     \
+    ENNX_CUDA(cudaGetLastError(), what);        \
+  } while (0)
 
 // Device-side error word shared by every kernel of one process and device.
 // Kernels write a nonzero code (ENNX_B200_TIMEOUT, ...) instead of trapping.
@@ -37,6 +41,15 @@ int32_t consume_device_error(cudaStream_t stream);  // synchronises `stream`
 
 // Number of SMs of the current device (cached per device).
 int sm_count();
+
+// Launch accounting and optional CUDA-event profiling per kernel class.
+void note_launch(int n = 1);
+struct ProfScope {
+  int slot;
+  cudaStream_t stream;
+  ProfScope(const char* cls, cudaStream_t s, double flops, double bytes);
+  ~ProfScope();
+};
 
 // Per-device staging area for small per-call descriptor arrays (leaves,
 // terms, status words).  Grows on demand; one per device; not thread-safe.

@@ -1,0 +1,455 @@
+// forward.cu -- public operator entry points and the population forward.
+//
+// The population forward is the B200 replacement of the reference's
+// evaluation seam: ForwardEvaluator::evaluate (rust/crates/ennx/src/
+// forward_program.rs:210-212) driven by ResidentBoState::ask_evaluate
+// (:706-720), with the decoder layer order of
+// KdaMoeMetalExecutor::encode_decode_layer (forward_metal.rs:614-810):
+//   rms_norm -> qkv proj -> split -> L2 norm q,k -> control proj -> split ->
+//   forget / output-gate proj -> gate, beta -> KDA -> post-norm * gate ->
+//   out proj -> residual -> rms_norm -> router top-k -> gate_up -> down ->
+//   residual
+// generalised to prefill over whole sequences, GQA layers every
+// `attn_period` layers, and a fused LM-head cross-entropy at the end.
+//
+// Work is organised per antithetic pair: the pair's W+sigma*eps and
+// W-sigma*eps copies of one layer are generated into a scratch area (HBM
+// streaming kernel), then both candidates' tokens run through the layer as
+// one batch; every GEMM is a 2-group tcgen05 launch (MoE: 2*E groups).
+#include <string.h>
+
+#include <algorithm>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ennx {
+namespace {
+
+constexpr int HD = 128;  // head dim of both attention kinds
+
+struct Carver {
+  uint8_t* base;
+  size_t off = 0, cap;
+  bool measure;
+  template <typename T>
+  T* take(size_t count) {
+    size_t bytes = (count * sizeof(T) + 255) & ~(size_t)255;
+    T* p = measure ? nullptr : reinterpret_cast<T*>(base + off);
+    off += bytes;
+    return p;
+  }
+};
+
+__global__ void targets_kernel(const int* __restrict__ tokens, int batch, int seq, int* __restrict__ inp,
+                               int* __restrict__ tgt2) {
+  int n = batch * seq;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+    int b = i / seq, t = i % seq;
+    inp[i] = tokens[b * (seq + 1) + t];
+    int y = tokens[b * (seq + 1) + t + 1];
+    tgt2[i] = y;
+    tgt2[i + n] = y;
+  }
+}
+
+// ---------------------------------------------------------------------------
+// MoE layer body shared by ennx_b200_moe_layer and the population forward
+// ---------------------------------------------------------------------------
+struct MoeBuffers {
+  float* logits;
+  int *idx, *counters, *offsets, *perm_pos, *src_row;
+  float *gate, *perm_gate;
+  uint16_t *xperm, *act, *yperm;
+};
+
+void carve_moe(Carver& c, long long tokens, int hidden, int experts, int top_k, int width, int sets, MoeBuffers& m) {
+  long long rows = tokens * top_k;
+  m.idx = c.take<int>(rows);
+  m.gate = c.take<float>(rows);
+  m.counters = c.take<int>(2 * sets * experts);
+  m.offsets = c.take<int>(sets * experts + 1);
+  m.perm_pos = c.take<int>(rows);
+  m.src_row = c.take<int>(rows);
+  m.perm_gate = c.take<float>(rows);
+  m.xperm = c.take<uint16_t>(rows * hidden);
+  m.act = c.take<uint16_t>(rows * width);
+  m.yperm = c.take<uint16_t>(rows * hidden);
+  m.logits = nullptr;
+}
+
+// x [tokens, hidden] -> out = residual + MoE(x).  Sets: rows < split use
+// expert block 0 of the weights, the rest block 1 (block stride = experts).
+int32_t run_moe(const uint16_t* x, const uint16_t* wr0, const uint16_t* wr1, const uint16_t* wgu, const uint16_t* wd,
+                long long tokens, long long split, int sets, int hidden, int experts, int top_k, int width,
+                const uint16_t* residual, uint16_t* out, MoeBuffers& m, cudaStream_t s) {
+  if (width % 128) return set_error(ENNX_B200_UNSUPPORTED, "moe: expert width %d must be a multiple of 128", width);
+  long long rows = tokens * top_k;
+  {
+    ProfScope ps("moe_routing", s, 2.0 * tokens * hidden * experts,
+                 2.0 * tokens * hidden + 2.0 * sets * experts * hidden + 4.0 * rows * hidden);
+    ENNX_TRY(launch_router_topk(x, hidden, wr0, sets > 1 ? wr1 : nullptr, split, tokens, hidden, experts, top_k,
+                                m.logits, m.idx, m.gate, s));
+    ENNX_TRY(launch_moe_permute(m.idx, m.gate, tokens, top_k, experts, split, sets, m.counters, m.offsets,
+                                m.perm_pos, m.src_row, m.perm_gate, s));
+    ENNX_TRY(launch_gather_rows(x, hidden, m.src_row, rows, hidden, m.xperm, s));
+  }
+  ennx_b200_gemm_params p;
+  memset(&p, 0, sizeof(p));
+  p.m = (int)rows; p.n = 2 * width; p.k = hidden;
+  p.lda = hidden; p.ldb = hidden; p.ldc = width;
+  p.groups = sets * experts; p.b_group_rows = 2 * width; p.group_offsets = m.offsets;
+  p.epilogue = ENNX_B200_EPI_SWIGLU; p.alpha = 1.0f;
+  {
+    ProfScope ps("gemm", s, 2.0 * rows * 2 * width * hidden,
+                 2.0 * (rows * hidden + (double)sets * experts * 2 * width * hidden + rows * width));
+    ENNX_TRY(gemm_bf16(&p, m.xperm, wgu, m.act, s));
+  }
+  memset(&p, 0, sizeof(p));
+  p.m = (int)rows; p.n = hidden; p.k = width;
+  p.lda = width; p.ldb = width; p.ldc = hidden;
+  p.groups = sets * experts; p.b_group_rows = hidden; p.group_offsets = m.offsets;
+  p.epilogue = ENNX_B200_EPI_ROWSCALE; p.row_scale = m.perm_gate; p.alpha = 1.0f;
+  {
+    ProfScope ps("gemm", s, 2.0 * rows * hidden * width,
+                 2.0 * (rows * width + (double)sets * experts * hidden * width + rows * hidden));
+    ENNX_TRY(gemm_bf16(&p, m.act, wd, m.yperm, s));
+  }
+  {
+    ProfScope ps("moe_combine", s, 0, 2.0 * (rows * hidden + 2.0 * tokens * hidden));
+    ENNX_TRY(launch_moe_combine(m.yperm, m.perm_pos, tokens, top_k, hidden, residual, out, s));
+  }
+  return ENNX_B200_OK;
+}
+
+// ---------------------------------------------------------------------------
+// population forward
+// ---------------------------------------------------------------------------
+enum Field { F_ATTN_NORM, F_QKV, F_CTL, F_FORGET, F_OGATE, F_DECAY, F_TB, F_OUT_NORM, F_WO, F_MOE_NORM, F_ROUTER,
+             F_GATE_UP, F_DOWN, F_COUNT };
+
+struct Shapes {
+  long long rows[F_COUNT], cols[F_COUNT];
+};
+
+bool is_gqa(const ennx_b200_model_config& c, int l) {
+  return c.attn_period > 0 && (l % c.attn_period) == c.attn_period - 1;
+}
+
+Shapes layer_shapes(const ennx_b200_model_config& c, bool gqa) {
+  Shapes s;
+  memset(&s, 0, sizeof(s));
+  const long long H = c.hidden, I = c.expert_width, E = c.experts;
+  const long long heads = gqa ? c.q_heads : c.kda_heads;
+  s.rows[F_ATTN_NORM] = 1; s.cols[F_ATTN_NORM] = H;
+  s.rows[F_QKV] = gqa ? (long long)(c.q_heads + 2 * c.kv_heads) * HD : 3LL * c.kda_heads * HD; s.cols[F_QKV] = H;
+  if (!gqa) {
+    s.rows[F_CTL] = 2LL * c.gate_rank + c.kda_heads; s.cols[F_CTL] = H;
+    s.rows[F_FORGET] = (long long)c.kda_heads * HD; s.cols[F_FORGET] = c.gate_rank;
+    s.rows[F_OGATE] = (long long)c.kda_heads * HD; s.cols[F_OGATE] = c.gate_rank;
+    s.rows[F_DECAY] = 1; s.cols[F_DECAY] = c.kda_heads;
+    s.rows[F_TB] = 1; s.cols[F_TB] = (long long)c.kda_heads * HD;
+    s.rows[F_OUT_NORM] = 1; s.cols[F_OUT_NORM] = HD;
+  }
+  s.rows[F_WO] = H; s.cols[F_WO] = heads * HD;
+  s.rows[F_MOE_NORM] = 1; s.cols[F_MOE_NORM] = H;
+  s.rows[F_ROUTER] = E; s.cols[F_ROUTER] = H;
+  s.rows[F_GATE_UP] = E * 2 * I; s.cols[F_GATE_UP] = H;
+  s.rows[F_DOWN] = E * H; s.cols[F_DOWN] = I;
+  return s;
+}
+
+size_t align_elems(long long n) { return (size_t)((n + 127) / 128 * 128); }  // 256-byte granules of bf16
+
+struct Work {
+  uint16_t *emb_scr;    // [2][V*H]
+  uint16_t *layer_scr;  // per-field [2][n] areas
+  size_t field_off[F_COUNT];  // element offsets into layer_scr (for the plus copy; minus follows)
+  uint16_t *hidden, *xn, *qkv, *ctl, *fg, *og, *o, *post;
+  float *gate, *beta;
+  int *inp, *tgt;
+  float *lse, *tlogit, *row_loss;
+  MoeBuffers moe;
+  size_t bytes;
+};
+
+int32_t validate_config(const ennx_b200_model_config* c, int batch, int seq) {
+  if (!c) return set_error(ENNX_B200_INVALID_ARGUMENT, "null model config");
+  if (c->layers <= 0 || c->hidden <= 0 || c->vocab <= 0 || batch <= 0 || seq <= 0)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "model config and token batch must be non-empty");
+  if (c->hidden % 256) return set_error(ENNX_B200_UNSUPPORTED, "hidden must be a multiple of 256");
+  if (c->expert_width % 128) return set_error(ENNX_B200_UNSUPPORTED, "expert_width must be a multiple of 128");
+  if (c->gate_rank % 64 || c->gate_rank <= 0) return set_error(ENNX_B200_UNSUPPORTED, "gate_rank must be a multiple of 64");
+  if (c->attn_period > 0 && (c->kv_heads <= 0 || c->q_heads % c->kv_heads))
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "q_heads must be a multiple of kv_heads");
+  if (c->top_k < 1 || c->top_k > 8 || c->top_k > c->experts)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "top_k must be in [1, min(8, experts)]");
+  if (2 * c->experts > 256) return set_error(ENNX_B200_UNSUPPORTED, "at most 128 experts");
+  return ENNX_B200_OK;
+}
+
+void carve_work(const ennx_b200_model_config& c, int batch, int seq, uint8_t* base, Work& w) {
+  Carver cv{base, 0, 0, base == nullptr};
+  const long long Tc = (long long)batch * seq, T = 2 * Tc, H = c.hidden;
+  w.emb_scr = cv.take<uint16_t>(2 * align_elems((long long)c.vocab * H));
+  size_t per_field_max[F_COUNT] = {0};
+  for (int g = 0; g < 2; ++g) {
+    Shapes sh = layer_shapes(c, g == 1);
+    for (int f = 0; f < F_COUNT; ++f) {
+      size_t n = align_elems(sh.rows[f] * sh.cols[f]);
+      if (n > per_field_max[f]) per_field_max[f] = n;
+    }
+  }
+  size_t off = 0;
+  for (int f = 0; f < F_COUNT; ++f) { w.field_off[f] = off; off += 2 * per_field_max[f]; }
+  w.layer_scr = cv.take<uint16_t>(off);
+  const long long qkv_cols = std::max(3LL * c.kda_heads, (long long)(c.q_heads + 2 * c.kv_heads)) * HD;
+  const long long heads_max = std::max(c.kda_heads, c.q_heads);
+  const long long ctl_cols = (2LL * c.gate_rank + c.kda_heads + 7) / 8 * 8;
+  w.hidden = cv.take<uint16_t>(T * H);
+  w.xn = cv.take<uint16_t>(T * H);
+  w.qkv = cv.take<uint16_t>(T * qkv_cols);
+  w.ctl = cv.take<uint16_t>(T * ctl_cols);
+  w.fg = cv.take<uint16_t>(T * c.kda_heads * HD);
+  w.og = cv.take<uint16_t>(T * c.kda_heads * HD);
+  w.o = cv.take<uint16_t>(T * heads_max * HD);
+  w.post = cv.take<uint16_t>(T * c.kda_heads * HD);
+  w.gate = cv.take<float>(T * c.kda_heads * HD);
+  w.beta = cv.take<float>(T * c.kda_heads);
+  w.inp = cv.take<int>(Tc);
+  w.tgt = cv.take<int>(T);
+  const long long ntiles = (c.vocab + 255) / 256;
+  w.lse = cv.take<float>(T * ntiles * 2);
+  w.tlogit = cv.take<float>(T);
+  w.row_loss = cv.take<float>(T);
+  carve_moe(cv, T, c.hidden, c.experts, c.top_k, c.expert_width, 2, w.moe);
+  w.bytes = cv.off;
+}
+
+const uint16_t* field_ptr(const ennx_b200_layer_weights& L, int f) {
+  switch (f) {
+    case F_ATTN_NORM: return L.attn_norm;
+    case F_QKV: return L.w_qkv;
+    case F_CTL: return L.w_ctl;
+    case F_FORGET: return L.w_forget;
+    case F_OGATE: return L.w_ogate;
+    case F_DECAY: return L.decay;
+    case F_TB: return L.time_bias;
+    case F_OUT_NORM: return L.out_norm;
+    case F_WO: return L.w_o;
+    case F_MOE_NORM: return L.moe_norm;
+    case F_ROUTER: return L.w_router;
+    case F_GATE_UP: return L.w_gate_up;
+    default: return L.w_down;
+  }
+}
+
+int32_t perturb_pair(const uint16_t* src, long long n, uint64_t seed, uint32_t pair, uint32_t tensor, float sigma,
+                     uint16_t* dst_plus, uint16_t* dst_minus, cudaStream_t s) {
+  if (!src) return set_error(ENNX_B200_INVALID_ARGUMENT, "missing weight tensor %u", tensor);
+  ProfScope ps("perturb", s, 0, 6.0 * n);
+  return ennx_b200_perturb_bf16(src, (size_t)n, seed, pair, tensor, sigma, dst_plus, dst_minus, s);
+}
+
+int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* b, long long n, long long k, void* c, long long ldc,
+              long long rows, const uint16_t* residual, cudaStream_t s) {
+  ennx_b200_gemm_params p;
+  memset(&p, 0, sizeof(p));
+  p.m = (int)rows; p.n = (int)n; p.k = (int)k;
+  p.lda = lda; p.ldb = k; p.ldc = ldc;
+  p.groups = 2; p.b_group_rows = (int)n;
+  p.epilogue = ENNX_B200_EPI_BF16; p.alpha = 1.0f;
+  p.residual = residual; p.ldr = ldc;
+  ProfScope ps("gemm", s, 2.0 * rows * n * k, 2.0 * (rows * k + 2.0 * n * k + rows * n * (residual ? 2 : 1)));
+  return gemm_bf16(&p, a, b, c, s);
+}
+
+int32_t run_pair(const ennx_b200_model_config& c, const ennx_b200_model_weights& W, uint64_t seed, float sigma,
+                 uint32_t pair, int batch, int seq, Work& w, float* fit, cudaStream_t s) {
+  const long long Tc = (long long)batch * seq, T = 2 * Tc, H = c.hidden, V = c.vocab;
+  const size_t vh = align_elems(V * H);
+  uint16_t* e_plus = w.emb_scr;
+  uint16_t* e_minus = w.emb_scr + vh;
+  ENNX_TRY(perturb_pair(W.embedding, V * H, seed, pair, 0, sigma, e_plus, e_minus, s));
+  ENNX_TRY(launch_embed(w.inp, e_plus, e_minus, Tc, T, (int)H, (int)V, w.hidden, s));
+
+  for (int l = 0; l < c.layers; ++l) {
+    const ennx_b200_layer_weights& L = W.layers[l];
+    const bool gqa = is_gqa(c, l);
+    Shapes sh = layer_shapes(c, gqa);
+    uint16_t* P[F_COUNT];
+    uint16_t* M[F_COUNT];
+    for (int f = 0; f < F_COUNT; ++f) {
+      long long n = sh.rows[f] * sh.cols[f];
+      P[f] = M[f] = nullptr;
+      if (n == 0) continue;
+      P[f] = w.layer_scr + w.field_off[f];
+      // minus copy directly after plus (GEMM operands: n % 64 == 0, so the
+      // B row-block stride between the two signs is exactly `rows`)
+      M[f] = P[f] + (n % 8 == 0 ? (size_t)n : align_elems(n));
+      ENNX_TRY(perturb_pair(field_ptr(L, f), n, seed, pair, 16 + 16 * l + f, sigma, P[f], M[f], s));
+    }
+    // ---- mixer ----
+    ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_ATTN_NORM], M[F_ATTN_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
+    const long long qkv_cols = sh.rows[F_QKV];
+    ENNX_TRY(gemm2(w.xn, H, P[F_QKV], qkv_cols, H, w.qkv, qkv_cols, T, nullptr, s));
+    if (gqa) {
+      const long long kd = (long long)c.q_heads * HD, vd = kd + (long long)c.kv_heads * HD;
+      ENNX_TRY(launch_rope(w.qkv, qkv_cols, c.q_heads, HD, T, seq, c.rope_theta, s));
+      ENNX_TRY(launch_rope(w.qkv + kd, qkv_cols, c.kv_heads, HD, T, seq, c.rope_theta, s));
+      {
+        ProfScope ps("attention", s, 2.0 * batch * c.q_heads * (double)seq * (seq + 1) * HD * 2.0,
+                     2.0 * T * (2.0 * kd + 2.0 * c.kv_heads * HD));
+        ENNX_TRY(launch_gqa_attention(w.qkv, qkv_cols, w.qkv + kd, qkv_cols, w.qkv + vd, qkv_cols, w.o, kd, 2 * batch,
+                                      seq, c.q_heads, c.kv_heads, s));
+      }
+      ENNX_TRY(gemm2(w.o, kd, P[F_WO], H, kd, w.hidden, H, T, w.hidden, s));
+    } else {
+      const long long hw = (long long)c.kda_heads * HD, r = c.gate_rank;
+      const long long ctl_cols = sh.rows[F_CTL];
+      const long long ldctl = (ctl_cols + 7) / 8 * 8;
+      ENNX_TRY(gemm2(w.xn, H, P[F_CTL], ctl_cols, H, w.ctl, ldctl, T, nullptr, s));
+      ENNX_TRY(gemm2(w.ctl, ldctl, P[F_FORGET], hw, r, w.fg, hw, T, nullptr, s));
+      ENNX_TRY(gemm2(w.ctl + r, ldctl, P[F_OGATE], hw, r, w.og, hw, T, nullptr, s));
+      ENNX_TRY(launch_kda_gate(w.fg, hw, w.ctl + 2 * r, ldctl, P[F_DECAY], M[F_DECAY], P[F_TB], M[F_TB], Tc, T,
+                               c.kda_heads, HD, w.gate, w.beta, s));
+      ENNX_TRY(launch_l2norm_heads(w.qkv, qkv_cols, c.kda_heads, T, s));
+      ENNX_TRY(launch_l2norm_heads(w.qkv + hw, qkv_cols, c.kda_heads, T, s));
+      {
+        ProfScope ps("kda", s, (double)T * c.kda_heads * (6.0 * HD * HD + 6.0 * 64 * HD),
+                     (double)T * c.kda_heads * HD * (2.0 * 4 + 4.0) + 4.0 * T * c.kda_heads);
+        ENNX_TRY(launch_kda_chunked(w.qkv, w.qkv + hw, w.qkv + 2 * hw, qkv_cols, w.gate, w.beta, nullptr, w.o, hw,
+                                    2 * batch, seq, c.kda_heads, s));
+      }
+      ENNX_TRY(launch_kda_post(w.o, w.og, hw, P[F_OUT_NORM], M[F_OUT_NORM], Tc, c.kda_heads, T, c.rms_eps, w.post, s));
+      ENNX_TRY(gemm2(w.post, hw, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s));
+    }
+    // ---- MoE ----
+    ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_MOE_NORM], M[F_MOE_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
+    ENNX_TRY(run_moe(w.xn, P[F_ROUTER], M[F_ROUTER], P[F_GATE_UP], P[F_DOWN], T, Tc, 2, (int)H, c.experts, c.top_k,
+                     c.expert_width, w.hidden, w.hidden, w.moe, s));
+  }
+  // ---- final norm + fused LM-head cross-entropy ----
+  uint16_t* fn = w.layer_scr + w.field_off[F_ATTN_NORM];  // reuse: final norm pair
+  ENNX_TRY(perturb_pair(W.final_norm, H, seed, pair, 1, sigma, fn, fn + H, s));
+  ENNX_TRY(launch_rmsnorm(w.hidden, H, fn, fn + H, Tc, w.xn, H, T, (int)H, c.rms_eps, s));
+  ennx_b200_gemm_params p;
+  memset(&p, 0, sizeof(p));
+  p.m = (int)T; p.n = (int)V; p.k = (int)H;
+  p.lda = H; p.ldb = H;
+  p.groups = 2; p.b_group_rows = (int)V;
+  p.epilogue = ENNX_B200_EPI_LSE; p.alpha = 1.0f;
+  p.targets = w.tgt; p.lse_partial = w.lse; p.target_logit = w.tlogit;
+  if (vh != (size_t)(V * H)) return set_error(ENNX_B200_UNSUPPORTED, "vocab*hidden must be a multiple of 128");
+  {
+    ProfScope ps("gemm", s, 2.0 * T * V * H, 2.0 * (T * H + 2.0 * V * H));
+    ENNX_TRY(gemm_bf16(&p, w.xn, e_plus, nullptr, s));
+  }
+  ENNX_TRY(launch_lse_loss(w.lse, (int)((V + 255) / 256), w.tlogit, T, w.row_loss, s));
+  ENNX_TRY(launch_mean_per_set(w.row_loss, Tc, 2, fit, s));
+  return ENNX_B200_OK;
+}
+
+}  // namespace
+}  // namespace ennx
+
+using namespace ennx;
+
+extern "C" {
+
+int32_t ennx_b200_rmsnorm_bf16(const uint16_t* x, const uint16_t* w, int64_t rows, int32_t width, float eps,
+                               uint16_t* out, void* stream) {
+  if (!x || !w || !out || rows <= 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "rmsnorm: empty input");
+  if ((((uintptr_t)x | (uintptr_t)w | (uintptr_t)out) & 15u))
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "rmsnorm: buffers must be 16-byte aligned");
+  return launch_rmsnorm(x, width, w, nullptr, rows, out, width, rows, width, eps, (cudaStream_t)stream);
+}
+
+int32_t ennx_b200_moe_route(const uint16_t* x, const uint16_t* w_router, int64_t tokens, int32_t hidden,
+                            int32_t experts, int32_t top_k, float* logits, int32_t* index, float* gate, void* stream) {
+  if (!x || !w_router || !index || !gate || tokens <= 0)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "moe_route: null or empty argument");
+  return launch_router_topk(x, hidden, w_router, nullptr, tokens, tokens, hidden, experts, top_k, logits, index, gate,
+                            (cudaStream_t)stream);
+}
+
+size_t ennx_b200_moe_workspace_size(int64_t tokens, int32_t hidden, int32_t experts, int32_t top_k,
+                                    int32_t expert_width) {
+  Carver c{nullptr, 0, 0, true};
+  MoeBuffers m;
+  carve_moe(c, tokens, hidden, experts, top_k, expert_width, 1, m);
+  return c.off;
+}
+
+int32_t ennx_b200_moe_layer(const uint16_t* x, const uint16_t* w_router, const uint16_t* w_gate_up,
+                            const uint16_t* w_down, int64_t tokens, int32_t hidden, int32_t experts, int32_t top_k,
+                            int32_t expert_width, const uint16_t* residual, uint16_t* y, int32_t* index, float* gate,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  if (!x || !w_router || !w_gate_up || !w_down || !y || tokens <= 0)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "moe_layer: null or empty argument");
+  size_t need = ennx_b200_moe_workspace_size(tokens, hidden, experts, top_k, expert_width);
+  if (!workspace || workspace_bytes < need)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "moe_layer: workspace of %zu bytes required", need);
+  Carver c{(uint8_t*)workspace, 0, workspace_bytes, false};
+  MoeBuffers m;
+  carve_moe(c, tokens, hidden, experts, top_k, expert_width, 1, m);
+  cudaStream_t s = (cudaStream_t)stream;
+  ENNX_TRY(run_moe(x, w_router, nullptr, w_gate_up, w_down, tokens, tokens, 1, hidden, experts, top_k, expert_width,
+                   residual, y, m, s));
+  if (index) ENNX_CUDA(cudaMemcpyAsync(index, m.idx, sizeof(int) * tokens * top_k, cudaMemcpyDeviceToDevice, s), "idx");
+  if (gate) ENNX_CUDA(cudaMemcpyAsync(gate, m.gate, sizeof(float) * tokens * top_k, cudaMemcpyDeviceToDevice, s), "gate");
+  return ENNX_B200_OK;
+}
+
+int32_t ennx_b200_gqa_attention(uint16_t* q, uint16_t* k, const uint16_t* v, uint16_t* o, int32_t batch, int32_t seq,
+                                int32_t hq, int32_t hkv, float rope_theta, void* stream) {
+  if (!q || !k || !v || !o) return set_error(ENNX_B200_INVALID_ARGUMENT, "attention: null argument");
+  cudaStream_t s = (cudaStream_t)stream;
+  long long T = (long long)batch * seq;
+  if (rope_theta > 0.0f) {
+    ENNX_TRY(launch_rope(q, (long long)hq * HD, hq, HD, T, seq, rope_theta, s));
+    ENNX_TRY(launch_rope(k, (long long)hkv * HD, hkv, HD, T, seq, rope_theta, s));
+  }
+  return launch_gqa_attention(q, (long long)hq * HD, k, (long long)hkv * HD, v, (long long)hkv * HD, o,
+                              (long long)hq * HD, batch, seq, hq, hkv, s);
+}
+
+int32_t ennx_b200_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
+                              const float* beta, float* state, uint16_t* o, int32_t batch, int32_t seq, int32_t heads,
+                              void* stream) {
+  if (!q || !k || !v || !g || !beta || !o) return set_error(ENNX_B200_INVALID_ARGUMENT, "kda: null argument");
+  return launch_kda_chunked(q, k, v, (long long)heads * HD, g, beta, state, o, (long long)heads * HD, batch, seq,
+                            heads, (cudaStream_t)stream);
+}
+
+size_t ennx_b200_population_workspace_size(const ennx_b200_model_config* cfg, int32_t batch, int32_t seq) {
+  if (!cfg || validate_config(cfg, batch, seq) != ENNX_B200_OK) return 0;
+  Work w;
+  carve_work(*cfg, batch, seq, nullptr, w);
+  return w.bytes;
+}
+
+int32_t ennx_b200_population_forward(const ennx_b200_model_config* cfg, const ennx_b200_model_weights* weights,
+                                     uint64_t seed, float sigma, int32_t first_pair, int32_t num_pairs,
+                                     const int32_t* tokens, int32_t batch, int32_t seq, float* fitness,
+                                     void* workspace, size_t workspace_bytes, void* stream) {
+  ENNX_TRY(validate_config(cfg, batch, seq));
+  if (!weights || !weights->embedding || !weights->final_norm || !weights->layers || !tokens || !fitness)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "population_forward: null argument");
+  if (num_pairs <= 0 || first_pair < 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "population_forward: empty pair range");
+  if (!isfinite(sigma) || sigma < 0.0f) return set_error(ENNX_B200_INVALID_ARGUMENT, "sigma must be finite and >= 0");
+  Work w;
+  carve_work(*cfg, batch, seq, nullptr, w);
+  if (!workspace || workspace_bytes < w.bytes)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "population_forward: workspace of %zu bytes required", w.bytes);
+  carve_work(*cfg, batch, seq, (uint8_t*)workspace, w);
+  cudaStream_t s = (cudaStream_t)stream;
+  targets_kernel<<<(batch * seq + 255) / 256, 256, 0, s>>>(tokens, batch, seq, w.inp, w.tgt);
+  ENNX_LAUNCH_CHECK("targets");
+  for (int i = 0; i < num_pairs; ++i)
+    ENNX_TRY(run_pair(*cfg, *weights, seed, sigma, (uint32_t)(first_pair + i), batch, seq, w, fitness + 2 * i, s));
+  return ENNX_B200_OK;
+}
+
+}  // extern "C"

@@ -23,6 +23,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace ennx {
 namespace {
@@ -316,11 +317,9 @@ bool g_attr_set[64];
 }  // namespace
 }  // namespace ennx
 
-using namespace ennx;
+namespace ennx {
 
-extern "C" int32_t ennx_b200_gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint16_t* B,
-                                       void* C, void* stream) {
-  cudaStream_t st = (cudaStream_t)stream;
+int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint16_t* B, void* C, cudaStream_t st) {
   if (!p || !A || !B) return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: null argument");
   const int M = p->m, N = p->n, K = p->k;
   const int G = p->groups < 1 ? 1 : p->groups;
@@ -385,4 +384,11 @@ extern "C" int32_t ennx_b200_gemm_bf16(const ennx_b200_gemm_params* p, const uin
   gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, a);
   ENNX_LAUNCH_CHECK("gemm launch");
   return ENNX_B200_OK;
+}
+
+}  // namespace ennx
+
+extern "C" int32_t ennx_b200_gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint16_t* B,
+                                       void* C, void* stream) {
+  return ennx::gemm_bf16(p, A, B, C, (cudaStream_t)stream);
 }

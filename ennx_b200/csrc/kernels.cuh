@@ -1,0 +1,57 @@
+// kernels.cuh -- internal launchers shared by the C-ABI entry points and the
+// population-forward orchestrator.  All launch on `s`, validate their own
+// shape contract, and return an ENNX_B200_* status.
+#pragma once
+#include "common.cuh"
+
+namespace ennx {
+
+// norm.cu
+int32_t launch_rmsnorm(const uint16_t* x, long long ldx, const uint16_t* w0, const uint16_t* w1, long long split,
+                       uint16_t* out, long long ldo, long long rows, int width, float eps, cudaStream_t s);
+int32_t launch_embed(const int* tokens, const uint16_t* t0, const uint16_t* t1, long long per_set, long long rows,
+                     int width, int vocab, uint16_t* out, cudaStream_t s);
+int32_t launch_l2norm_heads(uint16_t* base, long long ld, int heads, long long rows, cudaStream_t s);
+int32_t launch_kda_gate(const uint16_t* raw, long long ldraw, const uint16_t* rbeta, long long ldb,
+                        const uint16_t* decay0, const uint16_t* decay1, const uint16_t* tb0, const uint16_t* tb1,
+                        long long split, long long rows, int heads, int head_width, float* gate, float* beta,
+                        cudaStream_t s);
+int32_t launch_kda_post(const uint16_t* o, const uint16_t* og, long long ldog, const uint16_t* n0, const uint16_t* n1,
+                        long long split, int heads, long long rows, float eps, uint16_t* out, cudaStream_t s);
+int32_t launch_rope(uint16_t* base, long long ld, int heads, int dim, long long rows, int seq, float theta,
+                    cudaStream_t s);
+
+// moe.cu
+int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0, const uint16_t* w1, long long split,
+                           long long tokens, int hidden, int experts, int top_k, float* logits, int* idx,
+                           float* gate, cudaStream_t s);
+// Builds the expert-major permutation.  Group of (token t, rank r) is
+// set(t) * experts + idx[t, r] (set = t >= split).  Writes group_offsets
+// [sets*experts + 1], perm_pos[t*k + r] (row of (t, r) in permuted order),
+// src_row[pos], perm_gate[pos].  `counters` is scratch int[2*sets*experts].
+int32_t launch_moe_permute(const int* idx, const float* gate, long long tokens, int top_k, int experts, long long split,
+                           int sets, int* counters, int* group_offsets, int* perm_pos, int* src_row,
+                           float* perm_gate, cudaStream_t s);
+int32_t launch_gather_rows(const uint16_t* x, long long ldx, const int* src_row, long long rows, int width,
+                           uint16_t* out, cudaStream_t s);
+// hidden[t] = residual[t] + sum_r y[perm_pos[t*k + r]]
+int32_t launch_moe_combine(const uint16_t* y, const int* perm_pos, long long tokens, int top_k, int width,
+                           const uint16_t* residual, uint16_t* out, cudaStream_t s);
+
+// loss.cu
+int32_t launch_lse_loss(const float* lse_partial, int n_tiles, const float* target_logit, long long rows,
+                        float* row_loss, cudaStream_t s);
+int32_t launch_mean_per_set(const float* row_loss, long long rows_per_set, int sets, float* out, cudaStream_t s);
+
+// attention.cu / kda.cu
+int32_t launch_gqa_attention(const uint16_t* q, long long ldq, const uint16_t* k, long long ldk, const uint16_t* v,
+                             long long ldv, uint16_t* o, long long ldo, int batch, int seq, int hq, int hkv,
+                             cudaStream_t s);
+int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, long long ld_qkv,
+                           const float* g, const float* beta, float* state, uint16_t* o, long long ldo, int batch,
+                           int seq, int heads, cudaStream_t s);
+
+// gemm.cu (internal form of ennx_b200_gemm_bf16)
+int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* a, const uint16_t* b, void* c, cudaStream_t s);
+
+}  // namespace ennx

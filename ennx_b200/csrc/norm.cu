@@ -1,0 +1,235 @@
+// norm.cu -- memory-bound elementwise/normalisation kernels of the hybrid
+// forward: RMSNorm, embedding gather, per-head L2 norm, KDA gate/beta,
+// KDA output norm + gate, RoPE.  One warp per row (or per token-head),
+// 16-byte loads, warp-shuffle reductions, fp32 math, bf16 RNE stores.
+//
+// Formulas restate rust/crates/ennx/src/kda_moe.metal:
+//   decoder_rms_norm          :536-554
+//   kda_normalize_qk          :510-534
+//   kda_make_gate_beta_16k    :869-895
+//   kda_postprocess_16k       :898-921
+//   token_embedding_lookup    :990-1003
+// RoPE has no reference counterpart (rotate-half pairing, theta given).
+#include "common.cuh"
+#include "kernels.cuh"
+
+namespace ennx {
+
+__device__ __forceinline__ void unpack8(uint4 v, float f[8]) {
+  uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    f[2 * i] = bf16_to_f32((uint16_t)(w[i] & 0xffffu));
+    f[2 * i + 1] = bf16_to_f32((uint16_t)(w[i] >> 16));
+  }
+}
+__device__ __forceinline__ uint4 pack8(const float f[8]) {
+  return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                    pack_bf16x2(f[6], f[7]));
+}
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// y = x * rsqrt(mean(x^2) + eps) * w; rows [0, split) use w0, the rest w1.
+__global__ void rmsnorm_kernel(const uint16_t* __restrict__ x, long long ldx, const uint16_t* __restrict__ w0,
+                               const uint16_t* __restrict__ w1, long long split, uint16_t* __restrict__ out,
+                               long long ldo, long long rows, int width, float eps) {
+  long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const uint16_t* w = row < split ? w0 : w1;
+  const uint16_t* xr = x + row * ldx;
+  float ss = 0.0f;
+  for (int c = lane * 8; c < width; c += 256) {
+    float f[8];
+    unpack8(*reinterpret_cast<const uint4*>(xr + c), f);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss = fmaf(f[i], f[i], ss);
+  }
+  ss = warp_sum(ss);
+  float inv = rsqrtf(ss / (float)width + eps);
+  uint16_t* o = out + row * ldo;
+  for (int c = lane * 8; c < width; c += 256) {
+    float f[8], g[8];
+    unpack8(*reinterpret_cast<const uint4*>(xr + c), f);
+    unpack8(*reinterpret_cast<const uint4*>(w + c), g);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) f[i] = f[i] * inv * g[i];
+    *reinterpret_cast<uint4*>(o + c) = pack8(f);
+  }
+}
+
+// hidden[r] = table_s[tokens[r % per_set]] for r in set s (s = r / per_set).
+__global__ void embed_kernel(const int* __restrict__ tokens, const uint16_t* __restrict__ t0,
+                             const uint16_t* __restrict__ t1, long long per_set, long long rows, int width,
+                             int vocab, uint16_t* __restrict__ out, int* err) {
+  long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  int tok = tokens[row % per_set];
+  if (tok < 0 || tok >= vocab) {
+    if (lane == 0) atomicExch(err, ENNX_B200_INVALID_ARGUMENT);
+    tok = 0;
+  }
+  const uint16_t* src = (row < per_set ? t0 : t1) + (long long)tok * width;
+  uint16_t* dst = out + row * width;
+  for (int c = lane * 8; c < width; c += 256)
+    *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(src + c);
+}
+
+// In-place per-head L2 normalisation, 1/max(|x|, 1e-6), head width 128.
+// groups = rows * heads; head h of row r starts at base + r*ld + h*128.
+__global__ void l2norm_heads_kernel(uint16_t* __restrict__ base, long long ld, int heads, long long groups) {
+  long long gidx = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (gidx >= groups) return;
+  uint16_t* p = base + (gidx / heads) * ld + (gidx % heads) * 128 + lane * 4;
+  uint2 raw = *reinterpret_cast<uint2*>(p);
+  float f[4] = {bf16_to_f32(raw.x & 0xffffu), bf16_to_f32(raw.x >> 16), bf16_to_f32(raw.y & 0xffffu),
+                bf16_to_f32(raw.y >> 16)};
+  float ss = warp_sum(f[0] * f[0] + f[1] * f[1] + f[2] * f[2] + f[3] * f[3]);
+  float inv = 1.0f / fmaxf(sqrtf(ss), 1e-6f);
+  *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(f[0] * inv, f[1] * inv), pack_bf16x2(f[2] * inv, f[3] * inv));
+}
+
+__device__ __forceinline__ float softplus_stable(float x) { return fmaxf(x, 0.0f) + log1pf(__expf(-fabsf(x))); }
+
+// g[r, j] = max(-exp(decay[h]) * softplus(raw[r, j] + time_bias[j]), -5)   (fp32 out)
+// beta[r, h] = sigmoid(raw_beta[r, h])                                       (fp32 out)
+// Parameters (decay, time_bias) are bf16 and per set (rows < split use set 0).
+__global__ void kda_gate_kernel(const uint16_t* __restrict__ raw, long long ldraw, const uint16_t* __restrict__ rbeta,
+                                long long ldb, const uint16_t* __restrict__ decay0, const uint16_t* __restrict__ decay1,
+                                const uint16_t* __restrict__ tb0, const uint16_t* __restrict__ tb1, long long split,
+                                long long rows, int heads, int head_width, float* __restrict__ gate,
+                                float* __restrict__ beta) {
+  int width = heads * head_width;
+  long long total = rows * (long long)width;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    long long r = i / width;
+    int j = (int)(i % width);
+    int h = j / head_width;
+    bool s0 = r < split;
+    float x = bf16_to_f32(raw[r * ldraw + j]) + bf16_to_f32((s0 ? tb0 : tb1)[j]);
+    float g = -__expf(bf16_to_f32((s0 ? decay0 : decay1)[h])) * softplus_stable(x);
+    gate[i] = fmaxf(g, -5.0f);
+    if (j % head_width == 0) beta[r * heads + h] = 1.0f / (1.0f + __expf(-bf16_to_f32(rbeta[r * ldb + h])));
+  }
+}
+
+// out = rmsnorm_head(o) * norm * sigmoid(og), head width 128; norm per set.
+__global__ void kda_post_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ og, long long ldog,
+                                const uint16_t* __restrict__ n0, const uint16_t* __restrict__ n1, long long split,
+                                int heads, long long groups, float eps, uint16_t* __restrict__ out) {
+  long long gidx = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  int lane = threadIdx.x & 31;
+  if (gidx >= groups) return;
+  long long r = gidx / heads;
+  int h = (int)(gidx % heads);
+  long long off = r * (long long)heads * 128 + h * 128 + lane * 4;
+  uint2 raw = *reinterpret_cast<const uint2*>(o + off);
+  uint2 graw = *reinterpret_cast<const uint2*>(og + r * ldog + h * 128 + lane * 4);
+  const uint16_t* nw = (r < split ? n0 : n1) + lane * 4;
+  float f[4] = {bf16_to_f32(raw.x & 0xffffu), bf16_to_f32(raw.x >> 16), bf16_to_f32(raw.y & 0xffffu),
+                bf16_to_f32(raw.y >> 16)};
+  float g[4] = {bf16_to_f32(graw.x & 0xffffu), bf16_to_f32(graw.x >> 16), bf16_to_f32(graw.y & 0xffffu),
+                bf16_to_f32(graw.y >> 16)};
+  float ss = warp_sum(f[0] * f[0] + f[1] * f[1] + f[2] * f[2] + f[3] * f[3]);
+  float inv = rsqrtf(ss / 128.0f + eps);
+  float y[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) y[i] = f[i] * inv * bf16_to_f32(nw[i]) / (1.0f + __expf(-g[i]));
+  *reinterpret_cast<uint2*>(out + off) = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+}
+
+// Rotate-half RoPE in place on `heads` heads of width dim starting at base + r*ld.
+// Position of row r is r % seq.
+__global__ void rope_kernel(uint16_t* __restrict__ base, long long ld, int heads, int dim, long long rows, int seq,
+                            float log2_theta) {
+  int half = dim / 2;
+  long long total = rows * heads * (long long)half;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    int k = (int)(i % half);
+    long long rh = i / half;
+    long long r = rh / heads;
+    int h = (int)(rh % heads);
+    float pos = (float)(r % seq);
+    float inv_freq = exp2f(-log2_theta * (2.0f * k / (float)dim));
+    float s, c;
+    sincosf(pos * inv_freq, &s, &c);
+    uint16_t* p = base + r * ld + (long long)h * dim;
+    float x1 = bf16_to_f32(p[k]), x2 = bf16_to_f32(p[k + half]);
+    p[k] = f32_to_bf16_rne(x1 * c - x2 * s);
+    p[k + half] = f32_to_bf16_rne(x2 * c + x1 * s);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// launchers
+// ---------------------------------------------------------------------------
+static int warp_rows_grid(long long rows, int warps_per_block) {
+  return (int)((rows + warps_per_block - 1) / warps_per_block);
+}
+static int stride_grid(long long n, int threads) {
+  long long b = (n + threads - 1) / threads;
+  long long cap = (long long)sm_count() * 16;
+  return (int)(b < cap ? (b > 0 ? b : 1) : cap);
+}
+
+int32_t launch_rmsnorm(const uint16_t* x, long long ldx, const uint16_t* w0, const uint16_t* w1, long long split,
+                       uint16_t* out, long long ldo, long long rows, int width, float eps, cudaStream_t s) {
+  if (width % 256 != 0) return set_error(ENNX_B200_UNSUPPORTED, "rmsnorm width %d must be a multiple of 256", width);
+  rmsnorm_kernel<<<warp_rows_grid(rows, 8), 256, 0, s>>>(x, ldx, w0, w1 ? w1 : w0, w1 ? split : rows, out, ldo,
+                                                          rows, width, eps);
+  ENNX_LAUNCH_CHECK("rmsnorm");
+  return ENNX_B200_OK;
+}
+
+int32_t launch_embed(const int* tokens, const uint16_t* t0, const uint16_t* t1, long long per_set, long long rows,
+                     int width, int vocab, uint16_t* out, cudaStream_t s) {
+  if (width % 256 != 0) return set_error(ENNX_B200_UNSUPPORTED, "embedding width must be a multiple of 256");
+  embed_kernel<<<warp_rows_grid(rows, 8), 256, 0, s>>>(tokens, t0, t1 ? t1 : t0, per_set, rows, width, vocab, out,
+                                                        device_error_word());
+  ENNX_LAUNCH_CHECK("embed");
+  return ENNX_B200_OK;
+}
+
+int32_t launch_l2norm_heads(uint16_t* base, long long ld, int heads, long long rows, cudaStream_t s) {
+  long long groups = rows * heads;
+  l2norm_heads_kernel<<<warp_rows_grid(groups, 8), 256, 0, s>>>(base, ld, heads, groups);
+  ENNX_LAUNCH_CHECK("l2norm_heads");
+  return ENNX_B200_OK;
+}
+
+int32_t launch_kda_gate(const uint16_t* raw, long long ldraw, const uint16_t* rbeta, long long ldb,
+                        const uint16_t* decay0, const uint16_t* decay1, const uint16_t* tb0, const uint16_t* tb1,
+                        long long split, long long rows, int heads, int head_width, float* gate, float* beta,
+                        cudaStream_t s) {
+  long long total = rows * heads * (long long)head_width;
+  kda_gate_kernel<<<stride_grid(total, 256), 256, 0, s>>>(raw, ldraw, rbeta, ldb, decay0, decay1 ? decay1 : decay0,
+                                                           tb0, tb1 ? tb1 : tb0, decay1 ? split : rows, rows, heads,
+                                                           head_width, gate, beta);
+  ENNX_LAUNCH_CHECK("kda_gate");
+  return ENNX_B200_OK;
+}
+
+int32_t launch_kda_post(const uint16_t* o, const uint16_t* og, long long ldog, const uint16_t* n0, const uint16_t* n1,
+                        long long split, int heads, long long rows, float eps, uint16_t* out, cudaStream_t s) {
+  long long groups = rows * heads;
+  kda_post_kernel<<<warp_rows_grid(groups, 8), 256, 0, s>>>(o, og, ldog, n0, n1 ? n1 : n0, n1 ? split : rows, heads,
+                                                             groups, eps, out);
+  ENNX_LAUNCH_CHECK("kda_post");
+  return ENNX_B200_OK;
+}
+
+int32_t launch_rope(uint16_t* base, long long ld, int heads, int dim, long long rows, int seq, float theta,
+                    cudaStream_t s) {
+  long long total = rows * heads * (long long)(dim / 2);
+  rope_kernel<<<stride_grid(total, 256), 256, 0, s>>>(base, ld, heads, dim, rows, seq, log2f(theta));
+  ENNX_LAUNCH_CHECK("rope");
+  return ENNX_B200_OK;
+}
+
+}  // namespace ennx

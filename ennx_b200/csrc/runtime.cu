@@ -4,8 +4,10 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
 
@@ -122,9 +124,90 @@ int32_t make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, ui
   return ENNX_B200_OK;
 }
 
+static std::atomic<uint64_t> g_launches{0};
+void note_launch(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+struct ProfClass {
+  std::string name;
+  int64_t launches = 0;
+  double flops = 0, bytes = 0;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;
+};
+static thread_local bool g_prof_on = false;
+static thread_local std::vector<ProfClass> g_prof;
+static thread_local std::vector<cudaEvent_t> g_event_pool;
+
+static cudaEvent_t take_event() {
+  if (!g_event_pool.empty()) {
+    cudaEvent_t e = g_event_pool.back();
+    g_event_pool.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  cudaEventCreate(&e);
+  return e;
+}
+
+ProfScope::ProfScope(const char* cls, cudaStream_t s, double flops, double bytes) : slot(-1), stream(s) {
+  if (!g_prof_on) return;
+  for (size_t i = 0; i < g_prof.size(); ++i)
+    if (g_prof[i].name == cls) slot = (int)i;
+  if (slot < 0) {
+    g_prof.push_back(ProfClass());
+    g_prof.back().name = cls;
+    slot = (int)g_prof.size() - 1;
+  }
+  ProfClass& c = g_prof[slot];
+  c.launches += 1;
+  c.flops += flops;
+  c.bytes += bytes;
+  cudaEvent_t a = take_event(), b = take_event();
+  cudaEventRecord(a, s);
+  c.events.push_back({a, b});
+}
+
+ProfScope::~ProfScope() {
+  if (slot < 0 || !g_prof_on) return;
+  cudaEventRecord(g_prof[slot].events.back().second, stream);
+}
+
 }  // namespace ennx
 
 extern "C" {
+
+uint64_t ennx_b200_launch_count(void) { return ennx::g_launches.load(); }
+
+int32_t ennx_b200_profile_begin(void) {
+  for (auto& c : ennx::g_prof)
+    for (auto& e : c.events) { ennx::g_event_pool.push_back(e.first); ennx::g_event_pool.push_back(e.second); }
+  ennx::g_prof.clear();
+  ennx::g_prof_on = true;
+  return ENNX_B200_OK;
+}
+
+int32_t ennx_b200_profile_end(ennx_b200_profile_entry* out, int32_t max_entries, int32_t* num_entries) {
+  ennx::g_prof_on = false;
+  ENNX_CUDA(cudaDeviceSynchronize(), "profile sync");
+  int32_t n = 0;
+  for (auto& c : ennx::g_prof) {
+    double ms = 0;
+    for (auto& e : c.events) {
+      float t = 0;
+      if (cudaEventElapsedTime(&t, e.first, e.second) == cudaSuccess) ms += t;
+    }
+    if (out && n < max_entries) {
+      memset(&out[n], 0, sizeof(out[n]));
+      strncpy(out[n].name, c.name.c_str(), sizeof(out[n].name) - 1);
+      out[n].launches = c.launches;
+      out[n].total_ms = ms;
+      out[n].flops = c.flops;
+      out[n].bytes = c.bytes;
+    }
+    ++n;
+  }
+  if (num_entries) *num_entries = n;
+  return ENNX_B200_OK;
+}
 
 uint32_t ennx_b200_abi_version(void) { return ENNX_B200_ABI_VERSION; }
 

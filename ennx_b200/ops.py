@@ -72,3 +72,61 @@ def perturb_bf16(w: torch.Tensor, seed: int, pair: int, tensor: int, sigma: floa
 def device_status() -> None:
     """Synchronise and raise if any kernel recorded a bounded-wait timeout."""
     _abi.call("ennx_b200_device_status", _stream())
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out: torch.Tensor | None = None) -> torch.Tensor:
+    _check_dev(x, w)
+    out = torch.empty_like(x) if out is None else out
+    _abi.call("ennx_b200_rmsnorm_bf16", _ptr(x), _ptr(w), x.shape[0], x.shape[1], eps, _ptr(out), _stream())
+    return out
+
+
+def moe_route(x: torch.Tensor, w_router: torch.Tensor, top_k: int, with_logits: bool = False):
+    """Routing indices (bit-exact with the CPU oracle) and renormalised gates."""
+    _check_dev(x, w_router)
+    T, H = x.shape
+    E = w_router.shape[0]
+    idx = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+    gate = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
+    logits = torch.empty(T, E, dtype=torch.float32, device=x.device) if with_logits else None
+    _abi.call("ennx_b200_moe_route", _ptr(x), _ptr(w_router), T, H, E, top_k, _ptr(logits), _ptr(idx), _ptr(gate),
+              _stream())
+    return (idx, gate, logits) if with_logits else (idx, gate)
+
+
+def moe_layer(x: torch.Tensor, w_router: torch.Tensor, w_gate_up: torch.Tensor, w_down: torch.Tensor, top_k: int,
+              residual: torch.Tensor | None = None, return_routing: bool = False):
+    """y = (residual +) sum_r gate_r * W_d[e_r](silu(W_g[e_r] x) * W_u[e_r] x)."""
+    _check_dev(x, w_router, w_gate_up, w_down, residual)
+    T, H = x.shape
+    E, I2, _ = w_gate_up.shape
+    I = I2 // 2
+    y = torch.empty_like(x)
+    idx = torch.empty(T, top_k, dtype=torch.int32, device=x.device)
+    gate = torch.empty(T, top_k, dtype=torch.float32, device=x.device)
+    nbytes = _abi.lib().ennx_b200_moe_workspace_size(T, H, E, top_k, I)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=x.device)
+    _abi.call("ennx_b200_moe_layer", _ptr(x), _ptr(w_router), _ptr(w_gate_up), _ptr(w_down), T, H, E, top_k, I,
+              _ptr(residual), _ptr(y), _ptr(idx), _ptr(gate), _ptr(ws), nbytes, _stream())
+    return (y, idx, gate) if return_routing else y
+
+
+def gqa_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, rope_theta: float = 1e6) -> torch.Tensor:
+    """Causal GQA attention; q [B,S,Hq,128], k/v [B,S,Hkv,128] bf16.  q and k are
+    rotated in place when rope_theta > 0."""
+    _check_dev(q, k, v)
+    B, S, Hq, D = q.shape
+    o = torch.empty_like(q)
+    _abi.call("ennx_b200_gqa_attention", _ptr(q), _ptr(k), _ptr(v), _ptr(o), B, S, Hq, k.shape[2], rope_theta,
+              _stream())
+    return o
+
+
+def kda_chunked(q, k, v, g, beta, state: torch.Tensor | None = None) -> torch.Tensor:
+    """Chunked KDA; q,k,v bf16 [B,T,H,128], g f32 [B,T,H,128], beta f32 [B,T,H]."""
+    _check_dev(q, k, v, g, beta, state)
+    B, T, H, D = q.shape
+    o = torch.empty_like(v)
+    _abi.call("ennx_b200_kda_chunked", _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state), _ptr(o), B, T, H,
+              _stream())
+    return o

@@ -157,6 +157,138 @@ typedef struct {
 ENNX_B200_API int32_t ennx_b200_gemm_bf16(const ennx_b200_gemm_params* params, const uint16_t* a,
                             const uint16_t* b, void* c, void* stream);
 
+/* ---- forward-path operators (no reference counterpart unless cited) ---- */
+
+/* out = x * rsqrt(mean(x^2) + eps) * w per row; x/out bf16 [rows, width],
+ * w bf16 [width]; width % 256 == 0.  Restates decoder_rms_norm
+ * (rust/crates/ennx/src/kda_moe.metal:536-554). */
+ENNX_B200_API int32_t ennx_b200_rmsnorm_bf16(const uint16_t* x, const uint16_t* w, int64_t rows, int32_t width,
+                                             float eps, uint16_t* out, void* stream);
+
+/* Router logits (fp32, fixed reduction order, bit-identical to the CPU
+ * oracle), top-k with strict '>' (ties keep the lower expert index) and
+ * softmax over the kept logits.  Replaces moe_router_topk
+ * (kda_moe.metal:570-621); top_k <= 8 as KdaMoeLayerRequest::validate
+ * (forward_program.rs:428).  x bf16 [tokens, hidden], w_router bf16
+ * [experts, hidden], hidden in {256, 512, 1024, 2048, 4096}, experts <= 256.
+ * logits (nullable) f32 [tokens, experts]; index i32 / gate f32 [tokens, top_k]. */
+ENNX_B200_API int32_t ennx_b200_moe_route(const uint16_t* x, const uint16_t* w_router, int64_t tokens,
+                                          int32_t hidden, int32_t experts, int32_t top_k, float* logits,
+                                          int32_t* index, float* gate, void* stream);
+
+/* Full MoE layer y = sum_r gate_r * W_d[e_r] (silu(W_g[e_r] x) * W_u[e_r] x):
+ * router + expert-major permutation + grouped tcgen05 gate/up GEMM with a
+ * SwiGLU epilogue + grouped down GEMM + weighted combine (+ residual).
+ * Restates moe_gate_up / moe_down (kda_moe.metal:691-755).
+ * w_gate_up bf16 [experts, 2*I, hidden] in blocks of 256 rows =
+ * [128 gate rows | 128 up rows]; w_down bf16 [experts, hidden, I]; I % 128 == 0.
+ * residual (nullable) is added to y.  index/gate outputs (nullable) receive the
+ * routing.  workspace >= ennx_b200_moe_workspace_size(tokens, hidden, experts,
+ * top_k, I) bytes of device memory. */
+ENNX_B200_API size_t ennx_b200_moe_workspace_size(int64_t tokens, int32_t hidden, int32_t experts, int32_t top_k,
+                                                  int32_t expert_width);
+ENNX_B200_API int32_t ennx_b200_moe_layer(const uint16_t* x, const uint16_t* w_router, const uint16_t* w_gate_up,
+                                          const uint16_t* w_down, int64_t tokens, int32_t hidden, int32_t experts,
+                                          int32_t top_k, int32_t expert_width, const uint16_t* residual,
+                                          uint16_t* y, int32_t* index, float* gate, void* workspace,
+                                          size_t workspace_bytes, void* stream);
+
+/* Causal GQA attention, head_dim 128, softmax scale 1/sqrt(128), fp32
+ * softmax statistics.  q bf16 [batch, seq, hq, 128], k/v [batch, seq, hkv,
+ * 128], o [batch, seq, hq, 128].  If rope_theta > 0, rotary embedding
+ * (rotate-half pairing, position = sequence index) is applied to q and k IN
+ * PLACE first. */
+ENNX_B200_API int32_t ennx_b200_gqa_attention(uint16_t* q, uint16_t* k, const uint16_t* v, uint16_t* o,
+                                              int32_t batch, int32_t seq, int32_t hq, int32_t hkv,
+                                              float rope_theta, void* stream);
+
+/* Chunked KDA (gated delta rule, per-key-channel decay, chunk 64, d_k = d_v =
+ * 128), equivalent to the serial recurrence of kda_recurrence_16k
+ * (kda_moe.metal:167-225).  q, k, v bf16 [batch, seq, heads, 128]; g f32
+ * [batch, seq, heads, 128] (log decay per step); beta f32 [batch, seq, heads];
+ * state f32 [batch, heads, 128, 128] (nullable: zero initial state, final
+ * state discarded; otherwise read as the initial state and overwritten with
+ * the final state); o bf16 [batch, seq, heads, 128], scaled by 1/sqrt(128). */
+ENNX_B200_API int32_t ennx_b200_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
+                                            const float* beta, float* state, uint16_t* o, int32_t batch,
+                                            int32_t seq, int32_t heads, void* stream);
+
+/* ---- population forward: the hybrid KDA/GQA-MoE decoder --------------- */
+
+typedef struct {
+    int32_t layers, hidden, vocab;
+    int32_t attn_period;   /* layer l is GQA iff l % attn_period == attn_period - 1 (0: no GQA) */
+    int32_t q_heads, kv_heads;       /* GQA, head_dim 128 */
+    int32_t kda_heads, gate_rank;    /* KDA, head_dim 128 */
+    int32_t experts, top_k, expert_width;
+    float rms_eps, rope_theta;
+} ennx_b200_model_config;
+
+/* Device pointers, bf16.  KDA layers use every field; GQA layers use
+ * attn_norm, w_qkv, w_o and the MoE fields. */
+typedef struct {
+    const uint16_t* attn_norm;   /* [H] */
+    const uint16_t* w_qkv;       /* KDA [3*Hk*128, H]; GQA [(Hq + 2*Hkv)*128, H] */
+    const uint16_t* w_ctl;       /* KDA [2*rank + Hk, H] = forget state | output state | beta,
+                                    the control layout of kda_split_control_16k (kda_moe.metal:847-867) */
+    const uint16_t* w_forget;    /* KDA [Hk*128, rank] */
+    const uint16_t* w_ogate;     /* KDA [Hk*128, rank] */
+    const uint16_t* decay;       /* KDA [Hk] */
+    const uint16_t* time_bias;   /* KDA [Hk*128] */
+    const uint16_t* out_norm;    /* KDA [128] */
+    const uint16_t* w_o;         /* [H, heads*128] */
+    const uint16_t* moe_norm;    /* [H] */
+    const uint16_t* w_router;    /* [E, H] */
+    const uint16_t* w_gate_up;   /* [E, 2*I, H], blocks of [128 gate | 128 up] rows */
+    const uint16_t* w_down;      /* [E, H, I] */
+} ennx_b200_layer_weights;
+
+typedef struct {
+    const uint16_t* embedding;   /* [V, H]; also the (tied) LM head */
+    const uint16_t* final_norm;  /* [H] */
+    const ennx_b200_layer_weights* layers; /* host array [layers] */
+} ennx_b200_model_weights;
+
+/* Evaluates antithetic pairs [first_pair, first_pair + num_pairs) of a
+ * zeroth-order population: candidate 2p+0 uses W + sigma*eps_p, 2p+1 uses
+ * W - sigma*eps_p (every weight tensor t, eps = Philox normal of (seed, p, t,
+ * element), tensor ids: embedding 0, final_norm 1, field f of layer l
+ * 16 + 16*l + f).  Each candidate is scored by the mean next-token
+ * cross-entropy on tokens (device int32 [batch, seq + 1]: inputs [:, :seq],
+ * targets [:, 1:]).  fitness (device f32 [2*num_pairs]) receives candidate
+ * 2i+s of the range at index 2i+s.  This is the ForwardEvaluator seam of
+ * the reference (forward_program.rs:210-212) for a whole population.
+ * workspace >= ennx_b200_population_workspace_size(cfg, batch, seq). */
+ENNX_B200_API size_t ennx_b200_population_workspace_size(const ennx_b200_model_config* cfg, int32_t batch,
+                                                         int32_t seq);
+ENNX_B200_API int32_t ennx_b200_population_forward(const ennx_b200_model_config* cfg,
+                                                   const ennx_b200_model_weights* weights, uint64_t seed,
+                                                   float sigma, int32_t first_pair, int32_t num_pairs,
+                                                   const int32_t* tokens, int32_t batch, int32_t seq,
+                                                   float* fitness, void* workspace, size_t workspace_bytes,
+                                                   void* stream);
+
+/* ---- measurement (CUDA-event timing per kernel class, the counterpart of
+ *      the reference's AskProfile / ENNX_CUDA_PROFILE, cuda/src/lib.rs:165-171,
+ *      977-1005) --------------------------------------------------------- */
+
+typedef struct {
+    char name[32];
+    int64_t launches;
+    double total_ms;   /* sum of CUDA-event durations on the launching stream */
+    double flops;      /* algorithmic FLOPs of the timed launches */
+    double bytes;      /* algorithmic HBM bytes of the timed launches */
+} ennx_b200_profile_entry;
+
+/* Start recording CUDA events around every launch of the population forward
+ * (and the operators it uses) on the calling thread's device. */
+ENNX_B200_API int32_t ennx_b200_profile_begin(void);
+/* Synchronise, stop recording and return one entry per kernel class. */
+ENNX_B200_API int32_t ennx_b200_profile_end(ennx_b200_profile_entry* out, int32_t max_entries,
+                                            int32_t* num_entries);
+/* Number of kernels this library has launched in this process. */
+ENNX_B200_API uint64_t ennx_b200_launch_count(void);
+
 #ifdef __cplusplus
 }
 #endif

@@ -96,9 +96,17 @@ class ClockSampler:
                 "samples": len(rows), "power_w_max": max(float(r[3]) for r in rows)}
 
 
-def cpu_reference_sample(reps: int = 1) -> dict:
-    """Bounded CPU sample of the reference path (oracle port), extrapolated to
-    tokens/s of the full model.  Returns value/unit/cores/sample."""
+def cpu_reference_sample() -> dict:
+    """Bounded CPU sample of the reference path (oracle port) on all host cores,
+    extrapolated to tokens/s of the full workload.
+
+    Per candidate the CPU path must (1) materialise W + sigma*eps for all 7.95 G
+    parameters and (2) run 4096 tokens through 24 layers + the LM head.  (1) is
+    timed on a 16 M-element slice split over all cores (the C oracle releases
+    the GIL), (2) on 64 tokens through one KDA+MoE layer, one GQA+MoE layer and
+    the head (float64 BLAS GEMMs on all cores), then both are scaled."""
+    import concurrent.futures as cf
+
     import numpy as np
 
     import oracle as O
@@ -106,13 +114,23 @@ def cpu_reference_sample(reps: int = 1) -> dict:
     from ennx_b200.model import HybridConfig
 
     cfg = HybridConfig()
-    tokens_n = 64
+    cores = os.cpu_count() or 1
     rng = np.random.default_rng(0)
 
     def w(*shape):
-        return O.to_bf16_bits((rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)))
+        return O.to_bf16_bits(rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02))
 
-    H, I, E = cfg.hidden, cfg.expert_width, cfg.experts
+    # (1) perturbation throughput
+    n_slice = 1 << 23
+    base = w(n_slice)
+    chunks = np.array_split(np.arange(n_slice), cores)
+    t0 = time.perf_counter()
+    with cf.ThreadPoolExecutor(cores) as ex:
+        list(ex.map(lambda idx: O.perturb_bf16(base[idx[0]:idx[-1] + 1], 7, 0, 3, SIGMA, +1), chunks))
+    t_perturb = (time.perf_counter() - t0) * cfg.param_count() / n_slice
+
+    # (2) forward per token
+    tokens_n = 64
     tok = rng.integers(0, cfg.vocab, (1, tokens_n + 1)).astype(np.int32)
 
     def one_layer_model(gqa: bool):
@@ -127,33 +145,30 @@ def cpu_reference_sample(reps: int = 1) -> dict:
                 layer[name] = w(*shp)
         return c, layer
 
-    emb = w(cfg.vocab, H)
-    fnorm = O.to_bf16_bits(np.ones(H, np.float32))
+    emb = w(cfg.vocab, cfg.hidden)
+    fnorm = O.to_bf16_bits(np.ones(cfg.hidden, np.float32))
     times = {}
     for kind in ("kda", "gqa"):
         c, layer = one_layer_model(kind == "gqa")
-        model = {"embedding": emb, "final_norm": fnorm, "layers": [layer]}
-        best = None
-        for _ in range(reps):
-            t0 = time.perf_counter()
-            OF.candidate_loss(c, model, tok, 1, SIGMA, 0, +1)
-            dt = time.perf_counter() - t0
-            best = dt if best is None else min(best, dt)
-        times[kind] = best
-    # isolate the LM head + embedding perturbation: a 0-layer pass
-    c0 = HybridConfig(layers=0)
+        t0 = time.perf_counter()
+        OF.candidate_loss(c, {"embedding": emb, "final_norm": fnorm, "layers": [layer]}, tok, 1, None, 0, +1)
+        times[kind] = time.perf_counter() - t0
     t0 = time.perf_counter()
-    OF.candidate_loss(c0, {"embedding": emb, "final_norm": fnorm, "layers": []}, tok, 1, SIGMA, 0, +1)
+    OF.candidate_loss(HybridConfig(layers=0), {"embedding": emb, "final_norm": fnorm, "layers": []}, tok, 1, None,
+                      0, +1)
     t_head = time.perf_counter() - t0
     n_kda = sum(1 for l in range(cfg.layers) if not cfg.is_gqa(l))
     n_gqa = cfg.layers - n_kda
-    per_candidate = n_kda * (times["kda"] - t_head) + n_gqa * (times["gqa"] - t_head) + t_head
-    tps = tokens_n / per_candidate
-    return {"value": tps, "unit": "tokens/s", "cores": os.cpu_count(), "kind": "port",
-            "sample": (f"1 candidate x {tokens_n} tokens through 1 KDA+MoE layer ({times['kda']:.2f}s) and 1 "
-                       f"GQA+MoE layer ({times['gqa']:.2f}s) incl. LM head ({t_head:.2f}s), extrapolated to "
-                       f"{n_kda} KDA + {n_gqa} GQA layers; oracle C + float64 numpy GEMMs, "
-                       f"weight perturbation included")}
+    t_fwd_sample = n_kda * (times["kda"] - t_head) + n_gqa * (times["gqa"] - t_head) + t_head
+    tokens_per_candidate = BATCH * SEQ
+    per_candidate = t_perturb + t_fwd_sample * tokens_per_candidate / tokens_n
+    return {"value": tokens_per_candidate / per_candidate, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "sample": (f"perturbation timed on {n_slice} elements over {cores} threads "
+                       f"(-> {t_perturb:.1f}s per candidate for {cfg.param_count() / 1e9:.2f}G params); forward "
+                       f"timed on 1 candidate x {tokens_n} tokens through 1 KDA+MoE layer ({times['kda']:.2f}s), "
+                       f"1 GQA+MoE layer ({times['gqa']:.2f}s) and the LM head ({t_head:.2f}s), scaled to "
+                       f"{n_kda} KDA + {n_gqa} GQA layers and {tokens_per_candidate} tokens; oracle C + float64 "
+                       f"numpy BLAS")}
 
 
 def run_reference(args):
@@ -315,8 +330,71 @@ def run_ours(args):
     _ = ennx_b200
 
 
+def run_op(args):
+    """Single-operator configs of BASELINE.json (configs[0..3]) on one GPU, for
+    profiling and per-kernel roofline numbers; not the headline line."""
+    import torch
+
+    from ennx_b200 import _abi, ops
+    from ennx_b200.model import gate_up_interleave
+
+    torch.cuda.set_device(0)
+    g = torch.Generator(device="cuda").manual_seed(0)
+
+    def rn(*shape, std=1.0):
+        return (torch.randn(*shape, generator=g, device="cuda") * std).to(torch.bfloat16)
+
+    if args.op == "gemm":
+        M = N = K = 2048
+        a, b = rn(M, K), rn(N, K)
+        c = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+        fn = lambda: ops.gemm(a, b, out=c)  # noqa: E731
+        flops, nbytes, unit_name = 2.0 * M * N * K, 2.0 * (M * K + N * K + M * N), "gemm 2048^3"
+    elif args.op == "attention":
+        B, S, Hq, Hkv = 8, 2048, 16, 4
+        q, k, v = rn(B, S, Hq, 128), rn(B, S, Hkv, 128), rn(B, S, Hkv, 128)
+        fn = lambda: ops.gqa_attention(q, k, v, 0.0)  # noqa: E731  (RoPE timed separately in the forward)
+        flops, nbytes, unit_name = 4.0 * B * Hq * S * S / 2 * 128, 2.0 * (2 * q.numel() + k.numel() + v.numel()), \
+            "causal GQA 8x2048x16/4x128"
+    elif args.op == "moe":
+        T, H, E, I, topk = 16384, 2048, 64, 768, 8
+        x, wr = rn(T, H), rn(E, H, std=0.02)
+        wgu = gate_up_interleave(rn(E, I, H, std=0.02), rn(E, I, H, std=0.02))
+        wd = rn(E, H, I, std=0.02)
+        fn = lambda: ops.moe_layer(x, wr, wgu, wd, topk)  # noqa: E731
+        flops = 2.0 * T * H * E + 2.0 * T * topk * 3 * H * I
+        nbytes, unit_name = 2.0 * (wgu.numel() + wd.numel() + 2 * T * H), "MoE 16384x2048, 64 experts top-8"
+    else:  # kda
+        B, T, H = 8, 4096, 16
+        q = torch.nn.functional.normalize(torch.randn(B, T, H, 128, generator=g, device="cuda"), dim=-1).bfloat16()
+        k = torch.nn.functional.normalize(torch.randn(B, T, H, 128, generator=g, device="cuda"), dim=-1).bfloat16()
+        v = rn(B, T, H, 128)
+        gl = -5.0 * torch.rand(B, T, H, 128, generator=g, device="cuda") / 64.0
+        beta = torch.sigmoid(torch.randn(B, T, H, generator=g, device="cuda"))
+        fn = lambda: ops.kda_chunked(q, k, v, gl, beta)  # noqa: E731
+        flops = 6.0 * 128 * 128 * B * T * H
+        nbytes, unit_name = 3 * 2.0 * q.numel() + 4.0 * gl.numel() + 4.0 * beta.numel() + 2.0 * v.numel(), \
+            "KDA 8x4096x16x128 chunk 64"
+    for _ in range(args.warmup):
+        fn()
+    torch.cuda.synchronize()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(args.steps):
+        fn()
+    en.record()
+    torch.cuda.synchronize()
+    ms = st.elapsed_time(en) / args.steps
+    hbm, tf_burst, _, src = peaks()
+    print(json.dumps({"op": args.op, "workload": unit_name, "ms": ms, "tflops": flops / ms / 1e9,
+                      "gbs": nbytes / ms / 1e6, "frac_tensor": flops / ms / 1e9 / tf_burst,
+                      "frac_hbm": nbytes / ms / 1e6 / hbm, "peaks": src}), flush=True)
+    _ = _abi
+
+
 def main():
     ap = argparse.ArgumentParser()
+    ap.add_argument("--op", choices=["forward", "gemm", "attention", "moe", "kda"], default="forward")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
@@ -327,6 +405,8 @@ def main():
         print("note: fewer than 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
+    elif args.op != "forward":
+        run_op(args)
     else:
         run_ours(args)
 

@@ -183,14 +183,21 @@ __global__ void dense_linear_kernel(const float* __restrict__ x, const float* __
   }
 }
 
-// Population noise: 8 consecutive elements per thread (two Philox blocks),
-// 16-byte loads and stores.  W +/- sigma*eps with two fp32 roundings, RNE.
-__global__ void perturb_bf16_kernel(const uint16_t* __restrict__ w, uint64_t n, uint64_t seed, uint32_t pair,
-                                    uint32_t tensor, float sigma, uint16_t* __restrict__ plus,
-                                    uint16_t* __restrict__ minus) {
-  uint64_t groups = (n + 7) / 8;
-  for (uint64_t g = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; g < groups;
-       g += (uint64_t)gridDim.x * blockDim.x) {
+// Population noise: each thread owns 8 consecutive elements (two Philox
+// blocks) per step, 16-byte loads and stores; W +/- sigma*eps with two fp32
+// roundings, RNE.  Blocks cover a fixed 8192-element span and retire quickly,
+// so the block scheduler can interleave them with the compute stream's
+// kernels on the same SMs (this kernel runs on a low-priority stream).
+constexpr int kPerturbGroupsPerThread = 4;
+__global__ void __launch_bounds__(256) perturb_bf16_kernel(const uint16_t* __restrict__ w, uint64_t n, uint64_t seed,
+                                                           uint32_t pair, uint32_t tensor, float sigma,
+                                                           uint16_t* __restrict__ plus, uint16_t* __restrict__ minus) {
+  const uint64_t groups = (n + 7) / 8;
+  const uint64_t g0 = (uint64_t)blockIdx.x * (256 * kPerturbGroupsPerThread) + threadIdx.x;
+#pragma unroll
+  for (int it = 0; it < kPerturbGroupsPerThread; ++it) {
+    const uint64_t g = g0 + (uint64_t)it * 256;
+    if (g >= groups) return;
     uint64_t e0 = g * 8;
     float z[8];
     noise4(seed, pair, tensor, 2 * g, z);
@@ -212,9 +219,9 @@ __global__ void perturb_bf16_kernel(const uint16_t* __restrict__ w, uint64_t n, 
     } else {
       for (uint64_t e = e0; e < n; ++e) {
         float a = bf16_to_f32(w[e]);
-        float s = __fmul_rn(sigma, z[e - e0]);
-        plus[e] = f32_to_bf16_rne(__fadd_rn(a, s));
-        if (minus) minus[e] = f32_to_bf16_rne(__fsub_rn(a, s));
+        float sg = __fmul_rn(sigma, z[e - e0]);
+        plus[e] = f32_to_bf16_rne(__fadd_rn(a, sg));
+        if (minus) minus[e] = f32_to_bf16_rne(__fsub_rn(a, sg));
       }
     }
   }
@@ -379,7 +386,10 @@ int32_t ennx_b200_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint3
     return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16 buffers must be 16-byte aligned");
   if (!isfinite(sigma)) return set_error(ENNX_B200_INVALID_ARGUMENT, "sigma must be finite");
   uint64_t groups = (n + 7) / 8;
-  perturb_bf16_kernel<<<grid_for(groups, 256), 256, 0, s>>>(w, n, seed, pair, tensor, sigma, plus, minus);
+  uint64_t per_block = 256 * kPerturbGroupsPerThread;
+  uint64_t blocks = (groups + per_block - 1) / per_block;
+  if (blocks > 0x7fffffffull) return set_error(ENNX_B200_UNSUPPORTED, "perturb_bf16: tensor too large");
+  perturb_bf16_kernel<<<(unsigned)blocks, 256, 0, s>>>(w, n, seed, pair, tensor, sigma, plus, minus);
   ENNX_LAUNCH_CHECK("perturb_bf16 launch");
   return ENNX_B200_OK;
 }

@@ -163,13 +163,17 @@ Shapes layer_shapes(const ennx_b200_model_config& c, bool gqa) {
 size_t align_elems(long long n) { return (size_t)((n + 127) / 128 * 128); }  // 256-byte granules of bf16
 
 struct Work {
-  uint16_t *emb_scr;    // [2][V*H]
-  uint16_t *layer_scr;  // per-field [2][n] areas
+  const int* tokens;       // caller's [batch, seq + 1] token ids
+  uint16_t *emb_scr[2];    // two slots of [2][V*H] (plus, minus)
+  uint16_t *fnorm_scr[2];  // two slots of [2][H]
+  uint16_t *layer_scr[2];  // two slots of per-field [2][n] areas
   size_t field_off[F_COUNT];  // element offsets into layer_scr (for the plus copy; minus follows)
   uint16_t *hidden, *xn, *qkv, *ctl, *fg, *og, *o, *post;
   float *gate, *beta;
   int *inp, *tgt;
   float *lse, *tlogit, *row_loss;
+  void* kda_ws;
+  size_t kda_ws_bytes;
   MoeBuffers moe;
   size_t bytes;
 };
@@ -192,7 +196,10 @@ int32_t validate_config(const ennx_b200_model_config* c, int batch, int seq) {
 void carve_work(const ennx_b200_model_config& c, int batch, int seq, uint8_t* base, Work& w) {
   Carver cv{base, 0, 0, base == nullptr};
   const long long Tc = (long long)batch * seq, T = 2 * Tc, H = c.hidden;
-  w.emb_scr = cv.take<uint16_t>(2 * align_elems((long long)c.vocab * H));
+  for (int k = 0; k < 2; ++k) {
+    w.emb_scr[k] = cv.take<uint16_t>(2 * align_elems((long long)c.vocab * H));
+    w.fnorm_scr[k] = cv.take<uint16_t>(2 * align_elems(H));
+  }
   size_t per_field_max[F_COUNT] = {0};
   for (int g = 0; g < 2; ++g) {
     Shapes sh = layer_shapes(c, g == 1);
@@ -203,7 +210,7 @@ void carve_work(const ennx_b200_model_config& c, int batch, int seq, uint8_t* ba
   }
   size_t off = 0;
   for (int f = 0; f < F_COUNT; ++f) { w.field_off[f] = off; off += 2 * per_field_max[f]; }
-  w.layer_scr = cv.take<uint16_t>(off);
+  for (int k = 0; k < 2; ++k) w.layer_scr[k] = cv.take<uint16_t>(off);
   const long long qkv_cols = std::max(3LL * c.kda_heads, (long long)(c.q_heads + 2 * c.kv_heads)) * HD;
   const long long heads_max = std::max(c.kda_heads, c.q_heads);
   const long long ctl_cols = (2LL * c.gate_rank + c.kda_heads + 7) / 8 * 8;
@@ -224,6 +231,8 @@ void carve_work(const ennx_b200_model_config& c, int batch, int seq, uint8_t* ba
   w.tlogit = cv.take<float>(T);
   w.row_loss = cv.take<float>(T);
   carve_moe(cv, T, c.hidden, c.experts, c.top_k, c.expert_width, 2, w.moe);
+  w.kda_ws_bytes = kda_workspace_bytes(2 * batch, seq, std::max(c.kda_heads, 1));
+  w.kda_ws = cv.take<uint8_t>(w.kda_ws_bytes);
   w.bytes = cv.off;
 }
 
@@ -265,89 +274,187 @@ int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* b, long long n, 
   return gemm_bf16(&p, a, b, c, s);
 }
 
-int32_t run_pair(const ennx_b200_model_config& c, const ennx_b200_model_weights& W, uint64_t seed, float sigma,
-                 uint32_t pair, int batch, int seq, Work& w, float* fit, cudaStream_t s) {
-  const long long Tc = (long long)batch * seq, T = 2 * Tc, H = c.hidden, V = c.vocab;
-  const size_t vh = align_elems(V * H);
-  uint16_t* e_plus = w.emb_scr;
-  uint16_t* e_minus = w.emb_scr + vh;
-  ENNX_TRY(perturb_pair(W.embedding, V * H, seed, pair, 0, sigma, e_plus, e_minus, s));
-  ENNX_TRY(launch_embed(w.inp, e_plus, e_minus, Tc, T, (int)H, (int)V, w.hidden, s));
+// Per-device streams of the pipelined population forward: `compute` runs the
+// layers (highest priority), `noise` generates the next layer's perturbed
+// weights (lowest priority) into the other half of a double buffer, so the
+// HBM-streaming noise kernel fills the issue slots and bandwidth the tensor-
+// core GEMMs leave free.
+struct PipeStreams {
+  cudaStream_t compute = nullptr, noise = nullptr;
+  cudaEvent_t ev[8] = {};
+};
+PipeStreams g_pipe[64];
 
-  for (int l = 0; l < c.layers; ++l) {
-    const ennx_b200_layer_weights& L = W.layers[l];
-    const bool gqa = is_gqa(c, l);
-    Shapes sh = layer_shapes(c, gqa);
-    uint16_t* P[F_COUNT];
-    uint16_t* M[F_COUNT];
-    for (int f = 0; f < F_COUNT; ++f) {
-      long long n = sh.rows[f] * sh.cols[f];
-      P[f] = M[f] = nullptr;
-      if (n == 0) continue;
-      P[f] = w.layer_scr + w.field_off[f];
-      // minus copy directly after plus (GEMM operands: n % 64 == 0, so the
-      // B row-block stride between the two signs is exactly `rows`)
-      M[f] = P[f] + (n % 8 == 0 ? (size_t)n : align_elems(n));
-      ENNX_TRY(perturb_pair(field_ptr(L, f), n, seed, pair, 16 + 16 * l + f, sigma, P[f], M[f], s));
-    }
-    // ---- mixer ----
-    ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_ATTN_NORM], M[F_ATTN_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
-    const long long qkv_cols = sh.rows[F_QKV];
-    ENNX_TRY(gemm2(w.xn, H, P[F_QKV], qkv_cols, H, w.qkv, qkv_cols, T, nullptr, s));
-    if (gqa) {
-      const long long kd = (long long)c.q_heads * HD, vd = kd + (long long)c.kv_heads * HD;
-      ENNX_TRY(launch_rope(w.qkv, qkv_cols, c.q_heads, HD, T, seq, c.rope_theta, s));
-      ENNX_TRY(launch_rope(w.qkv + kd, qkv_cols, c.kv_heads, HD, T, seq, c.rope_theta, s));
-      {
-        ProfScope ps("attention", s, 2.0 * batch * c.q_heads * (double)seq * (seq + 1) * HD * 2.0,
-                     2.0 * T * (2.0 * kd + 2.0 * c.kv_heads * HD));
-        ENNX_TRY(launch_gqa_attention(w.qkv, qkv_cols, w.qkv + kd, qkv_cols, w.qkv + vd, qkv_cols, w.o, kd, 2 * batch,
-                                      seq, c.q_heads, c.kv_heads, s));
-      }
-      ENNX_TRY(gemm2(w.o, kd, P[F_WO], H, kd, w.hidden, H, T, w.hidden, s));
-    } else {
-      const long long hw = (long long)c.kda_heads * HD, r = c.gate_rank;
-      const long long ctl_cols = sh.rows[F_CTL];
-      const long long ldctl = (ctl_cols + 7) / 8 * 8;
-      ENNX_TRY(gemm2(w.xn, H, P[F_CTL], ctl_cols, H, w.ctl, ldctl, T, nullptr, s));
-      ENNX_TRY(gemm2(w.ctl, ldctl, P[F_FORGET], hw, r, w.fg, hw, T, nullptr, s));
-      ENNX_TRY(gemm2(w.ctl + r, ldctl, P[F_OGATE], hw, r, w.og, hw, T, nullptr, s));
-      ENNX_TRY(launch_kda_gate(w.fg, hw, w.ctl + 2 * r, ldctl, P[F_DECAY], M[F_DECAY], P[F_TB], M[F_TB], Tc, T,
-                               c.kda_heads, HD, w.gate, w.beta, s));
-      ENNX_TRY(launch_l2norm_heads(w.qkv, qkv_cols, c.kda_heads, T, s));
-      ENNX_TRY(launch_l2norm_heads(w.qkv + hw, qkv_cols, c.kda_heads, T, s));
-      {
-        ProfScope ps("kda", s, (double)T * c.kda_heads * (6.0 * HD * HD + 6.0 * 64 * HD),
-                     (double)T * c.kda_heads * HD * (2.0 * 4 + 4.0) + 4.0 * T * c.kda_heads);
-        ENNX_TRY(launch_kda_chunked(w.qkv, w.qkv + hw, w.qkv + 2 * hw, qkv_cols, w.gate, w.beta, nullptr, w.o, hw,
-                                    2 * batch, seq, c.kda_heads, s));
-      }
-      ENNX_TRY(launch_kda_post(w.o, w.og, hw, P[F_OUT_NORM], M[F_OUT_NORM], Tc, c.kda_heads, T, c.rms_eps, w.post, s));
-      ENNX_TRY(gemm2(w.post, hw, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s));
-    }
-    // ---- MoE ----
-    ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_MOE_NORM], M[F_MOE_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
-    ENNX_TRY(run_moe(w.xn, P[F_ROUTER], M[F_ROUTER], P[F_GATE_UP], P[F_DOWN], T, Tc, 2, (int)H, c.experts, c.top_k,
-                     c.expert_width, w.hidden, w.hidden, w.moe, s));
+int32_t pipe_streams(PipeStreams** out) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  PipeStreams& p = g_pipe[dev];
+  if (!p.compute) {
+    int least = 0, greatest = 0;
+    ENNX_CUDA(cudaDeviceGetStreamPriorityRange(&least, &greatest), "stream priorities");
+    ENNX_CUDA(cudaStreamCreateWithPriority(&p.compute, cudaStreamNonBlocking, greatest), "compute stream");
+    ENNX_CUDA(cudaStreamCreateWithPriority(&p.noise, cudaStreamNonBlocking, least), "noise stream");
+    for (auto& e : p.ev) ENNX_CUDA(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "pipe events");
   }
-  // ---- final norm + fused LM-head cross-entropy ----
-  uint16_t* fn = w.layer_scr + w.field_off[F_ATTN_NORM];  // reuse: final norm pair
-  ENNX_TRY(perturb_pair(W.final_norm, H, seed, pair, 1, sigma, fn, fn + H, s));
-  ENNX_TRY(launch_rmsnorm(w.hidden, H, fn, fn + H, Tc, w.xn, H, T, (int)H, c.rms_eps, s));
-  ennx_b200_gemm_params p;
-  memset(&p, 0, sizeof(p));
-  p.m = (int)T; p.n = (int)V; p.k = (int)H;
-  p.lda = H; p.ldb = H;
-  p.groups = 2; p.b_group_rows = (int)V;
-  p.epilogue = ENNX_B200_EPI_LSE; p.alpha = 1.0f;
-  p.targets = w.tgt; p.lse_partial = w.lse; p.target_logit = w.tlogit;
-  if (vh != (size_t)(V * H)) return set_error(ENNX_B200_UNSUPPORTED, "vocab*hidden must be a multiple of 128");
-  {
-    ProfScope ps("gemm", s, 2.0 * T * V * H, 2.0 * (T * H + 2.0 * V * H));
-    ENNX_TRY(gemm_bf16(&p, w.xn, e_plus, nullptr, s));
+  *out = &p;
+  return ENNX_B200_OK;
+}
+
+struct LayerPtrs {
+  uint16_t* P[F_COUNT];
+  uint16_t* M[F_COUNT];
+};
+
+LayerPtrs layer_ptrs(const ennx_b200_model_config& c, int l, const Work& w, int slot) {
+  LayerPtrs lp;
+  Shapes sh = layer_shapes(c, is_gqa(c, l));
+  for (int f = 0; f < F_COUNT; ++f) {
+    long long n = sh.rows[f] * sh.cols[f];
+    lp.P[f] = lp.M[f] = nullptr;
+    if (n == 0) continue;
+    lp.P[f] = w.layer_scr[slot] + w.field_off[f];
+    // minus copy directly after plus (GEMM operands: n % 64 == 0, so the
+    // B row-block stride between the two signs is exactly `rows`)
+    lp.M[f] = lp.P[f] + (n % 8 == 0 ? (size_t)n : align_elems(n));
   }
-  ENNX_TRY(launch_lse_loss(w.lse, (int)((V + 255) / 256), w.tlogit, T, w.row_loss, s));
-  ENNX_TRY(launch_mean_per_set(w.row_loss, Tc, 2, fit, s));
+  return lp;
+}
+
+// noise stream: W +/- sigma*eps of every tensor of layer l into scratch `slot`
+int32_t perturb_layer(const ennx_b200_model_config& c, const ennx_b200_model_weights& W, int l, uint64_t seed,
+                      float sigma, uint32_t pair, const Work& w, int slot, cudaStream_t s) {
+  const ennx_b200_layer_weights& L = W.layers[l];
+  Shapes sh = layer_shapes(c, is_gqa(c, l));
+  LayerPtrs lp = layer_ptrs(c, l, w, slot);
+  for (int f = 0; f < F_COUNT; ++f) {
+    long long n = sh.rows[f] * sh.cols[f];
+    if (n == 0) continue;
+    ENNX_TRY(perturb_pair(field_ptr(L, f), n, seed, pair, 16 + 16 * l + f, sigma, lp.P[f], lp.M[f], s));
+  }
+  return ENNX_B200_OK;
+}
+
+// compute stream: one decoder layer for both candidates of a pair (T rows)
+int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& lp, int batch, int seq, Work& w,
+                      cudaStream_t s) {
+  const long long Tc = (long long)batch * seq, T = 2 * Tc, H = c.hidden;
+  const bool gqa = is_gqa(c, l);
+  Shapes sh = layer_shapes(c, gqa);
+  uint16_t* const* P = lp.P;
+  uint16_t* const* M = lp.M;
+  ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_ATTN_NORM], M[F_ATTN_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
+  const long long qkv_cols = sh.rows[F_QKV];
+  ENNX_TRY(gemm2(w.xn, H, P[F_QKV], qkv_cols, H, w.qkv, qkv_cols, T, nullptr, s));
+  if (gqa) {
+    const long long kd = (long long)c.q_heads * HD, vd = kd + (long long)c.kv_heads * HD;
+    ENNX_TRY(launch_rope(w.qkv, qkv_cols, c.q_heads, HD, T, seq, c.rope_theta, s));
+    ENNX_TRY(launch_rope(w.qkv + kd, qkv_cols, c.kv_heads, HD, T, seq, c.rope_theta, s));
+    {
+      ProfScope ps("attention", s, 2.0 * batch * c.q_heads * (double)seq * (seq + 1) * HD * 2.0,
+                   2.0 * T * (2.0 * kd + 2.0 * c.kv_heads * HD));
+      ENNX_TRY(launch_gqa_attention(w.qkv, qkv_cols, w.qkv + kd, qkv_cols, w.qkv + vd, qkv_cols, w.o, kd, 2 * batch,
+                                    seq, c.q_heads, c.kv_heads, s));
+    }
+    ENNX_TRY(gemm2(w.o, kd, P[F_WO], H, kd, w.hidden, H, T, w.hidden, s));
+  } else {
+    const long long hw = (long long)c.kda_heads * HD, r = c.gate_rank;
+    const long long ctl_cols = sh.rows[F_CTL];
+    const long long ldctl = (ctl_cols + 7) / 8 * 8;
+    ENNX_TRY(gemm2(w.xn, H, P[F_CTL], ctl_cols, H, w.ctl, ldctl, T, nullptr, s));
+    ENNX_TRY(gemm2(w.ctl, ldctl, P[F_FORGET], hw, r, w.fg, hw, T, nullptr, s));
+    ENNX_TRY(gemm2(w.ctl + r, ldctl, P[F_OGATE], hw, r, w.og, hw, T, nullptr, s));
+    ENNX_TRY(launch_kda_gate(w.fg, hw, w.ctl + 2 * r, ldctl, P[F_DECAY], M[F_DECAY], P[F_TB], M[F_TB], Tc, T,
+                             c.kda_heads, HD, w.gate, w.beta, s));
+    ENNX_TRY(launch_l2norm_heads(w.qkv, qkv_cols, c.kda_heads, T, s));
+    ENNX_TRY(launch_l2norm_heads(w.qkv + hw, qkv_cols, c.kda_heads, T, s));
+    {
+      ProfScope ps("kda", s, (double)T * c.kda_heads * (6.0 * HD * HD + 6.0 * 64 * HD),
+                   (double)T * c.kda_heads * HD * (2.0 * 4 + 4.0) + 4.0 * T * c.kda_heads);
+      ENNX_TRY(launch_kda_chunked(w.qkv, w.qkv + hw, w.qkv + 2 * hw, qkv_cols, w.gate, w.beta, nullptr, w.o, hw,
+                                  2 * batch, seq, c.kda_heads, w.kda_ws, w.kda_ws_bytes, s));
+    }
+    ENNX_TRY(launch_kda_post(w.o, w.og, hw, P[F_OUT_NORM], M[F_OUT_NORM], Tc, c.kda_heads, T, c.rms_eps, w.post, s));
+    ENNX_TRY(gemm2(w.post, hw, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s));
+  }
+  ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_MOE_NORM], M[F_MOE_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
+  ENNX_TRY(run_moe(w.xn, P[F_ROUTER], M[F_ROUTER], P[F_GATE_UP], P[F_DOWN], T, Tc, 2, (int)H, c.experts, c.top_k,
+                   c.expert_width, w.hidden, w.hidden, w.moe, s));
+  return ENNX_B200_OK;
+}
+
+// Pipelined population forward.  Job j = (pair i, layer l), j = i*L + l.
+// The noise stream perturbs job j+1 into layer slot (j+1)%2 while the compute
+// stream runs job j; a pair's embedding (= LM head) and final norm are
+// perturbed with its layer 0 into embedding slot i%2.
+int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_weights& W, uint64_t seed, float sigma,
+                       int first_pair, int num_pairs, int batch, int seq, Work& w, float* fitness,
+                       cudaStream_t caller) {
+  PipeStreams* ps = nullptr;
+  ENNX_TRY(pipe_streams(&ps));
+  cudaStream_t cs = ps->compute, ns = ps->noise;
+  cudaEvent_t ev_start = ps->ev[0], ev_done_noise = ps->ev[1];
+  cudaEvent_t ready[2] = {ps->ev[2], ps->ev[3]}, freed[2] = {ps->ev[4], ps->ev[5]};
+  cudaEvent_t emb_freed[2] = {ps->ev[6], ps->ev[7]};
+  const long long Tc = (long long)batch * seq, T = 2 * Tc, H = c.hidden, V = c.vocab;
+  const int L = c.layers;
+  const int jobs = num_pairs * L;
+
+  ENNX_CUDA(cudaEventRecord(ev_start, caller), "fork");
+  ENNX_CUDA(cudaStreamWaitEvent(cs, ev_start, 0), "fork compute");
+  ENNX_CUDA(cudaStreamWaitEvent(ns, ev_start, 0), "fork noise");
+  targets_kernel<<<(unsigned)((Tc + 255) / 256), 256, 0, cs>>>(w.tokens, batch, seq, w.inp, w.tgt);
+  ENNX_LAUNCH_CHECK("targets");
+
+  bool freed_recorded[2] = {false, false}, emb_freed_recorded[2] = {false, false};
+  auto noise_job = [&](int j) -> int32_t {
+    const int i = j / L, l = j % L, slot = j % 2;
+    const uint32_t pair = (uint32_t)(first_pair + i);
+    if (freed_recorded[slot]) ENNX_CUDA(cudaStreamWaitEvent(ns, freed[slot], 0), "wait slot");
+    if (l == 0) {
+      const int es = i % 2;
+      if (emb_freed_recorded[es]) ENNX_CUDA(cudaStreamWaitEvent(ns, emb_freed[es], 0), "wait emb slot");
+      ENNX_TRY(perturb_pair(W.embedding, V * H, seed, pair, 0, sigma, w.emb_scr[es], w.emb_scr[es] + V * H, ns));
+      ENNX_TRY(perturb_pair(W.final_norm, H, seed, pair, 1, sigma, w.fnorm_scr[es], w.fnorm_scr[es] + H, ns));
+    }
+    ENNX_TRY(perturb_layer(c, W, l, seed, sigma, pair, w, slot, ns));
+    ENNX_CUDA(cudaEventRecord(ready[slot], ns), "ready");
+    return ENNX_B200_OK;
+  };
+
+  ENNX_TRY(noise_job(0));
+  for (int j = 0; j < jobs; ++j) {
+    if (j + 1 < jobs) ENNX_TRY(noise_job(j + 1));
+    const int i = j / L, l = j % L, slot = j % 2, es = i % 2;
+    ENNX_CUDA(cudaStreamWaitEvent(cs, ready[slot], 0), "wait ready");
+    if (l == 0) ENNX_TRY(launch_embed(w.inp, w.emb_scr[es], w.emb_scr[es] + V * H, Tc, T, (int)H, (int)V, w.hidden, cs));
+    ENNX_TRY(compute_layer(c, l, layer_ptrs(c, l, w, slot), batch, seq, w, cs));
+    ENNX_CUDA(cudaEventRecord(freed[slot], cs), "freed");
+    freed_recorded[slot] = true;
+    if (l == L - 1) {
+      uint16_t* fn = w.fnorm_scr[es];
+      ENNX_TRY(launch_rmsnorm(w.hidden, H, fn, fn + H, Tc, w.xn, H, T, (int)H, c.rms_eps, cs));
+      ennx_b200_gemm_params p;
+      memset(&p, 0, sizeof(p));
+      p.m = (int)T; p.n = (int)V; p.k = (int)H;
+      p.lda = H; p.ldb = H;
+      p.groups = 2; p.b_group_rows = (int)V;
+      p.epilogue = ENNX_B200_EPI_LSE; p.alpha = 1.0f;
+      p.targets = w.tgt; p.lse_partial = w.lse; p.target_logit = w.tlogit;
+      {
+        ProfScope pf("gemm", cs, 2.0 * T * V * H, 2.0 * (T * H + 2.0 * V * H));
+        ENNX_TRY(gemm_bf16(&p, w.xn, w.emb_scr[es], nullptr, cs));
+      }
+      ENNX_CUDA(cudaEventRecord(emb_freed[es], cs), "emb freed");
+      emb_freed_recorded[es] = true;
+      ENNX_TRY(launch_lse_loss(w.lse, (int)((V + 255) / 256), w.tlogit, T, w.row_loss, cs));
+      ENNX_TRY(launch_mean_per_set(w.row_loss, Tc, 2, fitness + 2 * i, cs));
+    }
+  }
+  // join both streams back into the caller's stream
+  ENNX_CUDA(cudaEventRecord(ev_done_noise, ns), "join noise");
+  ENNX_CUDA(cudaStreamWaitEvent(cs, ev_done_noise, 0), "join noise into compute");
+  ENNX_CUDA(cudaEventRecord(ev_start, cs), "join compute");
+  ENNX_CUDA(cudaStreamWaitEvent(caller, ev_start, 0), "join into caller");
   return ENNX_B200_OK;
 }
 
@@ -415,12 +522,17 @@ int32_t ennx_b200_gqa_attention(uint16_t* q, uint16_t* k, const uint16_t* v, uin
                               (long long)hq * HD, batch, seq, hq, hkv, s);
 }
 
+size_t ennx_b200_kda_workspace_size(int32_t batch, int32_t seq, int32_t heads) {
+  if (batch <= 0 || seq <= 0 || heads <= 0) return 0;
+  return kda_workspace_bytes(batch, seq, heads);
+}
+
 int32_t ennx_b200_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
                               const float* beta, float* state, uint16_t* o, int32_t batch, int32_t seq, int32_t heads,
-                              void* stream) {
+                              void* workspace, size_t workspace_bytes, void* stream) {
   if (!q || !k || !v || !g || !beta || !o) return set_error(ENNX_B200_INVALID_ARGUMENT, "kda: null argument");
   return launch_kda_chunked(q, k, v, (long long)heads * HD, g, beta, state, o, (long long)heads * HD, batch, seq,
-                            heads, (cudaStream_t)stream);
+                            heads, workspace, workspace_bytes, (cudaStream_t)stream);
 }
 
 size_t ennx_b200_population_workspace_size(const ennx_b200_model_config* cfg, int32_t batch, int32_t seq) {
@@ -444,11 +556,11 @@ int32_t ennx_b200_population_forward(const ennx_b200_model_config* cfg, const en
   if (!workspace || workspace_bytes < w.bytes)
     return set_error(ENNX_B200_INVALID_ARGUMENT, "population_forward: workspace of %zu bytes required", w.bytes);
   carve_work(*cfg, batch, seq, (uint8_t*)workspace, w);
-  cudaStream_t s = (cudaStream_t)stream;
-  targets_kernel<<<(batch * seq + 255) / 256, 256, 0, s>>>(tokens, batch, seq, w.inp, w.tgt);
-  ENNX_LAUNCH_CHECK("targets");
-  for (int i = 0; i < num_pairs; ++i)
-    ENNX_TRY(run_pair(*cfg, *weights, seed, sigma, (uint32_t)(first_pair + i), batch, seq, w, fitness + 2 * i, s));
+  w.tokens = tokens;
+  if ((size_t)cfg->vocab * cfg->hidden != align_elems((long long)cfg->vocab * cfg->hidden))
+    return set_error(ENNX_B200_UNSUPPORTED, "vocab*hidden must be a multiple of 128");
+  ENNX_TRY(run_population(*cfg, *weights, seed, sigma, first_pair, num_pairs, batch, seq, w, fitness,
+                          (cudaStream_t)stream));
   return ENNX_B200_OK;
 }
 

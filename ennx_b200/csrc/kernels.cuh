@@ -47,9 +47,10 @@ int32_t launch_mean_per_set(const float* row_loss, long long rows_per_set, int s
 int32_t launch_gqa_attention(const uint16_t* q, long long ldq, const uint16_t* k, long long ldk, const uint16_t* v,
                              long long ldv, uint16_t* o, long long ldo, int batch, int seq, int hq, int hkv,
                              cudaStream_t s);
+size_t kda_workspace_bytes(int batch, int seq, int heads);
 int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, long long ld_qkv,
                            const float* g, const float* beta, float* state, uint16_t* o, long long ldo, int batch,
-                           int seq, int heads, cudaStream_t s);
+                           int seq, int heads, void* workspace, size_t workspace_bytes, cudaStream_t s);
 
 // gemm.cu (internal form of ennx_b200_gemm_bf16)
 int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* a, const uint16_t* b, void* c, cudaStream_t s);

@@ -14,75 +14,145 @@
 
 namespace ennx {
 
+// Router: a block owns up to TPB consecutive tokens of one weight set and
+// walks the experts in chunks whose weights are staged in shared memory
+// (EC experts x H bf16 <= 32 KB), so W_r is read from L2 once per block
+// instead of once per token.  A warp handles one token at a time with x in
+// registers; the per-lane element ownership and the fma/butterfly order are
+// the fixed reduction order described above.
+constexpr int kRouterTPB = 32;
+constexpr int kRouterSmem = 32768;
+
 template <int NJ, int SLOTS>
-__global__ void router_topk_kernel(const uint16_t* __restrict__ x, long long ldx, const uint16_t* __restrict__ w0,
-                                   const uint16_t* __restrict__ w1, long long split, long long tokens, int experts,
-                                   int top_k, float* __restrict__ logits, int* __restrict__ idx,
-                                   float* __restrict__ gate) {
+__global__ void __launch_bounds__(256) router_topk_kernel(
+    const uint16_t* __restrict__ x, long long ldx, const uint16_t* __restrict__ w0, const uint16_t* __restrict__ w1,
+    long long split, long long tokens, int experts, int top_k, float* __restrict__ logits, int* __restrict__ idx,
+    float* __restrict__ gate) {
   constexpr int H = NJ * 256;
-  long long t = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (t >= tokens) return;
-  uint4 xs[NJ];
+  constexpr int EC = kRouterSmem / (H * 2);
+  constexpr int TPW = kRouterTPB / 8;  // tokens per warp
+  __shared__ __align__(16) uint16_t ws[EC * H];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long long nb0 = (split + kRouterTPB - 1) / kRouterTPB;
+  long long tb, te;
+  const uint16_t* w;
+  if ((long long)blockIdx.x < nb0) {
+    tb = (long long)blockIdx.x * kRouterTPB; te = min(split, tb + kRouterTPB); w = w0;
+  } else {
+    tb = split + ((long long)blockIdx.x - nb0) * kRouterTPB; te = min(tokens, tb + kRouterTPB); w = w1;
+  }
+  float mine[TPW][SLOTS];
 #pragma unroll
-  for (int j = 0; j < NJ; ++j) xs[j] = *reinterpret_cast<const uint4*>(x + t * ldx + 256 * j + 8 * lane);
-  const uint16_t* w = t < split ? w0 : w1;
-  float mine[SLOTS];
+  for (int tt = 0; tt < TPW; ++tt)
 #pragma unroll
-  for (int s = 0; s < SLOTS; ++s) mine[s] = -INFINITY;
+    for (int s = 0; s < SLOTS; ++s) mine[tt][s] = -INFINITY;
 
-  for (int e = 0; e < experts; ++e) {
-    const uint16_t* wr = w + (long long)e * H;
-    float p = 0.0f;
+  for (int e0 = 0; e0 < experts; e0 += EC) {
+    const int ne = min(EC, experts - e0);
+    __syncthreads();
+    for (int i = threadIdx.x; i < ne * H / 8; i += blockDim.x)
+      reinterpret_cast<uint4*>(ws)[i] = __ldg(reinterpret_cast<const uint4*>(w + (long long)e0 * H) + i);
+    __syncthreads();
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-      uint4 wv = __ldg(reinterpret_cast<const uint4*>(wr + 256 * j + 8 * lane));
-      uint32_t xw[4] = {xs[j].x, xs[j].y, xs[j].z, xs[j].w};
-      uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    for (int tt = 0; tt < TPW; ++tt) {
+      const long long t = tb + warp + 8 * tt;
+      if (t >= te) break;
+      uint4 xs[NJ];
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        p = __fmaf_rn(bf16_to_f32((uint16_t)(xw[h] & 0xffffu)), bf16_to_f32((uint16_t)(ww[h] & 0xffffu)), p);
-        p = __fmaf_rn(bf16_to_f32((uint16_t)(xw[h] >> 16)), bf16_to_f32((uint16_t)(ww[h] >> 16)), p);
+      for (int j = 0; j < NJ; ++j) xs[j] = *reinterpret_cast<const uint4*>(x + t * ldx + 256 * j + 8 * lane);
+      // four experts at a time: independent fma chains and butterflies give
+      // the warp instruction-level parallelism; each logit keeps its own
+      // fixed reduction order.
+      int el = 0;
+      for (; el + 4 <= ne; el += 4) {
+        float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          uint32_t xw[4] = {xs[j].x, xs[j].y, xs[j].z, xs[j].w};
+#pragma unroll
+          for (int g = 0; g < 4; ++g) {
+            uint4 wv = *reinterpret_cast<const uint4*>(ws + (el + g) * H + 256 * j + 8 * lane);
+            uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              p[g] = __fmaf_rn(bf16_to_f32((uint16_t)(xw[h] & 0xffffu)), bf16_to_f32((uint16_t)(ww[h] & 0xffffu)), p[g]);
+              p[g] = __fmaf_rn(bf16_to_f32((uint16_t)(xw[h] >> 16)), bf16_to_f32((uint16_t)(ww[h] >> 16)), p[g]);
+            }
+          }
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1)
+#pragma unroll
+          for (int g = 0; g < 4; ++g) p[g] = __fadd_rn(p[g], __shfl_xor_sync(0xffffffffu, p[g], o));
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          const int e = e0 + el + g;
+#pragma unroll
+          for (int s2 = 0; s2 < SLOTS; ++s2)
+            if (e >> 5 == s2 && lane == (e & 31)) mine[tt][s2] = p[g];
+          if (logits && lane == 0) logits[t * experts + e] = p[g];
+        }
+      }
+      for (; el < ne; ++el) {
+        const uint16_t* wr = ws + el * H;
+        float p = 0.0f;
+#pragma unroll
+        for (int j = 0; j < NJ; ++j) {
+          uint4 wv = *reinterpret_cast<const uint4*>(wr + 256 * j + 8 * lane);
+          uint32_t xw[4] = {xs[j].x, xs[j].y, xs[j].z, xs[j].w};
+          uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            p = __fmaf_rn(bf16_to_f32((uint16_t)(xw[h] & 0xffffu)), bf16_to_f32((uint16_t)(ww[h] & 0xffffu)), p);
+            p = __fmaf_rn(bf16_to_f32((uint16_t)(xw[h] >> 16)), bf16_to_f32((uint16_t)(ww[h] >> 16)), p);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, o));
+        const int e = e0 + el;
+#pragma unroll
+        for (int s2 = 0; s2 < SLOTS; ++s2)
+          if (e >> 5 == s2 && lane == (e & 31)) mine[tt][s2] = p;
+        if (logits && lane == 0) logits[t * experts + e] = p;
       }
     }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, o));
-#pragma unroll
-    for (int s = 0; s < SLOTS; ++s)
-      if (e >> 5 == s && lane == (e & 31)) mine[s] = p;
-    if (logits && lane == 0) logits[t * experts + e] = p;
   }
 
-  float val[8];
-  int ids[8];
-  unsigned used = 0;
-  for (int r = 0; r < top_k; ++r) {
-    float bv = -INFINITY;
-    int bi = 0x7fffffff;
 #pragma unroll
-    for (int s = 0; s < SLOTS; ++s) {
-      int e = s * 32 + lane;
-      if (e < experts && !(used >> s & 1u)) {
-        if (mine[s] > bv || (mine[s] == bv && e < bi)) { bv = mine[s]; bi = e; }
-      }
-    }
-#pragma unroll
-    for (int o = 16; o >= 1; o >>= 1) {
-      float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-    }
-    if (bi == 0x7fffffff) bi = 0;  // fewer finite logits than k: keep index 0 like the reference
-    val[r] = bv;
-    ids[r] = bi;
-    if ((bi & 31) == lane) used |= 1u << (bi >> 5);
-  }
-  if (lane == 0) {
-    float ex[8], den = 0.0f;
-    for (int r = 0; r < top_k; ++r) { ex[r] = expf(val[r] - val[0]); den += ex[r]; }
+  for (int tt = 0; tt < TPW; ++tt) {
+    const long long t = tb + warp + 8 * tt;
+    if (t >= te) break;
+    float val[8];
+    int ids[8];
+    unsigned used = 0;
     for (int r = 0; r < top_k; ++r) {
-      idx[t * top_k + r] = ids[r];
-      gate[t * top_k + r] = ex[r] / den;
+      float bv = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int s = 0; s < SLOTS; ++s) {
+        int e = s * 32 + lane;
+        if (e < experts && !(used >> s & 1u)) {
+          if (mine[tt][s] > bv || (mine[tt][s] == bv && e < bi)) { bv = mine[tt][s]; bi = e; }
+        }
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+      }
+      if (bi == 0x7fffffff) bi = 0;  // fewer finite logits than k: keep index 0 like the reference
+      val[r] = bv;
+      ids[r] = bi;
+      if ((bi & 31) == lane) used |= 1u << (bi >> 5);
+    }
+    if (lane == 0) {
+      float ex[8], den = 0.0f;
+      for (int r = 0; r < top_k; ++r) { ex[r] = expf(val[r] - val[0]); den += ex[r]; }
+      for (int r = 0; r < top_k; ++r) {
+        idx[t * top_k + r] = ids[r];
+        gate[t * top_k + r] = ex[r] / den;
+      }
     }
   }
 }
@@ -206,8 +276,9 @@ int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0,
     return set_error(ENNX_B200_INVALID_ARGUMENT, "router: operands must be 16-byte aligned");
   int slots = (experts + 31) / 32;
   slots = slots <= 1 ? 1 : slots <= 2 ? 2 : slots <= 4 ? 4 : 8;
-  dim3 g((unsigned)((tokens + 7) / 8)), b(256);
   if (!w1) { w1 = w0; split = tokens; }
+  long long blocks = (split + kRouterTPB - 1) / kRouterTPB + (tokens - split + kRouterTPB - 1) / kRouterTPB;
+  dim3 g((unsigned)blocks), b(256);
   switch (hidden) {
     case 256: launch_router_nj<1>(slots, g, b, s, x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;
     case 512: launch_router_nj<2>(slots, g, b, s, x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;

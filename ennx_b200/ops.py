@@ -127,6 +127,8 @@ def kda_chunked(q, k, v, g, beta, state: torch.Tensor | None = None) -> torch.Te
     _check_dev(q, k, v, g, beta, state)
     B, T, H, D = q.shape
     o = torch.empty_like(v)
+    nbytes = _abi.lib().ennx_b200_kda_workspace_size(B, T, H)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
     _abi.call("ennx_b200_kda_chunked", _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state), _ptr(o), B, T, H,
-              _stream())
+              _ptr(ws), nbytes, _stream())
     return o

@@ -208,10 +208,14 @@ ENNX_B200_API int32_t ennx_b200_gqa_attention(uint16_t* q, uint16_t* k, const ui
  * [batch, seq, heads, 128] (log decay per step); beta f32 [batch, seq, heads];
  * state f32 [batch, heads, 128, 128] (nullable: zero initial state, final
  * state discarded; otherwise read as the initial state and overwritten with
- * the final state); o bf16 [batch, seq, heads, 128], scaled by 1/sqrt(128). */
+ * the final state); o bf16 [batch, seq, heads, 128], scaled by 1/sqrt(128).
+ * workspace (device, 16-byte aligned) >= ennx_b200_kda_workspace_size(batch,
+ * seq, heads) bytes holds the per-chunk operands of the two-phase scheme. */
+ENNX_B200_API size_t ennx_b200_kda_workspace_size(int32_t batch, int32_t seq, int32_t heads);
 ENNX_B200_API int32_t ennx_b200_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, const float* g,
                                             const float* beta, float* state, uint16_t* o, int32_t batch,
-                                            int32_t seq, int32_t heads, void* stream);
+                                            int32_t seq, int32_t heads, void* workspace, size_t workspace_bytes,
+                                            void* stream);
 
 /* ---- population forward: the hybrid KDA/GQA-MoE decoder --------------- */
 

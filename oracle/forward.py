@@ -29,7 +29,10 @@ def _softplus(x):
     return np.maximum(x, 0) + np.log1p(np.exp(-np.abs(x)))
 
 
-def perturbed(bits: np.ndarray, seed: int, pair: int, tensor: int, sigma: float, sign: int) -> np.ndarray:
+def perturbed(bits: np.ndarray, seed: int, pair: int, tensor: int, sigma, sign: int) -> np.ndarray:
+    """bf16 bits -> float32 values of W + sign*sigma*eps (sigma None: W itself)."""
+    if sigma is None:
+        return from_bf16_bits(bits)
     return from_bf16_bits(perturb_bf16(bits.reshape(-1), seed, pair, tensor, sigma, sign)).reshape(bits.shape)
 
 

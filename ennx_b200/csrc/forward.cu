@@ -226,7 +226,7 @@ void carve_work(const ennx_b200_model_config& c, int batch, int seq, uint8_t* ba
   w.beta = cv.take<float>(T * c.kda_heads);
   w.inp = cv.take<int>(Tc);
   w.tgt = cv.take<int>(T);
-  const long long ntiles = (c.vocab + 255) / 256;
+  const long long ntiles = 2 * ((c.vocab + 255) / 256);  // LSE partials per row
   w.lse = cv.take<float>(T * ntiles * 2);
   w.tlogit = cv.take<float>(T);
   w.row_loss = cv.take<float>(T);
@@ -363,15 +363,18 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
     ENNX_TRY(gemm2(w.xn, H, P[F_CTL], ctl_cols, H, w.ctl, ldctl, T, nullptr, s));
     ENNX_TRY(gemm2(w.ctl, ldctl, P[F_FORGET], hw, r, w.fg, hw, T, nullptr, s));
     ENNX_TRY(gemm2(w.ctl + r, ldctl, P[F_OGATE], hw, r, w.og, hw, T, nullptr, s));
-    ENNX_TRY(launch_kda_gate(w.fg, hw, w.ctl + 2 * r, ldctl, P[F_DECAY], M[F_DECAY], P[F_TB], M[F_TB], Tc, T,
-                             c.kda_heads, HD, w.gate, w.beta, s));
-    ENNX_TRY(launch_l2norm_heads(w.qkv, qkv_cols, c.kda_heads, T, s));
-    ENNX_TRY(launch_l2norm_heads(w.qkv + hw, qkv_cols, c.kda_heads, T, s));
     {
+      KdaRawGate rg;
+      rg.f = w.fg; rg.ldf = hw;
+      rg.rbeta = w.ctl + 2 * r; rg.ldb = ldctl;
+      rg.decay0 = P[F_DECAY]; rg.decay1 = M[F_DECAY];
+      rg.tb0 = P[F_TB]; rg.tb1 = M[F_TB];
+      rg.split_seq = batch;
+      rg.active = 1;
       ProfScope ps("kda", s, (double)T * c.kda_heads * (6.0 * HD * HD + 6.0 * 64 * HD),
                    (double)T * c.kda_heads * HD * (2.0 * 4 + 4.0) + 4.0 * T * c.kda_heads);
-      ENNX_TRY(launch_kda_chunked(w.qkv, w.qkv + hw, w.qkv + 2 * hw, qkv_cols, w.gate, w.beta, nullptr, w.o, hw,
-                                  2 * batch, seq, c.kda_heads, w.kda_ws, w.kda_ws_bytes, s));
+      ENNX_TRY(launch_kda_chunked(w.qkv, w.qkv + hw, w.qkv + 2 * hw, qkv_cols, nullptr, nullptr, nullptr, w.o, hw,
+                                  2 * batch, seq, c.kda_heads, w.kda_ws, w.kda_ws_bytes, s, &rg));
     }
     ENNX_TRY(launch_kda_post(w.o, w.og, hw, P[F_OUT_NORM], M[F_OUT_NORM], Tc, c.kda_heads, T, c.rms_eps, w.post, s));
     ENNX_TRY(gemm2(w.post, hw, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s));
@@ -446,7 +449,7 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
       }
       ENNX_CUDA(cudaEventRecord(emb_freed[es], cs), "emb freed");
       emb_freed_recorded[es] = true;
-      ENNX_TRY(launch_lse_loss(w.lse, (int)((V + 255) / 256), w.tlogit, T, w.row_loss, cs));
+      ENNX_TRY(launch_lse_loss(w.lse, (int)(2 * ((V + 255) / 256)), w.tlogit, T, w.row_loss, cs));
       ENNX_TRY(launch_mean_per_set(w.row_loss, Tc, 2, fitness + 2 * i, cs));
     }
   }

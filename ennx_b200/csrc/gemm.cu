@@ -32,10 +32,12 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-constexpr int THREADS = 192;
+constexpr int EPI_WARPS = 8;                 // two warpgroups, each owns half of the tile's columns
+constexpr int THREADS = 64 + 32 * EPI_WARPS;  // producer warp, MMA warp, epilogue warps
+constexpr int EPI_BUF = 32 * 32 * 2;          // per-warp 32x32 bf16 staging tile for TMA stores
 constexpr int TMEM_COLS = 512;
 constexpr int MAX_GROUPS = 256;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 4096 /*barriers, tables*/;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_WARPS * EPI_BUF + 1024 /*align*/ + 4096 /*barriers, tables*/;
 constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN);
 
 struct Args {
@@ -53,6 +55,8 @@ struct Args {
   float2* lse;
   float* tlogit;
   int n_tiles;
+  int n_parts;  // LSE partials per row: 2 * ceil(N / 256) (one per 128-column half tile)
+  int has_tmc;  // C tensor map valid (bf16 outputs): full tiles leave through TMA stores
   int* err;
 };
 
@@ -89,11 +93,13 @@ __device__ __forceinline__ TileInfo decode_tile(const Smem& s, const Args& a, in
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Args a) {
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     const __grid_constant__ CUtensorMap tmC, Args a) {
   extern __shared__ uint8_t smem_raw[];
   uint32_t raw_addr = smem_u32(smem_raw);
   uint8_t* ring = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
-  Smem& s = *reinterpret_cast<Smem*>(ring + STAGES * STAGE_BYTES);
+  uint8_t* epi_smem = ring + STAGES * STAGE_BYTES;
+  Smem& s = *reinterpret_cast<Smem*>(epi_smem + EPI_WARPS * EPI_BUF);
   uint8_t* sA = ring;
   uint8_t* sB = ring + STAGES * A_BYTES;
 
@@ -101,7 +107,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < STAGES; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], 4); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], EPI_WARPS); }
     s.abort_flag = 0;
     // group table: row offsets (device table or uniform split) and tile prefix
     int tiles = 0;
@@ -119,7 +125,11 @@ __global__ void __launch_bounds__(THREADS, 1)
     fence_barrier_init();
     fence_proxy_async();
   }
-  if (warp == 0 && lane == 0) { tma_prefetch_desc(&tmA); tma_prefetch_desc(&tmB); }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    if (a.has_tmc) tma_prefetch_desc(&tmC);
+  }
   if (warp == 1) { tmem_alloc(&s.tmem_base, TMEM_COLS); tmem_relinquish(); }
   __syncthreads();
   tc_fence_after();
@@ -173,9 +183,16 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // epilogue warps 2..5; TMEM lane quarter = warp % 4
+    // Epilogue: warps 2..9.  Warp w reads TMEM lane quarter w % 4 (rows
+    // 32*(w%4) .. +31 of the tile); warpgroup h = (w-2)/4 owns columns
+    // [h*128, h*128 + 128).  Full tiles leave through per-warp 32x32 staging
+    // tiles and TMA stores; group-tail tiles use masked direct stores.
+    const int ew = warp - 2;
     const int q = warp & 3;
+    const int half = ew >> 2;
     const int r_in_tile = q * 32 + lane;
+    uint8_t* stg = epi_smem + ew * EPI_BUF;
+    const uint32_t stg_addr = smem_u32(stg);
     int it = 0;
     for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
       int acc = it & 1;
@@ -186,40 +203,63 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int mrow = t.mt * BM + r_in_tile;
       const bool row_ok = mrow < t.rows;
       const long long grow = (long long)t.row0 + mrow;
+      const int warp_row0 = t.row0 + t.mt * BM + q * 32;
+      const bool use_tma = a.has_tmc && (t.mt * BM + BM <= t.rows || t.row0 + t.rows == a.M);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       uint32_t v[32];
 
+      // 32 packed bf16 pairs (16 words) of this lane's row -> C[row, col0 .. col0+31]
+      auto store_bf16 = [&](const uint32_t (&pk)[16], int col0, int ncols) {
+        if (use_tma) {
+          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+          __syncwarp();
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            int jj = (j + (lane >> 1)) & 3;  // rotate the 16-byte chunks: fewer bank conflicts
+            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(stg_addr + lane * 64 + jj * 16),
+                         "r"(pk[4 * jj]), "r"(pk[4 * jj + 1]), "r"(pk[4 * jj + 2]), "r"(pk[4 * jj + 3])
+                         : "memory");
+          }
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            asm volatile(
+                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)&tmC),
+                "r"(stg_addr), "r"(col0), "r"(warp_row0)
+                : "memory");
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+          }
+        } else if (row_ok && col0 < ncols) {
+          uint16_t* dst = (uint16_t*)a.C + grow * a.ldc + col0;
+          if (col0 + 32 <= ncols) {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) st_global_v4(dst + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+          } else {
+            for (int j = 0; col0 + j < ncols; ++j) dst[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
+          }
+        }
+      };
+
       if (a.epi == ENNX_B200_EPI_SWIGLU) {
-        uint16_t* C = (uint16_t*)a.C;
-        for (int c = 0; c < BN / 2; c += 32) {
+        for (int c = half * 64; c < half * 64 + 64; c += 32) {
           uint32_t u[32];
           tmem_ld32(tbase + c, v);
           tmem_ld32(tbase + c + BN / 2, u);
           tmem_ld_wait();
-          int col0 = t.nt * (BN / 2) + c;
-          int ncols = a.N / 2;
-          if (row_ok) {
-            uint16_t* dst = C + grow * a.ldc + col0;
-            uint32_t pk[16];
+          uint32_t pk[16];
 #pragma unroll
-            for (int j = 0; j < 16; ++j) {
-              float g0 = __uint_as_float(v[2 * j]) * a.alpha, g1 = __uint_as_float(v[2 * j + 1]) * a.alpha;
-              float u0 = __uint_as_float(u[2 * j]) * a.alpha, u1 = __uint_as_float(u[2 * j + 1]) * a.alpha;
-              pk[j] = pack_bf16x2(silu(g0) * u0, silu(g1) * u1);
-            }
-            if (col0 + 32 <= ncols) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) st_global_v4(dst + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-            } else {
-              for (int j = 0; j < 32 && col0 + j < ncols; ++j) dst[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
-            }
+          for (int j = 0; j < 16; ++j) {
+            float g0 = __uint_as_float(v[2 * j]) * a.alpha, g1 = __uint_as_float(v[2 * j + 1]) * a.alpha;
+            float u0 = __uint_as_float(u[2 * j]) * a.alpha, u1 = __uint_as_float(u[2 * j + 1]) * a.alpha;
+            pk[j] = pack_bf16x2(silu(g0) * u0, silu(g1) * u1);
           }
+          store_bf16(pk, t.nt * (BN / 2) + c, a.N / 2);
         }
       } else if (a.epi == ENNX_B200_EPI_LSE) {
         float m = -INFINITY, ssum = 0.0f, tl = 0.0f;
         int tgt = row_ok ? a.targets[grow] : -1;
         bool have_t = false;
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = half * 128; c < half * 128 + 128; c += 32) {
           tmem_ld32(tbase + c, v);
           tmem_ld_wait();
           int col0 = t.nt * BN + c;
@@ -227,8 +267,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             float x = __uint_as_float(v[j]) * a.alpha;
-            bool ok = col0 + j < a.N;
-            if (ok) cm = fmaxf(cm, x);
+            if (col0 + j < a.N) cm = fmaxf(cm, x);
             if (col0 + j == tgt) { tl = x; have_t = true; }
           }
           if (cm > -INFINITY) {
@@ -242,18 +281,18 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
         }
         if (row_ok) {
-          a.lse[grow * a.n_tiles + t.nt] = make_float2(m, ssum);
+          a.lse[grow * a.n_parts + t.nt * 2 + half] = make_float2(m, ssum);
           if (have_t) a.tlogit[grow] = tl;
         }
       } else {
         const float rs = (a.epi == ENNX_B200_EPI_ROWSCALE && row_ok) ? a.row_scale[grow] : a.alpha;
-        for (int c = 0; c < BN; c += 32) {
+        for (int c = half * 128; c < half * 128 + 128; c += 32) {
           tmem_ld32(tbase + c, v);
           tmem_ld_wait();
           int col0 = t.nt * BN + c;
-          if (!row_ok || col0 >= a.N) continue;
           bool full = col0 + 32 <= a.N;
           if (a.epi == ENNX_B200_EPI_F32) {
+            if (!row_ok || col0 >= a.N) continue;
             float* dst = (float*)a.C + grow * a.ldc + col0;
             if (full) {
 #pragma unroll
@@ -266,43 +305,41 @@ __global__ void __launch_bounds__(THREADS, 1)
             } else {
               for (int j = 0; col0 + j < a.N; ++j) dst[j] = __uint_as_float(v[j]) * rs;
             }
-          } else {
-            uint16_t* dst = (uint16_t*)a.C + grow * a.ldc + col0;
-            float x[32];
+            continue;
+          }
+          if (use_tma && col0 >= a.N) continue;  // warp-uniform: whole chunk outside C
+          float x[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(v[j]) * rs;
-            if (a.R) {
-              const uint16_t* rp = a.R + grow * a.ldr + col0;
-              if (full) {
-#pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  uint4 rv = *reinterpret_cast<const uint4*>(rp + 8 * j);
-                  uint32_t w4[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-                  for (int h = 0; h < 4; ++h) {
-                    x[8 * j + 2 * h] += bf16_to_f32((uint16_t)(w4[h] & 0xffffu));
-                    x[8 * j + 2 * h + 1] += bf16_to_f32((uint16_t)(w4[h] >> 16));
-                  }
-                }
-              } else {
-                for (int j = 0; col0 + j < a.N; ++j) x[j] += bf16_to_f32(rp[j]);
-              }
-            }
+          for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(v[j]) * rs;
+          if (a.R && row_ok && col0 < a.N) {
+            const uint16_t* rp = a.R + grow * a.ldr + col0;
             if (full) {
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
-                st_global_v4(dst + 8 * j, pack_bf16x2(x[8 * j], x[8 * j + 1]), pack_bf16x2(x[8 * j + 2], x[8 * j + 3]),
-                             pack_bf16x2(x[8 * j + 4], x[8 * j + 5]), pack_bf16x2(x[8 * j + 6], x[8 * j + 7]));
+              for (int j = 0; j < 4; ++j) {
+                uint4 rv = *reinterpret_cast<const uint4*>(rp + 8 * j);
+                uint32_t w4[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                  x[8 * j + 2 * h] += bf16_to_f32((uint16_t)(w4[h] & 0xffffu));
+                  x[8 * j + 2 * h + 1] += bf16_to_f32((uint16_t)(w4[h] >> 16));
+                }
+              }
             } else {
-              for (int j = 0; col0 + j < a.N; ++j) dst[j] = f32_to_bf16_rne(x[j]);
+              for (int j = 0; col0 + j < a.N; ++j) x[j] += bf16_to_f32(rp[j]);
             }
           }
+          uint32_t pk[16];
+#pragma unroll
+          for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(x[2 * j], x[2 * j + 1]);
+          store_bf16(pk, col0, a.N);
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s.tempty[acc]);
     }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
   }
 
   __syncthreads();
@@ -349,9 +386,15 @@ int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint1
     return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: residual must be 16-byte aligned with ldr %% 8 == 0");
 
   const long long b_rows = (long long)(G - 1) * p->b_group_rows + N;
-  CUtensorMap ta, tb;
-  ENNX_TRY(make_tmap_2d_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)p->lda, BK, BM));
-  ENNX_TRY(make_tmap_2d_bf16(&tb, B, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, BK, BN));
+  CUtensorMap ta, tb, tc;
+  ENNX_TRY(make_tmap_2d_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)p->lda, BK, BM, true));
+  ENNX_TRY(make_tmap_2d_bf16(&tb, B, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, BK, BN, true));
+  memset(&tc, 0, sizeof(tc));
+  const bool bf16_out = epi == ENNX_B200_EPI_BF16 || epi == ENNX_B200_EPI_SWIGLU || epi == ENNX_B200_EPI_ROWSCALE;
+  if (bf16_out) {
+    const long long out_cols = epi == ENNX_B200_EPI_SWIGLU ? N / 2 : N;
+    ENNX_TRY(make_tmap_2d_bf16(&tc, C, (uint64_t)out_cols, (uint64_t)M, (uint64_t)p->ldc, 32, 32, false));
+  }
 
   Args a;
   a.M = M; a.N = N; a.K = K;
@@ -368,6 +411,8 @@ int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint1
   a.lse = (float2*)p->lse_partial;
   a.tlogit = p->target_logit;
   a.n_tiles = (N + BN - 1) / BN;
+  a.n_parts = 2 * a.n_tiles;
+  a.has_tmc = bf16_out ? 1 : 0;
   a.err = device_error_word();
   if (!a.err) return set_error(ENNX_B200_CUDA_ERROR, "gemm: no device error word");
 
@@ -381,7 +426,7 @@ int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint1
   long long tiles_bound = ((long long)M / BM + G) * a.n_tiles;
   int grid = sm_count();
   if (tiles_bound < grid) grid = (int)tiles_bound;
-  gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, a);
+  gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, tc, a);
   ENNX_LAUNCH_CHECK("gemm launch");
   return ENNX_B200_OK;
 }

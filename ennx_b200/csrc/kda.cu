@@ -28,6 +28,8 @@
 #include "common.cuh"
 #include "kernels.cuh"
 
+#include <string.h>
+
 namespace ennx {
 namespace {
 
@@ -98,10 +100,12 @@ struct PrepSmem {
   uint16_t X[32][LQ], Y[C][LQ];
 };
 
+__device__ __forceinline__ float softplus_stable(float x) { return fmaxf(x, 0.0f) + log1pf(__expf(-fabsf(x))); }
+
 __global__ void __launch_bounds__(256) kda_prep_kernel(const uint16_t* __restrict__ qg, const uint16_t* __restrict__ kg,
                                                        long long ld, const float* __restrict__ gg, long long ldg,
                                                        const float* __restrict__ bg, int seq, int heads, int nchunks,
-                                                       uint8_t* __restrict__ ops) {
+                                                       KdaRawGate raw, uint8_t* __restrict__ ops) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   PrepSmem& s = *reinterpret_cast<PrepSmem*>(smem_raw);
   const int ch = blockIdx.x, bh = blockIdx.y, b = bh / heads, h = bh % heads;
@@ -125,13 +129,56 @@ __global__ void __launch_bounds__(256) kda_prep_kernel(const uint16_t* __restric
     *reinterpret_cast<uint4*>(&s.q[r][c]) = qv;
     *reinterpret_cast<uint4*>(&s.k[r][c]) = kv;
   }
-  for (int i = tid; i < C * (DK / 4); i += 256) {
-    int r = i / (DK / 4), c = (i % (DK / 4)) * 4;
-    float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
-    if (t0 + r < seq) gv = *reinterpret_cast<const float4*>(gg + (tok0 + t0 + r) * ldg + h * DK + c);
-    *reinterpret_cast<float4*>(&s.Gc[r][c]) = gv;
+  if (raw.active) {
+    // forward path: g = max(-exp(decay_h) * softplus(f + time_bias), -5) and
+    // beta = sigmoid(raw beta) from the raw projections (kda_moe.metal:869-895)
+    const bool set0 = b < raw.split_seq;
+    const uint16_t* tb = set0 ? raw.tb0 : raw.tb1;
+    const float dscale = __expf(bf16_to_f32((set0 ? raw.decay0 : raw.decay1)[h]));
+    for (int i = tid; i < C * (DK / 8); i += 256) {
+      int r = i / (DK / 8), c = (i % (DK / 8)) * 8;
+      float gv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (t0 + r < seq) {
+        uint4 fv = *reinterpret_cast<const uint4*>(raw.f + (tok0 + t0 + r) * raw.ldf + h * DK + c);
+        uint4 bv = *reinterpret_cast<const uint4*>(tb + h * DK + c);
+        uint32_t fw[4] = {fv.x, fv.y, fv.z, fv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float x = bf16_to_f32((uint16_t)(fw[j >> 1] >> (16 * (j & 1)))) +
+                    bf16_to_f32((uint16_t)(bw[j >> 1] >> (16 * (j & 1))));
+          gv[j] = fmaxf(-dscale * softplus_stable(x), -5.0f);
+        }
+      }
+      *reinterpret_cast<float4*>(&s.Gc[r][c]) = make_float4(gv[0], gv[1], gv[2], gv[3]);
+      *reinterpret_cast<float4*>(&s.Gc[r][c + 4]) = make_float4(gv[4], gv[5], gv[6], gv[7]);
+    }
+    if (tid < C)
+      s.beta[tid] = t0 + tid < seq
+                        ? 1.0f / (1.0f + __expf(-bf16_to_f32(raw.rbeta[(tok0 + t0 + tid) * raw.ldb + h])))
+                        : 0.0f;
+    __syncthreads();
+    // per-token L2 normalisation of q and k, 1/max(|x|, 1e-6) (kda_moe.metal:510-534)
+    for (int r = warp; r < 2 * C; r += 8) {
+      uint16_t* row = r < C ? &s.q[r][0] : &s.k[r - C][0];
+      uint2 rv = *reinterpret_cast<uint2*>(row + lane * 4);
+      float f[4] = {bf16_to_f32(rv.x & 0xffffu), bf16_to_f32(rv.x >> 16), bf16_to_f32(rv.y & 0xffffu),
+                    bf16_to_f32(rv.y >> 16)};
+      float ss = f[0] * f[0] + f[1] * f[1] + f[2] * f[2] + f[3] * f[3];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      float inv = 1.0f / fmaxf(sqrtf(ss), 1e-6f);
+      *reinterpret_cast<uint2*>(row + lane * 4) =
+          make_uint2(pack_bf16x2(f[0] * inv, f[1] * inv), pack_bf16x2(f[2] * inv, f[3] * inv));
+    }
+  } else {
+    for (int i = tid; i < C * (DK / 4); i += 256) {
+      int r = i / (DK / 4), c = (i % (DK / 4)) * 4;
+      float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t0 + r < seq) gv = *reinterpret_cast<const float4*>(gg + (tok0 + t0 + r) * ldg + h * DK + c);
+      *reinterpret_cast<float4*>(&s.Gc[r][c]) = gv;
+    }
+    if (tid < C) s.beta[tid] = t0 + tid < seq ? bg[(tok0 + t0 + tid) * heads + h] : 0.0f;
   }
-  if (tid < C) s.beta[tid] = t0 + tid < seq ? bg[(tok0 + t0 + tid) * heads + h] : 0.0f;
   __syncthreads();
   if (tid < DK) {  // inclusive prefix sum of the log decay per key channel
     float acc = 0.0f;
@@ -492,7 +539,7 @@ size_t kda_workspace_bytes(int batch, int seq, int heads) {
 
 int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, long long ld_qkv, const float* g,
                            const float* beta, float* state, uint16_t* o, long long ldo, int batch, int seq, int heads,
-                           void* workspace, size_t workspace_bytes, cudaStream_t s) {
+                           void* workspace, size_t workspace_bytes, cudaStream_t s, const KdaRawGate* raw) {
   if (batch <= 0 || seq <= 0 || heads <= 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "kda: empty input");
   if (ld_qkv % 8 || ldo % 2 || (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15u))
     return set_error(ENNX_B200_INVALID_ARGUMENT, "kda: q/k/v must be 16-byte aligned with ld %% 8 == 0");
@@ -511,8 +558,12 @@ int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t*
     g_attr[dev] = true;
   }
   const int nchunks = (seq + C - 1) / C;
+  KdaRawGate rg;
+  memset(&rg, 0, sizeof(rg));
+  if (raw) rg = *raw;
+  if (!raw && (!g || !beta)) return set_error(ENNX_B200_INVALID_ARGUMENT, "kda: g and beta are required");
   kda_prep_kernel<<<dim3(nchunks, batch * heads), 256, sizeof(PrepSmem), s>>>(
-      q, k, ld_qkv, g, (long long)heads * DK, beta, seq, heads, nchunks, (uint8_t*)workspace);
+      q, k, ld_qkv, g, (long long)heads * DK, beta, seq, heads, nchunks, rg, (uint8_t*)workspace);
   ENNX_LAUNCH_CHECK("kda prep");
   kda_scan_kernel<<<dim3(batch * heads, DK / SV), 128, sizeof(ScanSmem), s>>>(v, ld_qkv, (const uint8_t*)workspace,
                                                                                state, o, ldo, seq, heads, nchunks);

@@ -48,9 +48,22 @@ int32_t launch_gqa_attention(const uint16_t* q, long long ldq, const uint16_t* k
                              long long ldv, uint16_t* o, long long ldo, int batch, int seq, int hq, int hkv,
                              cudaStream_t s);
 size_t kda_workspace_bytes(int batch, int seq, int heads);
+// Forward-path inputs of the chunked KDA: gates from the raw projections and
+// in-kernel L2 normalisation of q and k (sequences < split_seq use set 0).
+struct KdaRawGate {
+  const uint16_t* f;      // raw forget logits [T, heads*128]
+  long long ldf;
+  const uint16_t* rbeta;  // raw beta logits, column h of row t
+  long long ldb;
+  const uint16_t *decay0, *decay1;  // [heads]
+  const uint16_t *tb0, *tb1;        // [heads*128]
+  long long split_seq;
+  int active;
+};
 int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, long long ld_qkv,
                            const float* g, const float* beta, float* state, uint16_t* o, long long ldo, int batch,
-                           int seq, int heads, void* workspace, size_t workspace_bytes, cudaStream_t s);
+                           int seq, int heads, void* workspace, size_t workspace_bytes, cudaStream_t s,
+                           const KdaRawGate* raw = nullptr);
 
 // gemm.cu (internal form of ennx_b200_gemm_bf16)
 int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* a, const uint16_t* b, void* c, cudaStream_t s);

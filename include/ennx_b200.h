@@ -135,8 +135,9 @@ enum {
  *
  * Epilogues: EPI_SWIGLU expects B's rows in blocks of 256 = [128 gate rows |
  * 128 up rows]; output column j of block b is silu(g)*u of row 128b+j.
- * EPI_LSE writes lse_partial[r * ceil(N/256) + tile] = (max, sum exp(x-max))
- * as float2 and target_logit[r] = acc[r, targets[r]].
+ * EPI_LSE writes lse_partial[r * 2*ceil(N/256) + j] = (max, sum exp(x - max))
+ * over columns [128j, 128j + 128) as float2 ((-inf, 0) for an empty range),
+ * and target_logit[r] = acc[r, targets[r]].
  * Requirements: K % 64 == 0, K >= 64, lda/ldb % 8 == 0, 16-byte aligned A/B. */
 typedef struct {
     int32_t m, n, k;
@@ -150,7 +151,7 @@ typedef struct {
     int64_t ldr;
     const float* row_scale;   /* EPI_ROWSCALE: device float[M] */
     const int32_t* targets;   /* EPI_LSE: device int32[M] */
-    float* lse_partial;       /* EPI_LSE: device float2[M, ceil(N/256)] */
+    float* lse_partial;       /* EPI_LSE: device float2[M, 2*ceil(N/256)] */
     float* target_logit;      /* EPI_LSE: device float[M] */
 } ennx_b200_gemm_params;
 

@@ -295,7 +295,7 @@ static void box_muller(uint32_t a, uint32_t b, float* z0, float* z1) {
     float u1 = ((float)(a >> 8) + 0.5f) * 5.9604644775390625e-08f; /* 2^-24 */
     float u2 = (float)(b >> 8) * 5.9604644775390625e-08f;
     double r = sqrt(-2.0 * log((double)u1));
-    double th = 2.0 * M_PI * (double)u2;
+    double th = 2.0 * M_PI * ((double)u2 - 0.5);
     *z0 = (float)(r * cos(th));
     *z1 = (float)(r * sin(th));
 }

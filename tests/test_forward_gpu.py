@@ -11,7 +11,7 @@ torch = pytest.importorskip("torch")
 
 from ennx_b200.model import HybridConfig, PopulationEvaluator, init_weights  # noqa: E402
 
-SMALL = HybridConfig(layers=4, hidden=256, vocab=1000, attn_period=4, q_heads=2, kv_heads=1, kda_heads=2,
+SMALL = HybridConfig(layers=4, hidden=256, vocab=1152, attn_period=4, q_heads=2, kv_heads=1, kda_heads=2,
                      gate_rank=64, experts=8, top_k=2, expert_width=128)
 
 

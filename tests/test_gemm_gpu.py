@@ -96,11 +96,12 @@ def test_gemm_rowscale_epilogue():
     close(c.float().cpu().numpy(), ref_gemm(a, b) * s.numpy()[:, None].astype(np.float64))
 
 
-def test_gemm_lse_epilogue_cross_entropy():
-    M, V, K = 257, 1000, 128
+@pytest.mark.parametrize("V", [1000, 1100, 1152])
+def test_gemm_lse_epilogue_cross_entropy(V):
+    M, K = 257, 128
     a, b = rand_bf16((M, K), 16, 0.5), rand_bf16((V, K), 17, 0.5)
     tg = torch.randint(0, V, (M,), generator=torch.Generator().manual_seed(0), dtype=torch.int32)
-    nt = (V + 255) // 256
+    nt = 2 * ((V + 255) // 256)
     lse = torch.empty(M, nt, 2, device="cuda")
     tl = torch.empty(M, device="cuda")
     ops.gemm(a.cuda(), b.cuda(), epilogue=_abi.EPI_LSE, targets=tg.cuda(), lse_partial=lse, target_logit=tl)

@@ -98,6 +98,7 @@ SIGNATURES = {
     "ennx_b200_gqa_attention": (_I32, [_P, _P, _P, _P, _I32, _I32, _I32, _I32, _F32, _P]),
     "ennx_b200_kda_workspace_size": (_SZ, [_I32, _I32, _I32]),
     "ennx_b200_kda_chunked": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P, _SZ, _P]),
+    "ennx_b200_kda_chunked_noalloc": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P]),
     "ennx_b200_population_workspace_size": (_SZ, [_P, _I32, _I32]),
     "ennx_b200_population_forward": (_I32, [_P, _P, _U64, _F32, _I32, _I32, _P, _I32, _I32, _P, _P, _SZ, _P]),
     "ennx_b200_profile_begin": (_I32, []),

@@ -218,6 +218,23 @@ ENNX_B200_API int32_t ennx_b200_kda_chunked(const uint16_t* q, const uint16_t* k
                                             int32_t seq, int32_t heads, void* workspace, size_t workspace_bytes,
                                             void* stream);
 
+/* Same operation as ennx_b200_kda_chunked for callers that cannot allocate
+ * device memory (code inside a CUDA graph being captured, hosts that reserve
+ * all device memory for their own pool, latency-critical embedders).  No
+ * counterpart exists in the reference.  The per-chunk scratch comes from one
+ * 32 MiB static device array that every GPU loading this library holds until
+ * exit, so batch * heads * ceil(seq / 64) must stay <= 508 (66 048 bytes per
+ * chunk record); larger problems are rejected with ENNX_B200_INVALID_ARGUMENT.
+ * Calls allocate nothing (no cudaMalloc/cudaFree, no allocating library
+ * call).  The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress) with that device current; make that first call
+ * before any stream capture.  Every call shares the one array: calls that
+ * overlap on the GPU (different streams, or threads) race on it. */
+ENNX_B200_API int32_t ennx_b200_kda_chunked_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v,
+                                                    const float* g, const float* beta, float* state,
+                                                    uint16_t* o, int32_t batch, int32_t seq, int32_t heads,
+                                                    void* stream);
+
 /* ---- population forward: the hybrid KDA/GQA-MoE decoder --------------- */
 
 typedef struct {

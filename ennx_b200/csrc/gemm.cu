@@ -215,9 +215,14 @@ __global__ void __launch_bounds__(THREADS, 1)
           __syncwarp();
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
-            int jj = (j + (lane >> 1)) & 3;  // rotate the 16-byte chunks: fewer bank conflicts
+            const int jj = (j + (lane >> 1)) & 3;  // rotate the 16-byte chunks: fewer bank conflicts
+            uint32_t c0, c1, c2, c3;  // constant-index selects keep pk in registers
+            c0 = jj == 0 ? pk[0] : jj == 1 ? pk[4] : jj == 2 ? pk[8] : pk[12];
+            c1 = jj == 0 ? pk[1] : jj == 1 ? pk[5] : jj == 2 ? pk[9] : pk[13];
+            c2 = jj == 0 ? pk[2] : jj == 1 ? pk[6] : jj == 2 ? pk[10] : pk[14];
+            c3 = jj == 0 ? pk[3] : jj == 1 ? pk[7] : jj == 2 ? pk[11] : pk[15];
             asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(stg_addr + lane * 64 + jj * 16),
-                         "r"(pk[4 * jj]), "r"(pk[4 * jj + 1]), "r"(pk[4 * jj + 2]), "r"(pk[4 * jj + 3])
+                         "r"(c0), "r"(c1), "r"(c2), "r"(c3)
                          : "memory");
           }
           fence_proxy_async();
@@ -235,7 +240,9 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
             for (int j = 0; j < 4; ++j) st_global_v4(dst + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
           } else {
-            for (int j = 0; col0 + j < ncols; ++j) dst[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < ncols) dst[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
           }
         }
       };
@@ -303,7 +310,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                              __float_as_uint(x3));
               }
             } else {
-              for (int j = 0; col0 + j < a.N; ++j) dst[j] = __uint_as_float(v[j]) * rs;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < a.N) dst[j] = __uint_as_float(v[j]) * rs;
             }
             continue;
           }
@@ -325,7 +334,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 }
               }
             } else {
-              for (int j = 0; col0 + j < a.N; ++j) x[j] += bf16_to_f32(rp[j]);
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (col0 + j < a.N) x[j] += bf16_to_f32(rp[j]);
             }
           }
           uint32_t pk[16];

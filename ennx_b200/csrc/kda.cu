@@ -366,8 +366,10 @@ __global__ void __launch_bounds__(128) kda_scan_kernel(const uint16_t* __restric
                                                        int nchunks) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   ScanSmem& s = *reinterpret_cast<ScanSmem*>(smem_raw);
-  const int bh = blockIdx.x, b = bh / heads, h = bh % heads;
-  const int j0 = blockIdx.y * SV;
+  // the value slices of one (sequence, head) are adjacent block indices, so
+  // they run together and share the chunk records through L2
+  const int bh = blockIdx.y, b = bh / heads, h = bh % heads;
+  const int j0 = blockIdx.x * SV;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long tok0 = (long long)b * seq;
   const float qscale = rsqrtf((float)DK);
@@ -565,7 +567,7 @@ int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t*
   kda_prep_kernel<<<dim3(nchunks, batch * heads), 256, sizeof(PrepSmem), s>>>(
       q, k, ld_qkv, g, (long long)heads * DK, beta, seq, heads, nchunks, rg, (uint8_t*)workspace);
   ENNX_LAUNCH_CHECK("kda prep");
-  kda_scan_kernel<<<dim3(batch * heads, DK / SV), 128, sizeof(ScanSmem), s>>>(v, ld_qkv, (const uint8_t*)workspace,
+  kda_scan_kernel<<<dim3(DK / SV, batch * heads), 128, sizeof(ScanSmem), s>>>(v, ld_qkv, (const uint8_t*)workspace,
                                                                                state, o, ldo, seq, heads, nchunks);
   ENNX_LAUNCH_CHECK("kda scan");
   return ENNX_B200_OK;

@@ -20,6 +20,7 @@
 // The reference has no GEMM (its only contraction is the fp32 GEMV of
 // cuda/kernels/src/lib.rs:2359-2423); this kernel is the B200 replacement of
 // the "linear" operator for M > 1 (rust/crates/ennx/src/dense/linear.rs:484).
+#include <stdlib.h>
 #include <string.h>
 
 #include "common.cuh"
@@ -32,6 +33,19 @@ constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;  // 16 KB
 constexpr int B_BYTES = BN * BK * 2;  // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int MAX_STAGES = 6;
+// Per-variant geometry.  Single-CTA: 128x256 tiles, 4 stages of A 128x64 +
+// B 256x64.  CTA pair (cta_group::2): 256x256 tiles over two SMs, each CTA
+// holding A 128x64 and half of B (128x64) per stage, 6 stages.
+template <bool PAIR> struct Geo {
+  static constexpr int TM = PAIR ? 256 : 128;       // rows per tile unit
+  static constexpr int BROWS = PAIR ? 128 : 256;    // B rows loaded per CTA
+  static constexpr int NST = PAIR ? 6 : 4;          // pipeline stages
+  static constexpr int BBYTES = BROWS * BK * 2;
+  static constexpr int STAGE = A_BYTES + BBYTES;
+  static constexpr uint32_t IDESC = idesc_bf16_f32(PAIR ? 256 : 128, BN);
+};
+static_assert(Geo<true>::NST * Geo<true>::STAGE == STAGES * STAGE_BYTES, "both variants use the same ring size");
 constexpr int EPI_WARPS = 8;                 // two warpgroups, each owns half of the tile's columns
 constexpr int THREADS = 64 + 32 * EPI_WARPS;  // producer warp, MMA warp, epilogue warps
 constexpr int EPI_BUF = 32 * 32 * 2;          // per-warp 32x32 bf16 staging tile for TMA stores
@@ -61,7 +75,7 @@ struct Args {
 };
 
 struct Smem {  // lives after the stage ring
-  uint64_t full[STAGES], empty[STAGES], tfull[2], tempty[2];
+  uint64_t full[MAX_STAGES], empty[MAX_STAGES], tfull[2], tempty[2];
   uint32_t tmem_base;
   int abort_flag;
   int total_tiles;
@@ -73,6 +87,7 @@ struct TileInfo {
   int g, mt, nt, row0, rows;
 };
 
+template <int TM>
 __device__ __forceinline__ TileInfo decode_tile(const Smem& s, const Args& a, int tile) {
   int lo = 0, hi = a.groups - 1;
   while (lo < hi) {
@@ -83,7 +98,7 @@ __device__ __forceinline__ TileInfo decode_tile(const Smem& s, const Args& a, in
   t.g = lo;
   t.row0 = s.row0[lo];
   t.rows = s.row0[lo + 1] - s.row0[lo];
-  int mtiles = (t.rows + BM - 1) / BM;
+  int mtiles = (t.rows + TM - 1) / TM;
   int local = tile - s.tile0[lo];
   t.mt = local % mtiles;
   t.nt = local / mtiles;
@@ -92,6 +107,7 @@ __device__ __forceinline__ TileInfo decode_tile(const Smem& s, const Args& a, in
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
+template <bool PAIR>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, Args a) {
@@ -100,14 +116,18 @@ __global__ void __launch_bounds__(THREADS, 1)
   uint8_t* ring = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* epi_smem = ring + STAGES * STAGE_BYTES;
   Smem& s = *reinterpret_cast<Smem*>(epi_smem + EPI_WARPS * EPI_BUF);
+  using G = Geo<PAIR>;
   uint8_t* sA = ring;
-  uint8_t* sB = ring + STAGES * A_BYTES;
+  uint8_t* sB = ring + G::NST * A_BYTES;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = PAIR ? (int)cluster_ctarank() : 0;          // CTA within the pair
+  const int unit0 = PAIR ? blockIdx.x >> 1 : blockIdx.x;        // first tile unit
+  const int units = PAIR ? gridDim.x >> 1 : gridDim.x;          // tile-unit stride
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < STAGES; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], 1); }
-    for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], EPI_WARPS); }
+    for (int i = 0; i < G::NST; ++i) { mbar_init(&s.full[i], 1); mbar_init(&s.empty[i], 1); }
+    for (int i = 0; i < 2; ++i) { mbar_init(&s.tfull[i], 1); mbar_init(&s.tempty[i], (PAIR ? 2 : 1) * EPI_WARPS); }
     s.abort_flag = 0;
     // group table: row offsets (device table or uniform split) and tile prefix
     int tiles = 0;
@@ -118,7 +138,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       s.row0[g + 1] = r1;
       s.tile0[g] = tiles;
       int rows = r1 - r0;
-      tiles += (rows > 0 ? (rows + BM - 1) / BM : 0) * a.n_tiles;
+      tiles += (rows > 0 ? (rows + G::TM - 1) / G::TM : 0) * a.n_tiles;
     }
     s.tile0[a.groups] = tiles;
     s.total_tiles = tiles;
@@ -130,8 +150,12 @@ __global__ void __launch_bounds__(THREADS, 1)
     tma_prefetch_desc(&tmB);
     if (a.has_tmc) tma_prefetch_desc(&tmC);
   }
-  if (warp == 1) { tmem_alloc(&s.tmem_base, TMEM_COLS); tmem_relinquish(); }
+  if (warp == 1) {
+    if (PAIR) { tmem_alloc_pair(&s.tmem_base, TMEM_COLS); tmem_relinquish_pair(); }
+    else { tmem_alloc(&s.tmem_base, TMEM_COLS); tmem_relinquish(); }
+  }
   __syncthreads();
+  if (PAIR) cluster_sync();  // the peer's barriers exist before any cross-CTA arrive
   tc_fence_after();
   const uint32_t tmem_base = s.tmem_base;
   const int total = s.total_tiles;
@@ -141,25 +165,33 @@ __global__ void __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int tile = blockIdx.x; tile < total && !*(volatile int*)&s.abort_flag; tile += gridDim.x) {
-        TileInfo t = decode_tile(s, a, tile);
-        int arow = t.row0 + t.mt * BM;
-        int brow = t.g * a.b_group_rows + t.nt * BN;
+      for (int tile = unit0; tile < total && !*(volatile int*)&s.abort_flag; tile += units) {
+        TileInfo t = decode_tile<G::TM>(s, a, tile);
+        int arow = t.row0 + t.mt * G::TM + rank * BM;
+        int brow = t.g * a.b_group_rows + t.nt * BN + rank * G::BROWS;
         for (int kb = 0; kb < KB; ++kb) {
           if (!mbar_wait(&s.empty[stage], phase ^ 1u, a.err)) { s.abort_flag = 1; break; }
-          mbar_arrive_expect_tx(&s.full[stage], STAGE_BYTES);
-          tma_load_2d(sA + stage * A_BYTES, &tmA, &s.full[stage], kb * BK, arow);
-          tma_load_2d(sB + stage * B_BYTES, &tmB, &s.full[stage], kb * BK, brow);
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          if (PAIR) {
+            // both CTAs' bytes complete on the leader's barrier; only the leader arrives
+            if (rank == 0) mbar_arrive_expect_tx(&s.full[stage], 2 * G::STAGE);
+            const uint32_t bar = mapa_shared(&s.full[stage], 0);
+            tma_load_2d_pair(sA + stage * A_BYTES, &tmA, bar, kb * BK, arow);
+            tma_load_2d_pair(sB + stage * G::BBYTES, &tmB, bar, kb * BK, brow);
+          } else {
+            mbar_arrive_expect_tx(&s.full[stage], G::STAGE);
+            tma_load_2d(sA + stage * A_BYTES, &tmA, &s.full[stage], kb * BK, arow);
+            tma_load_2d(sB + stage * G::BBYTES, &tmB, &s.full[stage], kb * BK, brow);
+          }
+          if (++stage == G::NST) { stage = 0; phase ^= 1u; }
         }
       }
     }
   } else if (warp == 1) {
-    if (lane == 0) {
+    if (lane == 0 && rank == 0) {  // the leader CTA issues the MMAs of the pair
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
-      for (int tile = blockIdx.x; tile < total && !*(volatile int*)&s.abort_flag; tile += gridDim.x, ++it) {
+      for (int tile = unit0; tile < total && !*(volatile int*)&s.abort_flag; tile += units, ++it) {
         int acc = it & 1;
         uint32_t acc_phase = (it >> 1) & 1;
         if (!mbar_wait(&s.tempty[acc], acc_phase ^ 1u, a.err)) { s.abort_flag = 1; break; }
@@ -170,16 +202,22 @@ __global__ void __launch_bounds__(THREADS, 1)
           if (!mbar_wait(&s.full[stage], phase, a.err)) { s.abort_flag = 1; ok = false; break; }
           tc_fence_after();
           uint32_t abase = smem_u32(sA + stage * A_BYTES);
-          uint32_t bbase = smem_u32(sB + stage * B_BYTES);
+          uint32_t bbase = smem_u32(sB + stage * G::BBYTES);
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k)
-            umma_f16(d, smem_desc_sw128(abase + k * 32), smem_desc_sw128(bbase + k * 32), IDESC,
-                     (kb | k) != 0);
-          umma_commit(&s.empty[stage]);
-          if (++stage == STAGES) { stage = 0; phase ^= 1u; }
+          for (int k = 0; k < BK / 16; ++k) {
+            if (PAIR)
+              umma_f16_pair(d, smem_desc_sw128(abase + k * 32), smem_desc_sw128(bbase + k * 32), G::IDESC,
+                            (kb | k) != 0);
+            else
+              umma_f16(d, smem_desc_sw128(abase + k * 32), smem_desc_sw128(bbase + k * 32), G::IDESC, (kb | k) != 0);
+          }
+          if (PAIR) umma_commit_pair(&s.empty[stage], 0x3);
+          else umma_commit(&s.empty[stage]);
+          if (++stage == G::NST) { stage = 0; phase ^= 1u; }
         }
         if (!ok) break;
-        umma_commit(&s.tfull[acc]);
+        if (PAIR) umma_commit_pair(&s.tfull[acc], 0x3);
+        else umma_commit(&s.tfull[acc]);
       }
     }
   } else {
@@ -194,17 +232,18 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t* stg = epi_smem + ew * EPI_BUF;
     const uint32_t stg_addr = smem_u32(stg);
     int it = 0;
-    for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++it) {
+    for (int tile = unit0; tile < total; tile += units, ++it) {
       int acc = it & 1;
       uint32_t acc_phase = (it >> 1) & 1;
       if (!mbar_wait(&s.tfull[acc], acc_phase, a.err)) { s.abort_flag = 1; break; }
       tc_fence_after();
-      TileInfo t = decode_tile(s, a, tile);
-      const int mrow = t.mt * BM + r_in_tile;
+      TileInfo t = decode_tile<G::TM>(s, a, tile);
+      const int cta_row = t.mt * G::TM + rank * BM;  // first row of this CTA's 128 rows, within the group
+      const int mrow = cta_row + r_in_tile;
       const bool row_ok = mrow < t.rows;
       const long long grow = (long long)t.row0 + mrow;
-      const int warp_row0 = t.row0 + t.mt * BM + q * 32;
-      const bool use_tma = a.has_tmc && (t.mt * BM + BM <= t.rows || t.row0 + t.rows == a.M);
+      const int warp_row0 = t.row0 + cta_row + q * 32;
+      const bool use_tma = a.has_tmc && (cta_row + BM <= t.rows || t.row0 + t.rows == a.M);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
       uint32_t v[32];
 
@@ -347,16 +386,21 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&s.tempty[acc]);
+      if (lane == 0) {
+        if (PAIR) mbar_arrive_cluster(mapa_shared(&s.tempty[acc], 0));  // the leader's MMA waits on both CTAs
+        else mbar_arrive(&s.tempty[acc]);
+      }
     }
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     __syncwarp();
   }
 
   __syncthreads();
+  if (PAIR) cluster_sync();  // both CTAs are done with TMEM and with each other's barriers
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, TMEM_COLS);
+    if (PAIR) tmem_dealloc_pair(tmem_base, TMEM_COLS);
+    else tmem_dealloc(tmem_base, TMEM_COLS);
   }
 }
 
@@ -396,10 +440,16 @@ int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint1
   if (p->residual && (p->ldr % 8 || ((uintptr_t)p->residual & 15u)))
     return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: residual must be 16-byte aligned with ldr %% 8 == 0");
 
+  // CTA-pair variant for problems with enough rows to fill 256-row tiles;
+  // ENNX_B200_GEMM_PAIR=0/1 forces a variant (tests exercise both).
+  bool pair = M >= 1024;
+  if (const char* e = getenv("ENNX_B200_GEMM_PAIR")) pair = e[0] == '1';
+  const int brows = pair ? Geo<true>::BROWS : Geo<false>::BROWS;
+
   const long long b_rows = (long long)(G - 1) * p->b_group_rows + N;
   CUtensorMap ta, tb, tc;
   ENNX_TRY(make_tmap_2d_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)p->lda, BK, BM, true));
-  ENNX_TRY(make_tmap_2d_bf16(&tb, B, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, BK, BN, true));
+  ENNX_TRY(make_tmap_2d_bf16(&tb, B, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, BK, brows, true));
   memset(&tc, 0, sizeof(tc));
   const bool bf16_out = epi == ENNX_B200_EPI_BF16 || epi == ENNX_B200_EPI_SWIGLU || epi == ENNX_B200_EPI_ROWSCALE;
   if (bf16_out) {
@@ -430,14 +480,36 @@ int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint1
   int dev = 0;
   cudaGetDevice(&dev);
   if (!g_attr_set[dev]) {
-    ENNX_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+    ENNX_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
               "gemm: set smem");
+    ENNX_CUDA(cudaFuncSetAttribute(gemm_bf16_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+              "gemm: set smem (pair)");
     g_attr_set[dev] = true;
   }
-  long long tiles_bound = ((long long)M / BM + G) * a.n_tiles;
-  int grid = sm_count();
-  if (tiles_bound < grid) grid = (int)tiles_bound;
-  gemm_bf16_kernel<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, tc, a);
+  if (!pair) {
+    long long tiles_bound = ((long long)M / BM + G) * a.n_tiles;
+    int grid = sm_count();
+    if (tiles_bound < grid) grid = (int)tiles_bound;
+    gemm_bf16_kernel<false><<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, tc, a);
+  } else {
+    long long units_bound = ((long long)M / Geo<true>::TM + G) * a.n_tiles;
+    long long clusters = sm_count() / 2;
+    if (units_bound < clusters) clusters = units_bound;
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3((unsigned)(2 * clusters));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = SMEM_BYTES;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ENNX_CUDA(cudaLaunchKernelEx(&cfg, gemm_bf16_kernel<true>, ta, tb, tc, a), "gemm pair launch");
+  }
   ENNX_LAUNCH_CHECK("gemm launch");
   return ENNX_B200_OK;
 }

@@ -15,6 +15,13 @@ from ennx_b200 import _abi, ops  # noqa: E402
 RTOL, ATOL = 2e-2, 1e-2
 
 
+@pytest.fixture(params=["0", "1"], ids=["1cta", "cta_pair"], autouse=True)
+def gemm_variant(request, monkeypatch):
+    """Run every GEMM test with the single-CTA and the CTA-pair (cta_group::2) kernel."""
+    monkeypatch.setenv("ENNX_B200_GEMM_PAIR", request.param)
+    return request.param
+
+
 def rand_bf16(shape, seed, scale=1.0):
     g = torch.Generator().manual_seed(seed)
     return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16)

@@ -6,6 +6,7 @@
 
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <cuda_bf16.h>
 #include <stdint.h>
 #include <stddef.h>
 
@@ -66,12 +67,13 @@ __host__ __device__ __forceinline__ float bf16_to_f32(uint16_t v) {
   uint32_t u = ((uint32_t)v) << 16; float f; memcpy(&f, &u, 4); return f;
 #endif
 }
-__device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) {
-  uint32_t bits = __float_as_uint(f);
-  return (uint16_t)((bits + 0x7fffu + ((bits >> 16) & 1u)) >> 16);
-}
+// Round to nearest even.  For finite inputs the hardware conversion produces
+// exactly the bits of the reference formula (bits + 0x7fff + lsb) >> 16
+// (rust/crates/ennx/src/dense/bf16.rs:270-273), including overflow to inf.
+__device__ __forceinline__ uint16_t f32_to_bf16_rne(float f) { return __bfloat16_as_ushort(__float2bfloat16_rn(f)); }
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
-  return (uint32_t)f32_to_bf16_rne(lo) | ((uint32_t)f32_to_bf16_rne(hi) << 16);
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);  // .x = lo (low half), .y = hi
+  return *reinterpret_cast<uint32_t*>(&v);
 }
 
 // ---------------------------------------------------------------------------
@@ -95,14 +97,16 @@ __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32
   }
 }
 
-// Box-Muller on the top 24 bits of two Philox words: u1 in (0, 1), angle
-// 2*pi*(u2 - 1/2) in [-pi, pi).  Uses the SFU approximations (log2, rsqrt,
-// sin/cos on [-pi, pi]); values agree with the fp64 oracle to ~1e-6.
+// Box-Muller on two Philox words: u1 = ((a >> 9) + 1/2) / 2^23 lies in (0, 1)
+// and is exact in fp32 (a 24-bit numerator would round 2^24 - 1/2 up to 1,
+// giving ln(u1) = 0 and a NaN from 0 * rsqrt(0)); angle
+// 2*pi*((b >> 8) / 2^24 - 1/2) in [-pi, pi).  Uses the SFU approximations
+// (log2, rsqrt, sin/cos on [-pi, pi]); values agree with the fp64 oracle to ~1e-6.
 __device__ __forceinline__ void box_muller(uint32_t a, uint32_t b, float& z0, float& z1) {
-  float u1 = __fmul_rn(__fadd_rn((float)(a >> 8), 0.5f), 5.9604644775390625e-08f);
+  float u1 = __fmul_rn(__fadd_rn((float)(a >> 9), 0.5f), 1.1920928955078125e-07f);
   float u2 = __fmul_rn((float)(b >> 8), 5.9604644775390625e-08f);
-  float x = __fmul_rn(-1.3862943611198906f, __log2f(u1));  // -2 ln(u1) = -2 ln2 log2(u1) > 0
-  float r = __fmul_rn(x, rsqrtf(x));
+  float x = __fmul_rn(-1.3862943611198906f, __log2f(u1));  // -2 ln(u1) = -2 ln2 log2(u1) >= 0
+  float r = x > 0.0f ? __fmul_rn(x, rsqrtf(x)) : 0.0f;
   float s, c;
   __sincosf(__fmul_rn(6.283185307179586f, __fsub_rn(u2, 0.5f)), &s, &c);
   z0 = __fmul_rn(r, c);

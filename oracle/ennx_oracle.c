@@ -289,10 +289,10 @@ void eo_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out
     out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
 }
 
-/* Box-Muller on the top 24 bits of two Philox words; computed in double so
+/* Box-Muller on two Philox words (23-bit u1 in (0,1), 24-bit angle); computed in double so
  * the oracle is the exactly rounded value the device approximates. */
 static void box_muller(uint32_t a, uint32_t b, float* z0, float* z1) {
-    float u1 = ((float)(a >> 8) + 0.5f) * 5.9604644775390625e-08f; /* 2^-24 */
+    float u1 = ((float)(a >> 9) + 0.5f) * 1.1920928955078125e-07f; /* 2^-23: exact, < 1 */
     float u2 = (float)(b >> 8) * 5.9604644775390625e-08f;
     double r = sqrt(-2.0 * log((double)u1));
     double th = 2.0 * M_PI * ((double)u2 - 0.5);

@@ -131,3 +131,16 @@ def test_perturb_bf16_matches_oracle():
     assert st == 0
     e = O.perturb_bf16(w[:13], 7, 0, 3, 0.5, +1)
     assert np.abs(host_u16(plus)[:13].astype(np.int32) - e.astype(np.int32)).max() <= 1
+
+
+def test_perturb_noise_is_finite_over_many_draws():
+    # 2^26 normals: the top Philox words (which once gave u1 = 1 and a NaN
+    # radius) occur several times in this range; every output must be finite.
+    n = 1 << 26
+    w = torch.zeros(n, dtype=torch.int16, device="cuda")
+    plus, minus = torch.empty_like(w), torch.empty_like(w)
+    st = _abi.lib().ennx_b200_perturb_bf16(ptr(w), n, 12345, 7, 3, 1.0, ptr(plus), ptr(minus), stream())
+    assert st == 0
+    for t in (plus, minus):
+        bits = t.view(torch.int16)
+        assert not bool(((bits & 0x7F80) == 0x7F80).any().item())

@@ -4,156 +4,153 @@
 // Router math restates rust/crates/ennx/src/kda_moe.metal:570-621
 // (moe_router_topk): fp32 logits x.W_r^T, top-k by insertion with strict '>'
 // so ties keep the lower expert index, gates = max-subtracted softmax over the
-// k kept logits.  The logits use a FIXED reduction order so that they -- and
-// the routing indices -- are bit-identical to the CPU oracle
-// (oracle/ennx_oracle.c eo_router_logits): lane l of a warp owns elements
-// {256*j + 8*l + u}, runs a serial fma chain over j then u, and the 32
-// partials meet in an xor butterfly (16, 8, 4, 2, 1).
+// k kept logits.  Each logit is one serial fma chain over the hidden index,
+// the order of the reference's per-token loop, so the logits -- and the
+// routing indices -- are bit-identical to the CPU oracle
+// (oracle/ennx_oracle.c eo_router_logits).
 #include "common.cuh"
 #include "kernels.cuh"
 
 namespace ennx {
 
-// Router: a block owns up to TPB consecutive tokens of one weight set and
-// walks the experts in chunks whose weights are staged in shared memory
-// (EC experts x H bf16 <= 32 KB), so W_r is read from L2 once per block
-// instead of once per token.  A warp handles one token at a time with x in
-// registers; the per-lane element ownership and the fma/butterfly order are
-// the fixed reduction order described above.
-constexpr int kRouterTPB = 32;
-constexpr int kRouterSmem = 32768;
+// Router: a register-blocked fp32 SIMT GEMM.  A block owns RT consecutive
+// tokens of one weight set and all experts (in tiles of RE); K is staged
+// through shared memory in chunks of RK, converted from bf16 to fp32 once.
+// Thread (ty, tx) accumulates tokens 4*ty..4*ty+3 x experts 4*tx..4*tx+3,
+// each logit one serial fma chain over k = 0, 1, ..., H-1 starting from 0 --
+// the order of the reference's per-token loop (kda_moe.metal:589-595) and of
+// the CPU oracle, so logits are bit-identical.  The logits of the block's
+// tokens are kept in shared memory; one thread per token then runs the
+// insertion top-k and the gate softmax.
+constexpr int RT = 32, RE = 64, RK = 32, kRouterThreads = 128;
 
-template <int NJ, int SLOTS>
-__global__ void __launch_bounds__(256) router_topk_kernel(
+__global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
     const uint16_t* __restrict__ x, long long ldx, const uint16_t* __restrict__ w0, const uint16_t* __restrict__ w1,
-    long long split, long long tokens, int experts, int top_k, float* __restrict__ logits, int* __restrict__ idx,
-    float* __restrict__ gate) {
-  constexpr int H = NJ * 256;
-  constexpr int EC = kRouterSmem / (H * 2);
-  constexpr int TPW = kRouterTPB / 8;  // tokens per warp
-  __shared__ __align__(16) uint16_t ws[EC * H];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long long nb0 = (split + kRouterTPB - 1) / kRouterTPB;
+    long long split, long long tokens, int hidden, int experts, int top_k, float* __restrict__ logits,
+    int* __restrict__ idx, float* __restrict__ gate) {
+  extern __shared__ __align__(16) float rsm[];
+  float* As = rsm;                  // [2][RK][RT]
+  float* Bs = As + 2 * RK * RT;     // [2][RK][RE]
+  float* Ls = Bs + 2 * RK * RE;     // [RT][lds]
+  const int lds = ((experts + RE - 1) / RE) * RE + 1;
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const long long nb0 = (split + RT - 1) / RT;
   long long tb, te;
   const uint16_t* w;
   if ((long long)blockIdx.x < nb0) {
-    tb = (long long)blockIdx.x * kRouterTPB; te = min(split, tb + kRouterTPB); w = w0;
+    tb = (long long)blockIdx.x * RT; te = min(split, tb + RT); w = w0;
   } else {
-    tb = split + ((long long)blockIdx.x - nb0) * kRouterTPB; te = min(tokens, tb + kRouterTPB); w = w1;
+    tb = split + ((long long)blockIdx.x - nb0) * RT; te = min(tokens, tb + RT); w = w1;
   }
-  float mine[TPW][SLOTS];
+  const int nchunks = hidden / RK;
+  // global -> register staging: x: one uint4 (8 k of one token); w: two
+  const int xt = tid % RT, xq = tid / RT;  // token, 8-wide k group
+  for (int e0 = 0; e0 < experts; e0 += RE) {
+    uint4 rx, rw[2];
+    auto fetch = [&](int c) {
+      const long long t = tb + xt;
+      rx = t < te ? __ldg(reinterpret_cast<const uint4*>(x + t * ldx + c * RK + 8 * xq)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-  for (int tt = 0; tt < TPW; ++tt)
+      for (int i = 0; i < 2; ++i) {
+        const int li = tid + i * kRouterThreads, e = e0 + li % RE, q = li / RE;
+        rw[i] = e < experts ? __ldg(reinterpret_cast<const uint4*>(w + (long long)e * hidden + c * RK + 8 * q))
+                            : make_uint4(0, 0, 0, 0);
+      }
+    };
+    auto stash = [&](int buf) {
+      float* a = As + buf * RK * RT;
+      float* bb = Bs + buf * RK * RE;
+      const uint32_t xv[4] = {rx.x, rx.y, rx.z, rx.w};
 #pragma unroll
-    for (int s = 0; s < SLOTS; ++s) mine[tt][s] = -INFINITY;
-
-  for (int e0 = 0; e0 < experts; e0 += EC) {
-    const int ne = min(EC, experts - e0);
-    __syncthreads();
-    for (int i = threadIdx.x; i < ne * H / 8; i += blockDim.x)
-      reinterpret_cast<uint4*>(ws)[i] = __ldg(reinterpret_cast<const uint4*>(w + (long long)e0 * H) + i);
-    __syncthreads();
+      for (int h = 0; h < 4; ++h) {
+        a[(8 * xq + 2 * h) * RT + xt] = bf16_to_f32((uint16_t)(xv[h] & 0xffffu));
+        a[(8 * xq + 2 * h + 1) * RT + xt] = bf16_to_f32((uint16_t)(xv[h] >> 16));
+      }
 #pragma unroll
-    for (int tt = 0; tt < TPW; ++tt) {
-      const long long t = tb + warp + 8 * tt;
-      if (t >= te) break;
-      uint4 xs[NJ];
+      for (int i = 0; i < 2; ++i) {
+        const int li = tid + i * kRouterThreads, e = li % RE, q = li / RE;
+        const uint32_t wv[4] = {rw[i].x, rw[i].y, rw[i].z, rw[i].w};
 #pragma unroll
-      for (int j = 0; j < NJ; ++j) xs[j] = *reinterpret_cast<const uint4*>(x + t * ldx + 256 * j + 8 * lane);
-      // four experts at a time: independent fma chains and butterflies give
-      // the warp instruction-level parallelism; each logit keeps its own
-      // fixed reduction order.
-      int el = 0;
-      for (; el + 4 <= ne; el += 4) {
-        float p[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-          uint32_t xw[4] = {xs[j].x, xs[j].y, xs[j].z, xs[j].w};
-#pragma unroll
-          for (int g = 0; g < 4; ++g) {
-            uint4 wv = *reinterpret_cast<const uint4*>(ws + (el + g) * H + 256 * j + 8 * lane);
-            uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              p[g] = __fmaf_rn(bf16_to_f32((uint16_t)(xw[h] & 0xffffu)), bf16_to_f32((uint16_t)(ww[h] & 0xffffu)), p[g]);
-              p[g] = __fmaf_rn(bf16_to_f32((uint16_t)(xw[h] >> 16)), bf16_to_f32((uint16_t)(ww[h] >> 16)), p[g]);
-            }
-          }
-        }
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1)
-#pragma unroll
-          for (int g = 0; g < 4; ++g) p[g] = __fadd_rn(p[g], __shfl_xor_sync(0xffffffffu, p[g], o));
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const int e = e0 + el + g;
-#pragma unroll
-          for (int s2 = 0; s2 < SLOTS; ++s2)
-            if (e >> 5 == s2 && lane == (e & 31)) mine[tt][s2] = p[g];
-          if (logits && lane == 0) logits[t * experts + e] = p[g];
+        for (int h = 0; h < 4; ++h) {
+          bb[(8 * q + 2 * h) * RE + e] = bf16_to_f32((uint16_t)(wv[h] & 0xffffu));
+          bb[(8 * q + 2 * h + 1) * RE + e] = bf16_to_f32((uint16_t)(wv[h] >> 16));
         }
       }
-      for (; el < ne; ++el) {
-        const uint16_t* wr = ws + el * H;
-        float p = 0.0f;
+    };
+    float acc[4][4];
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-          uint4 wv = *reinterpret_cast<const uint4*>(wr + 256 * j + 8 * lane);
-          uint32_t xw[4] = {xs[j].x, xs[j].y, xs[j].z, xs[j].w};
-          uint32_t ww[4] = {wv.x, wv.y, wv.z, wv.w};
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            p = __fmaf_rn(bf16_to_f32((uint16_t)(xw[h] & 0xffffu)), bf16_to_f32((uint16_t)(ww[h] & 0xffffu)), p);
-            p = __fmaf_rn(bf16_to_f32((uint16_t)(xw[h] >> 16)), bf16_to_f32((uint16_t)(ww[h] >> 16)), p);
-          }
-        }
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+    __syncthreads();  // previous expert tile's readers are done with the buffers
+    fetch(0);
+    stash(0);
+    __syncthreads();
+    for (int c = 0; c < nchunks; ++c) {
+      if (c + 1 < nchunks) fetch(c + 1);
+      const float* a = As + (c & 1) * RK * RT + 4 * ty;
+      const float* bb = Bs + (c & 1) * RK * RE + 4 * tx;
 #pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) p = __fadd_rn(p, __shfl_xor_sync(0xffffffffu, p, o));
-        const int e = e0 + el;
+      for (int k = 0; k < RK; ++k) {
+        const float4 av = *reinterpret_cast<const float4*>(a + k * RT);
+        const float4 bv = *reinterpret_cast<const float4*>(bb + k * RE);
+        const float ar[4] = {av.x, av.y, av.z, av.w}, br[4] = {bv.x, bv.y, bv.z, bv.w};
 #pragma unroll
-        for (int s2 = 0; s2 < SLOTS; ++s2)
-          if (e >> 5 == s2 && lane == (e & 31)) mine[tt][s2] = p;
-        if (logits && lane == 0) logits[t * experts + e] = p;
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(ar[i], br[j], acc[i][j]);
       }
+      if (c + 1 < nchunks) stash((c + 1) & 1);
+      __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) Ls[(4 * ty + i) * lds + e0 + 4 * tx + j] = acc[i][j];
+  }
+  __syncthreads();
+  if (logits) {
+    for (int i = tid; i < RT * experts; i += kRouterThreads) {
+      const int r = i / experts, e = i % experts;
+      if (tb + r < te) logits[(tb + r) * experts + e] = Ls[r * lds + e];
     }
   }
-
-#pragma unroll
-  for (int tt = 0; tt < TPW; ++tt) {
-    const long long t = tb + warp + 8 * tt;
-    if (t >= te) break;
+  if (tid < RT && tb + tid < te) {
+    // insertion with strict '>': once a score is inserted at rank r every
+    // lower rank shifts down by one (branch-free over constant indices)
     float val[8];
     int ids[8];
-    unsigned used = 0;
-    for (int r = 0; r < top_k; ++r) {
-      float bv = -INFINITY;
-      int bi = 0x7fffffff;
 #pragma unroll
-      for (int s = 0; s < SLOTS; ++s) {
-        int e = s * 32 + lane;
-        if (e < experts && !(used >> s & 1u)) {
-          if (mine[tt][s] > bv || (mine[tt][s] == bv && e < bi)) { bv = mine[tt][s]; bi = e; }
+    for (int r = 0; r < 8; ++r) { val[r] = -INFINITY; ids[r] = 0; }
+    const float* row = Ls + tid * lds;
+    for (int e = 0; e < experts; ++e) {
+      float v = row[e];
+      int id = e;
+      bool shifting = false;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r < top_k) {
+          const bool take = shifting || v > val[r];
+          if (take) {
+            const float tv = val[r];
+            const int ti = ids[r];
+            val[r] = v; ids[r] = id; v = tv; id = ti;
+          }
+          shifting = take;
         }
       }
-#pragma unroll
-      for (int o = 16; o >= 1; o >>= 1) {
-        float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
-      }
-      if (bi == 0x7fffffff) bi = 0;  // fewer finite logits than k: keep index 0 like the reference
-      val[r] = bv;
-      ids[r] = bi;
-      if ((bi & 31) == lane) used |= 1u << (bi >> 5);
     }
-    if (lane == 0) {
-      float ex[8], den = 0.0f;
-      for (int r = 0; r < top_k; ++r) { ex[r] = expf(val[r] - val[0]); den += ex[r]; }
-      for (int r = 0; r < top_k; ++r) {
+    float ex[8], den = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < top_k) { ex[r] = expf(val[r] - val[0]); den += ex[r]; }
+    const long long t = tb + tid;
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < top_k) {
         idx[t * top_k + r] = ids[r];
         gate[t * top_k + r] = ex[r] / den;
       }
-    }
   }
 }
 
@@ -254,39 +251,31 @@ static int stride_grid(long long n, int threads) {
   return (int)(b < cap ? (b > 0 ? b : 1) : cap);
 }
 
-template <int NJ>
-static void launch_router_nj(int slots, dim3 g, dim3 b, cudaStream_t s, const uint16_t* x, long long ldx,
-                             const uint16_t* w0, const uint16_t* w1, long long split, long long tokens, int experts,
-                             int top_k, float* logits, int* idx, float* gate) {
-  switch (slots) {
-    case 1: router_topk_kernel<NJ, 1><<<g, b, 0, s>>>(x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;
-    case 2: router_topk_kernel<NJ, 2><<<g, b, 0, s>>>(x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;
-    case 4: router_topk_kernel<NJ, 4><<<g, b, 0, s>>>(x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;
-    default: router_topk_kernel<NJ, 8><<<g, b, 0, s>>>(x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;
-  }
-}
-
 int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0, const uint16_t* w1, long long split,
                            long long tokens, int hidden, int experts, int top_k, float* logits, int* idx,
                            float* gate, cudaStream_t s) {
   if (top_k < 1 || top_k > 8 || top_k > experts)
     return set_error(ENNX_B200_INVALID_ARGUMENT, "router: top_k must be in [1, min(8, experts)]");  // forward_program.rs:428
   if (experts > 256) return set_error(ENNX_B200_UNSUPPORTED, "router: at most 256 experts");
+  if (hidden <= 0 || hidden % RK) return set_error(ENNX_B200_UNSUPPORTED, "router: hidden %d must be a multiple of %d", hidden, RK);
   if (ldx % 8 || ((uintptr_t)x & 15u) || ((uintptr_t)w0 & 15u) || (w1 && ((uintptr_t)w1 & 15u)))
     return set_error(ENNX_B200_INVALID_ARGUMENT, "router: operands must be 16-byte aligned");
-  int slots = (experts + 31) / 32;
-  slots = slots <= 1 ? 1 : slots <= 2 ? 2 : slots <= 4 ? 4 : 8;
+  if (tokens <= 0) return ENNX_B200_OK;
   if (!w1) { w1 = w0; split = tokens; }
-  long long blocks = (split + kRouterTPB - 1) / kRouterTPB + (tokens - split + kRouterTPB - 1) / kRouterTPB;
-  dim3 g((unsigned)blocks), b(256);
-  switch (hidden) {
-    case 256: launch_router_nj<1>(slots, g, b, s, x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;
-    case 512: launch_router_nj<2>(slots, g, b, s, x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;
-    case 1024: launch_router_nj<4>(slots, g, b, s, x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;
-    case 2048: launch_router_nj<8>(slots, g, b, s, x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;
-    case 4096: launch_router_nj<16>(slots, g, b, s, x, ldx, w0, w1, split, tokens, experts, top_k, logits, idx, gate); break;
-    default: return set_error(ENNX_B200_UNSUPPORTED, "router: hidden %d not in {256,512,1024,2048,4096}", hidden);
+  const long long blocks = (split + RT - 1) / RT + (tokens - split + RT - 1) / RT;
+  const int lds = ((experts + RE - 1) / RE) * RE + 1;
+  const size_t smem = sizeof(float) * (2 * RK * RT + 2 * RK * RE + (size_t)RT * lds);
+  static bool attr[64];
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr[dev]) {
+    ENNX_CUDA(cudaFuncSetAttribute(router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)(sizeof(float) * (2 * RK * RT + 2 * RK * RE + RT * (256 + 1)))),
+              "router smem");
+    attr[dev] = true;
   }
+  router_topk_kernel<<<(unsigned)blocks, kRouterThreads, smem, s>>>(x, ldx, w0, w1, split, tokens, hidden, experts,
+                                                                      top_k, logits, idx, gate);
   ENNX_LAUNCH_CHECK("router_topk");
   return ENNX_B200_OK;
 }

@@ -338,31 +338,19 @@ void eo_rmsnorm(const float* x, const float* w, size_t rows, size_t width, float
     }
 }
 
-/* Router logits with the fixed fp32 reduction tree the CUDA router uses, so
- * that the logits -- and therefore the routing indices -- are bit-identical.
- * Lane l of 32 owns elements {256*j + 8*l + u}; it runs a serial fmaf chain
- * over j then u; the 32 partials are combined by an xor butterfly with
- * offsets 16, 8, 4, 2, 1.  The math is kda_moe.metal:585-595. */
+/* Router logits: one serial fmaf chain per (token, expert) over the hidden
+ * index 0..H-1 starting from 0, the loop order of kda_moe.metal:589-595
+ * (score += input * weight, contracted to a fused multiply-add).  The CUDA
+ * router keeps exactly this order, so the logits -- and therefore the routing
+ * indices -- are bit-identical. */
 void eo_router_logits(const uint16_t* x, const uint16_t* w, size_t tokens, size_t hidden,
                       size_t experts, float* logits) {
     for (size_t t = 0; t < tokens; ++t) {
         for (size_t e = 0; e < experts; ++e) {
-            float p[32];
-            for (int l = 0; l < 32; ++l) {
-                float acc = 0.0f;
-                for (size_t j = 0; j < hidden / 256; ++j)
-                    for (int u = 0; u < 8; ++u) {
-                        size_t i = 256 * j + 8 * (size_t)l + (size_t)u;
-                        acc = fmaf(eo_bf16_decode(x[t * hidden + i]), eo_bf16_decode(w[e * hidden + i]), acc);
-                    }
-                p[l] = acc;
-            }
-            for (int off = 16; off >= 1; off >>= 1) {
-                float q[32];
-                for (int l = 0; l < 32; ++l) q[l] = p[l] + p[l ^ off];
-                memcpy(p, q, sizeof(p));
-            }
-            logits[t * experts + e] = p[0];
+            float acc = 0.0f;
+            for (size_t i = 0; i < hidden; ++i)
+                acc = fmaf(eo_bf16_decode(x[t * hidden + i]), eo_bf16_decode(w[e * hidden + i]), acc);
+            logits[t * experts + e] = acc;
         }
     }
 }

@@ -1,4 +1,5 @@
-// kda.cu -- chunked KDA (gated delta rule with per-key-channel decay).
+// kda.cu -- chunked KDA (gated delta rule with per-key-channel decay) on
+// tcgen05 tensor cores.
 //
 // Recurrence (restated from rust/crates/ennx/src/kda_moe.metal:167-225):
 //   S_t = diag(exp g_t) S_{t-1};  u_t = beta_t (v_t - k_t^T S_t);
@@ -11,20 +12,31 @@
 //   O = ((Q o e^Gc) S0 + QK U) / sqrt(dk),  QK[t,s] likewise for s <= t
 //   S_C = diag(e^Gc_C) S0 + (K o e^(Gc_C - Gc))^T U
 // The per-channel exp(Gc_t - Gc_s) is factored through a reference token r
-// (first token of t's 16-token sub-block): both factors stay bounded for
-// s <= t because each step decays by at most e^-5.
+// (first token of t's 16-token block): both factors stay bounded for s <= t
+// because each step decays by at most e^-5.
 //
 // Two kernels:
-//   kda_prep_kernel  -- one CTA per (sequence, head, chunk), all in parallel:
-//     everything that does not depend on the state: Gc, the intra-chunk
-//     products QK and A', T = (I + diag(beta) A')^-1 diag(beta), and the
-//     decay-scaled operands K~ = K o e^Gc, Q~ = Q o e^Gc, K^ = K o e^(Gc_C - Gc).
-//   kda_scan_kernel  -- one CTA per (sequence, head, 32 value columns) walks
-//     the chunks in order with its fp32 state slice resident in shared
-//     memory: X = V - K~ S, U = T X, O = (Q~ S + QK U)/sqrt(dk),
-//     S = e^Gc_C o S + K^^T U.
-// Contractions run on mma.sync m16n8k16 bf16 tensor cores with fp32
-// accumulation; decays, triangular inverses and the state stay fp32.
+//   kda_prep_kernel -- one CTA per (sequence, head, chunk), all in parallel.
+//     Builds, straight from registers, the decay-scaled operands
+//     K~ = K o e^Gc, Q~ = Q o e^Gc, K^ = K o e^(Gc_C - Gc) (to the chunk
+//     record) and, in shared memory, the intra-chunk MMA operands
+//       A   = [Q o e^(Gc - Gc_r); K o e^(Gc - Gc_r)]        (128 x 128)
+//       B_b = K[0 : 16(b+1)] o e^(Gc_{r_b} - Gc)            (block b = 0..3)
+//     and runs the four intra-chunk products D_b = A B_b^T on tcgen05 with
+//     fp32 accumulators in TMEM: rows 0..63 of D_b give QK, rows 64..127
+//     give A', each read for the rows of block b.  Then
+//     T = (I + diag(beta) A')^-1 diag(beta) in fp32 on the CUDA cores.
+//   kda_scan_kernel -- one CTA per (sequence, head) walks the chunks in order
+//     in transposed form, TMEM lane = value column v:
+//       X^T = S^T K~^T, O^T = S^T Q~^T              (one MMA, N = 128)
+//       X^T = V^T - X^T  -> bf16 smem
+//       U^T = X^T T^T                               (MMA)
+//       O^T += U^T QK^T;  S^T = S^T diag(e^Gc_C) + U^T K^   (MMAs)
+//     The fp32 state S^T lives in TMEM for the whole sequence; a bf16 copy
+//     in shared memory is the A operand of the next chunk.  Chunk records
+//     and V tiles arrive by TMA (no multicast) through a producer warp; one
+//     thread issues the MMAs; eight warps do the element-wise steps.
+// Every wait is bounded.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -34,235 +46,287 @@ namespace ennx {
 namespace {
 
 constexpr int C = 64, DK = 128;
-constexpr int LQ = DK + 8;  // padded bf16 row (elements) of [64][128] tiles
-constexpr int LS = C + 8;   // padded bf16 row of [64][64] tiles
-constexpr int LF = C + 1;   // padded fp32 row of [64][64] matrices
-constexpr int SV = 32;      // value columns per scan CTA
-constexpr int LV = SV + 8;  // padded bf16 row of [*][32] tiles
+constexpr int LF = C + 1;  // padded fp32 row of [64][64] matrices
+constexpr float kLog2e = 1.4426950408889634f;
 
-// per-chunk operand record produced by the prep kernel (global memory)
-constexpr size_t kBigElems = 3ull * C * DK;   // K~, Q~, K^   (bf16)
-constexpr size_t kSmallElems = 2ull * C * C;  // T, QK        (bf16)
-constexpr size_t kChunkBytes = (kBigElems + kSmallElems) * 2 + DK * 4;  // + e^Gc_C (fp32)
+// Chunk records (workspace), as three arrays so that each is a plain 2-D
+// tensor for TMA:
+//   BIG   [R * 192][128] bf16 : rows 192r + [0,64) K~, [64,128) Q~, [128,192) K^
+//   SMALL [R * 128][64]  bf16 : rows 128r + [0,64) T diag(beta), [64,128) QK
+//   DEND  [R][128]       fp32 : e^Gc_C
+constexpr size_t kBigRecBytes = 192ull * DK * 2;
+constexpr size_t kSmallRecBytes = 128ull * C * 2;
+constexpr size_t kDendRecBytes = DK * 4;
+constexpr size_t kChunkBytes = kBigRecBytes + kSmallRecBytes + kDendRecBytes;
 
-__device__ __forceinline__ void ldsm_x4(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void ldsm_x4_t(const void* p, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(smem_u32(p)));
-}
-__device__ __forceinline__ void mma16816(float c[4], const uint32_t a[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
-// A fragment (16 x 16) at (m0, k0) of a row-major [m][k] bf16 tile.
-template <int LD>
-__device__ __forceinline__ void frag_a(const uint16_t* base, int m0, int k0, int lane, uint32_t a[4]) {
-  ldsm_x4(base + (m0 + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + k0 + (lane >> 4) * 8, a[0], a[1], a[2], a[3]);
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
-// A fragment (16 x 16) at (m0, k0) of a tile stored transposed, [k][m].
-template <int LD>
-__device__ __forceinline__ void frag_a_t(const uint16_t* base, int m0, int k0, int lane, uint32_t a[4]) {
-  ldsm_x4_t(base + (k0 + (lane & 7) + (lane >> 4) * 8) * LD + m0 + ((lane >> 3) & 1) * 8, a[0], a[1], a[2], a[3]);
+
+// byte offset of the 16-byte chunk `c` (0..7) of row `r` in a 128-byte-swizzled
+// K-major tile (rows of 128 bytes, chunk index XOR row % 8)
+__device__ __forceinline__ uint32_t sw128(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+__device__ __forceinline__ void unpack8(uint4 v, float f[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    f[2 * j] = bf16_to_f32((uint16_t)(w[j] & 0xffffu));
+    f[2 * j + 1] = bf16_to_f32((uint16_t)(w[j] >> 16));
+  }
 }
-// B fragments for n-tiles n0 and n0+8 (k0..k0+15) of a tile stored [n][k].
-template <int LD>
-__device__ __forceinline__ void frag_b_nk(const uint16_t* base, int n0, int k0, int lane, uint32_t b[4]) {
-  ldsm_x4(base + (n0 + (lane & 7) + (lane >> 4) * 8) * LD + k0 + ((lane >> 3) & 1) * 8, b[0], b[1], b[2], b[3]);
-}
-// B fragments for n-tiles n0 and n0+8 of a tile stored [k][n].
-template <int LD>
-__device__ __forceinline__ void frag_b_kn(const uint16_t* base, int n0, int k0, int lane, uint32_t b[4]) {
-  ldsm_x4_t(base + (k0 + (lane & 7) + ((lane >> 3) & 1) * 8) * LD + n0 + (lane >> 4) * 8, b[0], b[1], b[2], b[3]);
+__device__ __forceinline__ uint4 pack8(const float f[8]) {
+  return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                    pack_bf16x2(f[6], f[7]));
 }
 
 // ===========================================================================
 // prep: one CTA per (sequence, head, chunk)
 // ===========================================================================
-struct PrepSmem {
-  float Gc[C][DK];
-  float L[C][LF];         // beta_t A'[t,s] (strict lower); block rows become T rows
-  float Tdiag[4][16][17]; // inverses of the 16x16 diagonal blocks of I + L
-  float beta[C];
-  uint16_t q[C][LQ], k[C][LQ];
-  uint16_t X[32][LQ], Y[C][LQ];
-};
+constexpr int PREP_THREADS = 256;
+constexpr int P_XA = 0;                    // A operand, 2 sub-tiles of 128 rows x 128 B
+constexpr int P_YB = 32768;                // B_b operands, 16(b+1) rows each, 2 sub-tiles
+constexpr int P_GC = P_YB + 40960;         // fp32 [64][128] cumulative log2 decay
+constexpr int P_FB = P_GC + C * DK * 4;    // fp32 [4][128] block-to-block decay factors
+constexpr int P_BETA = P_FB + 4 * DK * 4;  // fp32 [64]
+constexpr int P_BAR = P_BETA + C * 4;      // mbarrier + TMEM slot
+constexpr int PREP_SMEM = P_BAR + 64 + 1024;
+// after the MMAs complete, the A operand region holds L and the diagonal inverses
+constexpr int P_L = P_XA;
+constexpr int P_TD = P_XA + C * LF * 4;
+static_assert(P_TD + 4 * 16 * 17 * 4 <= P_YB, "L and diagonal inverses must fit the A operand region");
+
+__host__ __device__ constexpr int yb_off(int b) { return P_YB + 4096 * (b * (b + 1) / 2); }
+__host__ __device__ constexpr int yb_rows(int b) { return 16 * (b + 1); }
+__host__ __device__ constexpr int d_col(int b) { return 8 * b * (b + 1); }  // TMEM column of D_b
 
 __device__ __forceinline__ float softplus_stable(float x) { return fmaxf(x, 0.0f) + log1pf(__expf(-fabsf(x))); }
 
-__global__ void __launch_bounds__(256) kda_prep_kernel(const uint16_t* __restrict__ qg, const uint16_t* __restrict__ kg,
-                                                       long long ld, const float* __restrict__ gg, long long ldg,
-                                                       const float* __restrict__ bg, int seq, int heads, int nchunks,
-                                                       KdaRawGate raw, uint8_t* __restrict__ ops) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  PrepSmem& s = *reinterpret_cast<PrepSmem*>(smem_raw);
+__global__ void __launch_bounds__(PREP_THREADS, 2)
+    kda_prep_kernel(const uint16_t* __restrict__ qg, const uint16_t* __restrict__ kg, long long ld,
+                    const float* __restrict__ gg, long long ldg, const float* __restrict__ bg, int seq, int heads,
+                    int nchunks, KdaRawGate raw, uint16_t* __restrict__ big, uint16_t* __restrict__ small,
+                    float* __restrict__ dend, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  float(*Gc)[DK] = reinterpret_cast<float(*)[DK]>(sm + P_GC);
+  float(*fb)[DK] = reinterpret_cast<float(*)[DK]>(sm + P_FB);
+  float* beta = reinterpret_cast<float*>(sm + P_BETA);
+  uint64_t* mma_done = reinterpret_cast<uint64_t*>(sm + P_BAR);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm + P_BAR + 8);
+
   const int ch = blockIdx.x, bh = blockIdx.y, b = bh / heads, h = bh % heads;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const long long tok0 = (long long)b * seq;
   const int t0 = ch * C;
-  uint8_t* rec = ops + ((size_t)bh * nchunks + ch) * kChunkBytes;
-  uint16_t* big = reinterpret_cast<uint16_t*>(rec);
-  uint16_t* small = big + kBigElems;
-  float* dend = reinterpret_cast<float*>(small + kSmallElems);
+  const size_t rec = (size_t)bh * nchunks + ch;
+  uint16_t* bigr = big + rec * (192 * DK);
+  uint16_t* smallr = small + rec * (128 * C);
 
-  // ---- loads (independent 16-byte loads from every thread) ----
-  for (int i = tid; i < C * (DK / 8); i += 256) {
-    int r = i / (DK / 8), c = (i % (DK / 8)) * 8;
-    uint4 qv = make_uint4(0, 0, 0, 0), kv = qv;
-    if (t0 + r < seq) {
-      long long off = (tok0 + t0 + r) * ld + h * DK + c;
-      qv = *reinterpret_cast<const uint4*>(qg + off);
-      kv = *reinterpret_cast<const uint4*>(kg + off);
-    }
-    *reinterpret_cast<uint4*>(&s.q[r][c]) = qv;
-    *reinterpret_cast<uint4*>(&s.k[r][c]) = kv;
+  if (tid == 0) {
+    mbar_init(mma_done, 1);
+    fence_barrier_init();
   }
+  if (warp == 0) { tmem_alloc(tmem_slot, 256); tmem_relinquish(); }
+
+  // ---- gates: log2 decay per (token, channel) and beta ----
   if (raw.active) {
-    // forward path: g = max(-exp(decay_h) * softplus(f + time_bias), -5) and
-    // beta = sigmoid(raw beta) from the raw projections (kda_moe.metal:869-895)
+    // g = max(-exp(decay_h) * softplus(f + time_bias), -5) and beta =
+    // sigmoid(raw beta) from the raw projections (kda_moe.metal:869-895)
     const bool set0 = b < raw.split_seq;
     const uint16_t* tb = set0 ? raw.tb0 : raw.tb1;
     const float dscale = __expf(bf16_to_f32((set0 ? raw.decay0 : raw.decay1)[h]));
-    for (int i = tid; i < C * (DK / 8); i += 256) {
-      int r = i / (DK / 8), c = (i % (DK / 8)) * 8;
+    for (int i = tid; i < C * (DK / 8); i += PREP_THREADS) {
+      const int r = i >> 4, c = (i & 15) * 8;
       float gv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       if (t0 + r < seq) {
-        uint4 fv = *reinterpret_cast<const uint4*>(raw.f + (tok0 + t0 + r) * raw.ldf + h * DK + c);
-        uint4 bv = *reinterpret_cast<const uint4*>(tb + h * DK + c);
-        uint32_t fw[4] = {fv.x, fv.y, fv.z, fv.w}, bw[4] = {bv.x, bv.y, bv.z, bv.w};
+        float fv[8], bv[8];
+        unpack8(*reinterpret_cast<const uint4*>(raw.f + (tok0 + t0 + r) * raw.ldf + h * DK + c), fv);
+        unpack8(*reinterpret_cast<const uint4*>(tb + h * DK + c), bv);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          float x = bf16_to_f32((uint16_t)(fw[j >> 1] >> (16 * (j & 1)))) +
-                    bf16_to_f32((uint16_t)(bw[j >> 1] >> (16 * (j & 1))));
-          gv[j] = fmaxf(-dscale * softplus_stable(x), -5.0f);
-        }
+        for (int j = 0; j < 8; ++j) gv[j] = fmaxf(-dscale * softplus_stable(fv[j] + bv[j]), -5.0f) * kLog2e;
       }
-      *reinterpret_cast<float4*>(&s.Gc[r][c]) = make_float4(gv[0], gv[1], gv[2], gv[3]);
-      *reinterpret_cast<float4*>(&s.Gc[r][c + 4]) = make_float4(gv[4], gv[5], gv[6], gv[7]);
+      *reinterpret_cast<float4*>(&Gc[r][c]) = make_float4(gv[0], gv[1], gv[2], gv[3]);
+      *reinterpret_cast<float4*>(&Gc[r][c + 4]) = make_float4(gv[4], gv[5], gv[6], gv[7]);
     }
     if (tid < C)
-      s.beta[tid] = t0 + tid < seq
-                        ? 1.0f / (1.0f + __expf(-bf16_to_f32(raw.rbeta[(tok0 + t0 + tid) * raw.ldb + h])))
-                        : 0.0f;
-    __syncthreads();
-    // per-token L2 normalisation of q and k, 1/max(|x|, 1e-6) (kda_moe.metal:510-534)
-    for (int r = warp; r < 2 * C; r += 8) {
-      uint16_t* row = r < C ? &s.q[r][0] : &s.k[r - C][0];
-      uint2 rv = *reinterpret_cast<uint2*>(row + lane * 4);
-      float f[4] = {bf16_to_f32(rv.x & 0xffffu), bf16_to_f32(rv.x >> 16), bf16_to_f32(rv.y & 0xffffu),
-                    bf16_to_f32(rv.y >> 16)};
-      float ss = f[0] * f[0] + f[1] * f[1] + f[2] * f[2] + f[3] * f[3];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-      float inv = 1.0f / fmaxf(sqrtf(ss), 1e-6f);
-      *reinterpret_cast<uint2*>(row + lane * 4) =
-          make_uint2(pack_bf16x2(f[0] * inv, f[1] * inv), pack_bf16x2(f[2] * inv, f[3] * inv));
-    }
+      beta[tid] = t0 + tid < seq ? 1.0f / (1.0f + __expf(-bf16_to_f32(raw.rbeta[(tok0 + t0 + tid) * raw.ldb + h])))
+                                 : 0.0f;
   } else {
-    for (int i = tid; i < C * (DK / 4); i += 256) {
-      int r = i / (DK / 4), c = (i % (DK / 4)) * 4;
+    for (int i = tid; i < C * (DK / 4); i += PREP_THREADS) {
+      const int r = i >> 5, c = (i & 31) * 4;
       float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
       if (t0 + r < seq) gv = *reinterpret_cast<const float4*>(gg + (tok0 + t0 + r) * ldg + h * DK + c);
-      *reinterpret_cast<float4*>(&s.Gc[r][c]) = gv;
+      *reinterpret_cast<float4*>(&Gc[r][c]) =
+          make_float4(gv.x * kLog2e, gv.y * kLog2e, gv.z * kLog2e, gv.w * kLog2e);
     }
-    if (tid < C) s.beta[tid] = t0 + tid < seq ? bg[(tok0 + t0 + tid) * heads + h] : 0.0f;
+    if (tid < C) beta[tid] = t0 + tid < seq ? bg[(tok0 + t0 + tid) * heads + h] : 0.0f;
   }
   __syncthreads();
-  if (tid < DK) {  // inclusive prefix sum of the log decay per key channel
-    float acc = 0.0f;
-#pragma unroll 8
-    for (int t = 0; t < C; ++t) {
-      acc += s.Gc[t][tid];
-      s.Gc[t][tid] = acc;
+  // ---- inclusive prefix over the chunk's tokens per channel: thread
+  // (channel, half) scans 32 tokens, the upper half then adds the lower total
+  {
+    const int c = tid & 127, half = tid >> 7;
+    float v[32];
+#pragma unroll
+    for (int t = 0; t < 32; ++t) v[t] = Gc[half * 32 + t][c];
+#pragma unroll
+    for (int t = 1; t < 32; ++t) v[t] += v[t - 1];
+    if (half == 0) {
+#pragma unroll
+      for (int t = 0; t < 32; ++t) Gc[t][c] = v[t];
     }
+    __syncthreads();
+    if (half == 1) {
+      const float base = Gc[31][c];
+#pragma unroll
+      for (int t = 0; t < 32; ++t) Gc[32 + t][c] = v[t] + base;
+    }
+    __syncthreads();
+  }
+  if (tid < DK) {
+    dend[rec * DK + tid] = ex2(Gc[C - 1][tid]);
+#pragma unroll
+    for (int bb = 1; bb < 4; ++bb) fb[bb][tid] = ex2(Gc[16 * bb][tid] - Gc[16 * (bb - 1)][tid]);
   }
   __syncthreads();
 
-  // ---- decay-scaled operands straight to global (K~, Q~, K^, e^Gc_C) ----
-  for (int i = tid; i < C * (DK / 8); i += 256) {
-    int t = i / (DK / 8), c = (i % (DK / 8)) * 8;
-    uint32_t ks[4], qs[4], ke[4];
+  // ---- operands: a half-warp per token row, one 8-channel chunk per lane ----
+  for (int it = 0; it < C * 16 / PREP_THREADS; ++it) {
+    const int t = it * (PREP_THREADS / 16) + (tid >> 4), cc = tid & 15, c0 = cc * 8;
+    const int blk = t >> 4, r = blk * 16;
+    float q[8], k[8];
+    if (t0 + t < seq) {
+      unpack8(*reinterpret_cast<const uint4*>(qg + (tok0 + t0 + t) * ld + h * DK + c0), q);
+      unpack8(*reinterpret_cast<const uint4*>(kg + (tok0 + t0 + t) * ld + h * DK + c0), k);
+    } else {
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float e0 = __expf(s.Gc[t][c + 2 * j]), e1 = __expf(s.Gc[t][c + 2 * j + 1]);
-      float d0 = __expf(s.Gc[C - 1][c + 2 * j] - s.Gc[t][c + 2 * j]);
-      float d1 = __expf(s.Gc[C - 1][c + 2 * j + 1] - s.Gc[t][c + 2 * j + 1]);
-      float k0 = bf16_to_f32(s.k[t][c + 2 * j]), k1 = bf16_to_f32(s.k[t][c + 2 * j + 1]);
-      float q0 = bf16_to_f32(s.q[t][c + 2 * j]), q1 = bf16_to_f32(s.q[t][c + 2 * j + 1]);
-      ks[j] = pack_bf16x2(k0 * e0, k1 * e1);
-      qs[j] = pack_bf16x2(q0 * e0, q1 * e1);
-      ke[j] = pack_bf16x2(k0 * d0, k1 * d1);
+      for (int j = 0; j < 8; ++j) q[j] = k[j] = 0.0f;
     }
-    *reinterpret_cast<uint4*>(big + t * DK + c) = make_uint4(ks[0], ks[1], ks[2], ks[3]);
-    *reinterpret_cast<uint4*>(big + C * DK + t * DK + c) = make_uint4(qs[0], qs[1], qs[2], qs[3]);
-    *reinterpret_cast<uint4*>(big + 2 * C * DK + t * DK + c) = make_uint4(ke[0], ke[1], ke[2], ke[3]);
-  }
-  if (tid < DK) dend[tid] = __expf(s.Gc[C - 1][tid]);
-
-  // ---- intra-chunk products, one 16-row block at a time ----
-  uint16_t* QKg = small + C * C;
-  for (int blk = 0; blk < 4; ++blk) {
-    const int r = blk * 16, ns = r + 16;
-    __syncthreads();
-    for (int i = tid; i < 32 * DK; i += 256) {  // X rows: 16 q-scaled, 16 k-scaled
-      int row = i / DK, c = i % DK;
-      int t = r + (row & 15);
-      float e = __expf(s.Gc[t][c] - s.Gc[r][c]);
-      float src = bf16_to_f32(row < 16 ? s.q[t][c] : s.k[t][c]);
-      s.X[row][c] = f32_to_bf16_rne(src * e);
-    }
-    for (int i = tid; i < ns * DK; i += 256) {
-      int t = i / DK, c = i % DK;
-      s.Y[t][c] = f32_to_bf16_rne(bf16_to_f32(s.k[t][c]) * __expf(s.Gc[r][c] - s.Gc[t][c]));
-    }
-    __syncthreads();
-    const int npairs = ns / 16;
-    for (int task = warp; task < 2 * npairs; task += 8) {
-      const int which = task / npairs;  // 0: QK, 1: A'
-      const int n0 = (task % npairs) * 16;
-      float acc[2][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}};
+    if (raw.active) {
+      // per-token L2 normalisation, 1/max(|x|, 1e-6), rounded to bf16 (kda_moe.metal:510-534)
+      float sq = 0.0f, sk = 0.0f;
 #pragma unroll
-      for (int kk = 0; kk < DK; kk += 16) {
-        uint32_t a[4], bb[4];
-        frag_a<LQ>(&s.X[0][0], which * 16, kk, lane, a);
-        frag_b_nk<LQ>(&s.Y[0][0], n0, kk, lane, bb);
-        mma16816(acc[0], a, bb[0], bb[1]);
-        mma16816(acc[1], a, bb[2], bb[3]);
+      for (int j = 0; j < 8; ++j) { sq += q[j] * q[j]; sk += k[j] * k[j]; }
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) {
+        sq += __shfl_xor_sync(0xffffffffu, sq, o);
+        sk += __shfl_xor_sync(0xffffffffu, sk, o);
       }
+      const float iq = 1.0f / fmaxf(sqrtf(sq), 1e-6f), ik = 1.0f / fmaxf(sqrtf(sk), 1e-6f);
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          int t = r + (lane >> 2) + (e >> 1) * 8;
-          int sc = n0 + nt * 8 + (lane & 3) * 2;
-          float x0 = acc[nt][e], x1 = acc[nt][e + 1];
-          if (which == 0) {
-            *reinterpret_cast<uint32_t*>(QKg + t * C + sc) =
-                pack_bf16x2(sc <= t ? x0 : 0.0f, sc + 1 <= t ? x1 : 0.0f);
-          } else {
-            s.L[t][sc] = sc < t ? s.beta[t] * x0 : 0.0f;
-            s.L[t][sc + 1] = sc + 1 < t ? s.beta[t] * x1 : 0.0f;
-          }
-        }
+      for (int j = 0; j < 8; ++j) {
+        q[j] = bf16_to_f32(f32_to_bf16_rne(q[j] * iq));
+        k[j] = bf16_to_f32(f32_to_bf16_rne(k[j] * ik));
+      }
     }
-    for (int i = tid; i < 16 * (C - ns); i += 256) {  // zero right of the computed columns
-      int t = r + i / (C - ns), sc = ns + i % (C - ns);
-      QKg[t * C + sc] = 0;
-      s.L[t][sc] = 0.0f;
+    float gt[8], gr[8], gC[8];
+    *reinterpret_cast<float4*>(gt) = *reinterpret_cast<const float4*>(&Gc[t][c0]);
+    *reinterpret_cast<float4*>(gt + 4) = *reinterpret_cast<const float4*>(&Gc[t][c0 + 4]);
+    *reinterpret_cast<float4*>(gr) = *reinterpret_cast<const float4*>(&Gc[r][c0]);
+    *reinterpret_cast<float4*>(gr + 4) = *reinterpret_cast<const float4*>(&Gc[r][c0 + 4]);
+    *reinterpret_cast<float4*>(gC) = *reinterpret_cast<const float4*>(&Gc[C - 1][c0]);
+    *reinterpret_cast<float4*>(gC + 4) = *reinterpret_cast<const float4*>(&Gc[C - 1][c0 + 4]);
+    float ks[8], qs[8], ke[8], xq[8], xk[8], y[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float e = ex2(gt[j]);
+      ks[j] = k[j] * e;
+      qs[j] = q[j] * e;
+      ke[j] = k[j] * ex2(gC[j] - gt[j]);
+      const float x = ex2(gt[j] - gr[j]);
+      xq[j] = q[j] * x;
+      xk[j] = k[j] * x;
+      y[j] = k[j] * ex2(gr[j] - gt[j]);
+    }
+    *reinterpret_cast<uint4*>(bigr + (size_t)t * DK + c0) = pack8(ks);
+    *reinterpret_cast<uint4*>(bigr + (size_t)(64 + t) * DK + c0) = pack8(qs);
+    *reinterpret_cast<uint4*>(bigr + (size_t)(128 + t) * DK + c0) = pack8(ke);
+    const int sub = cc >> 3, chk = cc & 7;
+    *reinterpret_cast<uint4*>(sm + P_XA + sub * 16384 + sw128(t, chk)) = pack8(xq);
+    *reinterpret_cast<uint4*>(sm + P_XA + sub * 16384 + sw128(64 + t, chk)) = pack8(xk);
+#pragma unroll
+    for (int bb = 0; bb < 4; ++bb) {
+      if (bb < blk) continue;
+      if (bb > blk) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) y[j] *= fb[bb][c0 + j];
+      }
+      *reinterpret_cast<uint4*>(sm + yb_off(bb) + sub * (yb_rows(bb) * 128) + sw128(t, chk)) = pack8(y);
     }
   }
+  fence_proxy_async();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  if (tid == 0) {
+    const uint32_t xa = smem_u32(sm + P_XA);
+#pragma unroll
+    for (int bb = 0; bb < 4; ++bb) {
+      const uint32_t yb = smem_u32(sm + yb_off(bb));
+      const uint32_t idesc = idesc_bf16_f32(128, yb_rows(bb));
+#pragma unroll
+      for (int kk = 0; kk < DK / 16; ++kk)
+        umma_f16(tmem + d_col(bb), smem_desc_sw128(xa + (kk >> 2) * 16384 + (kk & 3) * 32),
+                 smem_desc_sw128(yb + (kk >> 2) * (yb_rows(bb) * 128) + (kk & 3) * 32), idesc, kk != 0);
+    }
+    umma_commit(mma_done);
+  }
+  const bool ok = mbar_wait(mma_done, 0, err);
+  tc_fence_after();
+
+  // ---- read D_b: warp w reads TMEM lanes 32(w%4).., block 2((w%4)&1) + w/4 ----
+  float(*L)[LF] = reinterpret_cast<float(*)[LF]>(sm + P_L);
+  float(*Td)[16][17] = reinterpret_cast<float(*)[16][17]>(sm + P_TD);
+  {
+    const int qd = warp & 3, R = qd * 32 + lane;
+    const int bl = 2 * (qd & 1) + (warp >> 2);
+    const int t = R & 63;
+    const bool mine = (t >> 4) == bl;
+    const bool is_qk = R < 64;
+    const int n = yb_rows(bl);
+    float row[64];
+#pragma unroll
+    for (int s = 0; s < 64; ++s) row[s] = 0.0f;
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      if (p * 32 < n) {  // warp-uniform
+        uint32_t v[32];
+        tmem_ld32(tmem + ((uint32_t)(qd * 32) << 16) + d_col(bl) + p * 32, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          if (p * 32 + i < n) row[p * 32 + i] = ok ? __uint_as_float(v[i]) : 0.0f;
+      }
+    }
+    if (mine) {
+      if (is_qk) {
+        uint16_t* dst = smallr + (size_t)(64 + t) * C;
+#pragma unroll
+        for (int g = 0; g < 8; ++g) {
+          float f[8];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) f[j] = (8 * g + j <= t) ? row[8 * g + j] : 0.0f;
+          *reinterpret_cast<uint4*>(dst + 8 * g) = pack8(f);
+        }
+      } else {
+        const float bt = beta[t];
+#pragma unroll
+        for (int s = 0; s < 64; ++s) L[t][s] = s < t ? bt * row[s] : 0.0f;
+      }
+    }
+  }
+  tc_fence_before();
   __syncthreads();
 
   // ---- T = (I + L)^-1: 16x16 diagonal inverses, then block rows in order ----
@@ -273,11 +337,11 @@ __global__ void __launch_bounds__(256) kda_prep_kernel(const uint16_t* __restric
     for (int t = 0; t < 16; ++t) {
       float v = (t == jj) ? 1.0f : 0.0f;
 #pragma unroll
-      for (int u = 0; u < t; ++u) v -= s.L[d0 + t][d0 + u] * x[u];
+      for (int u = 0; u < t; ++u) v -= L[d0 + t][d0 + u] * x[u];
       x[t] = v;
     }
 #pragma unroll
-    for (int t = 0; t < 16; ++t) s.Tdiag[warp][t][jj] = x[t];
+    for (int t = 0; t < 16; ++t) Td[warp][t][jj] = x[t];
   }
   __syncthreads();
   // block row bi of T (bj < bi): T_ij = -T_ii sum_{k=j}^{i-1} L_ik T_kj.  Rows
@@ -287,14 +351,14 @@ __global__ void __launch_bounds__(256) kda_prep_kernel(const uint16_t* __restric
     const int n = bi * 256;
 #pragma unroll
     for (int q = 0; q < 3; ++q) {
-      int i = tid + q * 256;
+      const int i = tid + q * 256;
       mval[q] = 0.0f;
       if (i < n) {
-        int bj = i / 256, e = i % 256, rr = e / 16, cc = e % 16;
+        const int bj = i / 256, e = i % 256, rr = e / 16, c2 = e % 16;
         float acc = 0.0f;
         for (int kx = bj * 16; kx < bi * 16; ++kx) {
-          float tkj = (kx < (bj + 1) * 16) ? s.Tdiag[bj][kx - bj * 16][cc] : s.L[kx][bj * 16 + cc];
-          acc += s.L[bi * 16 + rr][kx] * tkj;
+          const float tkj = (kx < (bj + 1) * 16) ? Td[bj][kx - bj * 16][c2] : L[kx][bj * 16 + c2];
+          acc += L[bi * 16 + rr][kx] * tkj;
         }
         mval[q] = acc;
       }
@@ -302,232 +366,319 @@ __global__ void __launch_bounds__(256) kda_prep_kernel(const uint16_t* __restric
     __syncthreads();
 #pragma unroll
     for (int q = 0; q < 3; ++q) {
-      int i = tid + q * 256;
+      const int i = tid + q * 256;
       if (i < n) {
-        int bj = i / 256, e = i % 256, rr = e / 16, cc = e % 16;
-        s.L[bi * 16 + rr][bj * 16 + cc] = mval[q];  // M_ij, temporarily
+        const int bj = i / 256, e = i % 256, rr = e / 16, c2 = e % 16;
+        L[bi * 16 + rr][bj * 16 + c2] = mval[q];  // M_ij, temporarily
       }
     }
     __syncthreads();
 #pragma unroll
     for (int q = 0; q < 3; ++q) {
-      int i = tid + q * 256;
+      const int i = tid + q * 256;
       mval[q] = 0.0f;
       if (i < n) {
-        int bj = i / 256, e = i % 256, rr = e / 16, cc = e % 16;
+        const int bj = i / 256, e = i % 256, rr = e / 16, c2 = e % 16;
         float acc = 0.0f;
 #pragma unroll 4
-        for (int kx = 0; kx < 16; ++kx) acc -= s.Tdiag[bi][rr][kx] * s.L[bi * 16 + kx][bj * 16 + cc];
+        for (int kx = 0; kx < 16; ++kx) acc -= Td[bi][rr][kx] * L[bi * 16 + kx][bj * 16 + c2];
         mval[q] = acc;
       }
     }
     __syncthreads();
 #pragma unroll
     for (int q = 0; q < 3; ++q) {
-      int i = tid + q * 256;
+      const int i = tid + q * 256;
       if (i < n) {
-        int bj = i / 256, e = i % 256, rr = e / 16, cc = e % 16;
-        s.L[bi * 16 + rr][bj * 16 + cc] = mval[q];
+        const int bj = i / 256, e = i % 256, rr = e / 16, c2 = e % 16;
+        L[bi * 16 + rr][bj * 16 + c2] = mval[q];
       }
     }
     __syncthreads();
   }
-  // T diag(beta) -> global (lower incl. diagonal)
-  uint16_t* Tg = small;
-  for (int i = tid; i < C * C / 2; i += 256) {
-    int rr = (2 * i) / C, cc = (2 * i) % C;
-    float v[2];
+  // T diag(beta) -> record (lower triangle incl. diagonal), 8 columns per thread
+  for (int i = tid; i < C * C / 8; i += PREP_THREADS) {
+    const int rr = i >> 3, c0 = (i & 7) * 8;
+    float f[8];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-      int c2 = cc + u;
+    for (int u = 0; u < 8; ++u) {
+      const int c2 = c0 + u;
       float tv = 0.0f;
-      if (c2 <= rr) tv = (c2 >> 4) == (rr >> 4) ? s.Tdiag[rr >> 4][rr & 15][c2 & 15] : s.L[rr][c2];
-      v[u] = tv * s.beta[c2];
+      if (c2 <= rr) tv = (c2 >> 4) == (rr >> 4) ? Td[rr >> 4][rr & 15][c2 & 15] : L[rr][c2];
+      f[u] = tv * beta[c2];
     }
-    *reinterpret_cast<uint32_t*>(Tg + rr * C + cc) = pack_bf16x2(v[0], v[1]);
+    *reinterpret_cast<uint4*>(smallr + (size_t)rr * C + c0) = pack8(f);
+  }
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
   }
 }
 
 // ===========================================================================
-// scan: one CTA per (sequence, head, 32 value columns), chunks in order
+// scan: one CTA per (sequence, head), chunks in order, state in TMEM
 // ===========================================================================
-struct ScanSmem {
-  float Sf[DK][SV];      // state slice, fp32 master
-  float dend[DK];
-  uint16_t Sb[DK][LV];   // bf16 copy of the state slice
-  uint16_t Ks[C][LQ], Qs[C][LQ], Ke[C][LQ];
-  uint16_t T[C][LS], QK[C][LS];
-  uint16_t V[C][LV], XU[C][LV];
+constexpr int SCAN_THREADS = 320;  // producer, MMA, 8 element-wise warps
+constexpr int S_SB = 0;                 // bf16 state copy S^T [v][i], 2 sub-tiles of 16 KB
+constexpr int S_XS = 32768;             // X^T [v][t] bf16, one sub-tile
+constexpr int S_US = S_XS + 16384;      // U^T [v][t] bf16
+constexpr int S_KQ = S_US + 16384;      // [K~; Q~] as B (128 rows), 2 sub-tiles, x2 buffers
+constexpr int S_KE = S_KQ + 2 * 32768;  // K^ [t][i] MN-major B, 2 blocks of 8 KB
+constexpr int S_TT = S_KE + 16384;      // T [t][s]
+constexpr int S_QK = S_TT + 8192;       // QK [t][s]
+constexpr int S_V = S_QK + 8192;        // V [t][v] plain row-major
+constexpr int S_D = S_V + 16384;        // e^Gc_C, fp32 [128]
+constexpr int S_BAR = S_D + 512;
+constexpr int SCAN_SMEM = S_BAR + 256 + 1024;
+constexpr uint32_t IDESC_N128 = idesc_bf16_f32(128, 128);
+constexpr uint32_t IDESC_N64 = idesc_bf16_f32(128, 64);
+constexpr uint32_t IDESC_N128_BMN = idesc_bf16_f32(128, 128) | (1u << 16);  // B MN-major
+// TMEM columns
+constexpr uint32_t TM_X = 0, TM_O = 64, TM_U = 128, TM_S = 256;
+
+struct ScanBars {
+  uint64_t kq_full[2], kq_free[2], t_full, t_free, m3_full, m3_free, v_full, v_free;
+  uint64_t s_ready, x_full, xs_ready, u_full, us_ready, o_full;
+  uint32_t tmem_base;
+  int abort_flag;
 };
 
-__global__ void __launch_bounds__(128) kda_scan_kernel(const uint16_t* __restrict__ vg, long long ld,
-                                                       const uint8_t* __restrict__ ops, float* __restrict__ state,
-                                                       uint16_t* __restrict__ og, long long ldo, int seq, int heads,
-                                                       int nchunks) {
-  extern __shared__ __align__(16) uint8_t smem_raw[];
-  ScanSmem& s = *reinterpret_cast<ScanSmem*>(smem_raw);
-  // the value slices of one (sequence, head) are adjacent block indices, so
-  // they run together and share the chunk records through L2
-  const int bh = blockIdx.y, b = bh / heads, h = bh % heads;
-  const int j0 = blockIdx.x * SV;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+__global__ void __launch_bounds__(SCAN_THREADS, 1)
+    kda_scan_kernel(const __grid_constant__ CUtensorMap tmBig, const __grid_constant__ CUtensorMap tmSmall,
+                    const __grid_constant__ CUtensorMap tmV, const float* __restrict__ dend,
+                    float* __restrict__ state, uint16_t* __restrict__ og, long long ldo, int seq, int heads,
+                    int nchunks, int* err) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* sm = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  ScanBars& bar = *reinterpret_cast<ScanBars*>(sm + S_BAR);
+  const int bh = blockIdx.x, b = bh / heads, h = bh % heads;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const long long tok0 = (long long)b * seq;
-  const float qscale = rsqrtf((float)DK);
-  float* st_g = state ? state + (long long)bh * DK * DK : nullptr;
 
-  for (int i = tid; i < DK * SV; i += 128) {
-    int r = i / SV, c = i % SV;
-    float x = st_g ? st_g[r * DK + j0 + c] : 0.0f;
-    s.Sf[r][c] = x;
-    s.Sb[r][c] = f32_to_bf16_rne(x);
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) { mbar_init(&bar.kq_full[i], 1); mbar_init(&bar.kq_free[i], 1); }
+    mbar_init(&bar.t_full, 1); mbar_init(&bar.t_free, 1);
+    mbar_init(&bar.m3_full, 1); mbar_init(&bar.m3_free, 1);
+    mbar_init(&bar.v_full, 1); mbar_init(&bar.v_free, 8);
+    mbar_init(&bar.s_ready, 8); mbar_init(&bar.x_full, 1); mbar_init(&bar.xs_ready, 8);
+    mbar_init(&bar.u_full, 1); mbar_init(&bar.us_ready, 8); mbar_init(&bar.o_full, 1);
+    bar.abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async();
   }
+  if (warp == 1) { tmem_alloc(&bar.tmem_base, 512); tmem_relinquish(); }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = bar.tmem_base;
+  volatile int* abort_flag = &bar.abort_flag;
 
-  const int m0 = warp * 16;  // token rows of this warp for X, U, O
-  for (int ch = 0; ch < nchunks; ++ch) {
-    const int t0 = ch * C;
-    const uint8_t* rec = ops + ((size_t)bh * nchunks + ch) * kChunkBytes;
-    const uint16_t* big = reinterpret_cast<const uint16_t*>(rec);
-    const uint16_t* small = big + kBigElems;
-    const float* dend = reinterpret_cast<const float*>(small + kSmallElems);
-    __syncthreads();  // previous chunk done with every buffer
-    for (int i = tid; i < 3 * C * (DK / 8); i += 128) {
-      int m = i / (C * (DK / 8)), rem = i % (C * (DK / 8));
-      int r = rem / (DK / 8), c = (rem % (DK / 8)) * 8;
-      uint16_t* dst = m == 0 ? &s.Ks[r][c] : m == 1 ? &s.Qs[r][c] : &s.Ke[r][c];
-      cp_async16(dst, big + (size_t)m * C * DK + r * DK + c);
-    }
-    for (int i = tid; i < 2 * C * (C / 8); i += 128) {
-      int m = i / (C * (C / 8)), rem = i % (C * (C / 8));
-      int r = rem / (C / 8), c = (rem % (C / 8)) * 8;
-      cp_async16(m == 0 ? &s.T[r][c] : &s.QK[r][c], small + (size_t)m * C * C + r * C + c);
-    }
-    for (int i = tid; i < C * (SV / 8); i += 128) {
-      int r = i / (SV / 8), c = (i % (SV / 8)) * 8;
-      if (t0 + r < seq) cp_async16(&s.V[r][c], vg + (tok0 + t0 + r) * ld + h * DK + j0 + c);
-      else *reinterpret_cast<uint4*>(&s.V[r][c]) = make_uint4(0, 0, 0, 0);
-    }
-    for (int i = tid; i < DK / 4; i += 128) cp_async16(&s.dend[4 * i], dend + 4 * i);
-    cp_async_wait_all();
-    __syncthreads();
-
-    // X = V - K~ S and O1 = Q~ S for this warp's 16 rows x 32 columns
-    float xacc[4][4], oacc[4][4];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) xacc[nt][e] = oacc[nt][e] = 0.0f;
-#pragma unroll
-    for (int kk = 0; kk < DK; kk += 16) {
-      uint32_t ak[4], aq[4], b0[4], b1[4];
-      frag_a<LQ>(&s.Ks[0][0], m0, kk, lane, ak);
-      frag_a<LQ>(&s.Qs[0][0], m0, kk, lane, aq);
-      frag_b_kn<LV>(&s.Sb[0][0], 0, kk, lane, b0);
-      frag_b_kn<LV>(&s.Sb[0][0], 16, kk, lane, b1);
-      mma16816(xacc[0], ak, b0[0], b0[1]);
-      mma16816(xacc[1], ak, b0[2], b0[3]);
-      mma16816(xacc[2], ak, b1[0], b1[1]);
-      mma16816(xacc[3], ak, b1[2], b1[3]);
-      mma16816(oacc[0], aq, b0[0], b0[1]);
-      mma16816(oacc[1], aq, b0[2], b0[3]);
-      mma16816(oacc[2], aq, b1[0], b1[1]);
-      mma16816(oacc[3], aq, b1[2], b1[3]);
-    }
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int t = m0 + (lane >> 2) + (e >> 1) * 8;
-        int c = nt * 8 + (lane & 3) * 2;
-        uint32_t raw = *reinterpret_cast<const uint32_t*>(&s.V[t][c]);
-        *reinterpret_cast<uint32_t*>(&s.XU[t][c]) =
-            pack_bf16x2(bf16_to_f32(raw & 0xffffu) - xacc[nt][e], bf16_to_f32(raw >> 16) - xacc[nt][e + 1]);
-      }
-    __syncthreads();
-    // U = T X (T already carries diag(beta))
-    float uacc[4][4];
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) uacc[nt][e] = 0.0f;
-#pragma unroll
-    for (int kk = 0; kk < C; kk += 16) {
-      uint32_t a[4], b0[4], b1[4];
-      frag_a<LS>(&s.T[0][0], m0, kk, lane, a);
-      frag_b_kn<LV>(&s.XU[0][0], 0, kk, lane, b0);
-      frag_b_kn<LV>(&s.XU[0][0], 16, kk, lane, b1);
-      mma16816(uacc[0], a, b0[0], b0[1]);
-      mma16816(uacc[1], a, b0[2], b0[3]);
-      mma16816(uacc[2], a, b1[0], b1[1]);
-      mma16816(uacc[3], a, b1[2], b1[3]);
-    }
-    __syncthreads();
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int t = m0 + (lane >> 2) + (e >> 1) * 8;
-        int c = nt * 8 + (lane & 3) * 2;
-        *reinterpret_cast<uint32_t*>(&s.XU[t][c]) = pack_bf16x2(uacc[nt][e], uacc[nt][e + 1]);
-      }
-    __syncthreads();
-    // O = (Q~ S + QK U) / sqrt(dk)
-#pragma unroll
-    for (int kk = 0; kk < C; kk += 16) {
-      uint32_t a[4], b0[4], b1[4];
-      frag_a<LS>(&s.QK[0][0], m0, kk, lane, a);
-      frag_b_kn<LV>(&s.XU[0][0], 0, kk, lane, b0);
-      frag_b_kn<LV>(&s.XU[0][0], 16, kk, lane, b1);
-      mma16816(oacc[0], a, b0[0], b0[1]);
-      mma16816(oacc[1], a, b0[2], b0[3]);
-      mma16816(oacc[2], a, b1[0], b1[1]);
-      mma16816(oacc[3], a, b1[2], b1[3]);
-    }
-#pragma unroll
-    for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        int t = m0 + (lane >> 2) + (e >> 1) * 8;
-        int c = nt * 8 + (lane & 3) * 2;
-        if (t0 + t < seq)
-          *reinterpret_cast<uint32_t*>(og + (tok0 + t0 + t) * ldo + h * DK + j0 + c) =
-              pack_bf16x2(oacc[nt][e] * qscale, oacc[nt][e + 1] * qscale);
-      }
-    // S = e^Gc_C o S + K^^T U : this warp owns state rows [32w, 32w + 32)
-#pragma unroll
-    for (int mt = 0; mt < 2; ++mt) {
-      const int mi = warp * 32 + mt * 16;
-      float sacc[4][4];
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt) sacc[nt][0] = sacc[nt][1] = sacc[nt][2] = sacc[nt][3] = 0.0f;
-#pragma unroll
-      for (int kk = 0; kk < C; kk += 16) {
-        uint32_t a[4], b0[4], b1[4];
-        frag_a_t<LQ>(&s.Ke[0][0], mi, kk, lane, a);
-        frag_b_kn<LV>(&s.XU[0][0], 0, kk, lane, b0);
-        frag_b_kn<LV>(&s.XU[0][0], 16, kk, lane, b1);
-        mma16816(sacc[0], a, b0[0], b0[1]);
-        mma16816(sacc[1], a, b0[2], b0[3]);
-        mma16816(sacc[2], a, b1[0], b1[1]);
-        mma16816(sacc[3], a, b1[2], b1[3]);
-      }
-#pragma unroll
-      for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-        for (int e = 0; e < 4; e += 2) {
-          int i = mi + (lane >> 2) + (e >> 1) * 8;
-          int c = nt * 8 + (lane & 3) * 2;
-          float d = s.dend[i];
-          float n0 = d * s.Sf[i][c] + sacc[nt][e];
-          float n1 = d * s.Sf[i][c + 1] + sacc[nt][e + 1];
-          s.Sf[i][c] = n0;
-          s.Sf[i][c + 1] = n1;
-          *reinterpret_cast<uint32_t*>(&s.Sb[i][c]) = pack_bf16x2(n0, n1);
+  if (warp == 0) {
+    if (lane == 0) {
+      tma_prefetch_desc(&tmBig);
+      tma_prefetch_desc(&tmSmall);
+      tma_prefetch_desc(&tmV);
+      for (int c = 0; c < nchunks && !*abort_flag; ++c) {
+        const int rec = bh * nchunks + c, bf = c & 1;
+        const uint32_t par = (c & 1) ^ 1u;
+        if (!mbar_wait(&bar.kq_free[bf], ((c >> 1) & 1) ^ 1u, err)) { *abort_flag = 1; break; }
+        mbar_arrive_expect_tx(&bar.kq_full[bf], 32768);
+        uint8_t* kq = sm + S_KQ + bf * 32768;
+        for (int j = 0; j < 2; ++j) {
+          tma_load_2d(kq + j * 16384, &tmBig, &bar.kq_full[bf], 64 * j, 192 * rec);
+          tma_load_2d(kq + j * 16384 + 8192, &tmBig, &bar.kq_full[bf], 64 * j, 192 * rec + 64);
         }
+        if (!mbar_wait(&bar.t_free, par, err)) { *abort_flag = 1; break; }
+        mbar_arrive_expect_tx(&bar.t_full, 8192);
+        tma_load_2d(sm + S_TT, &tmSmall, &bar.t_full, 0, 128 * rec);
+        if (!mbar_wait(&bar.m3_free, par, err)) { *abort_flag = 1; break; }
+        mbar_arrive_expect_tx(&bar.m3_full, 16384 + 8192);
+        tma_load_2d(sm + S_KE, &tmBig, &bar.m3_full, 0, 192 * rec + 128);
+        tma_load_2d(sm + S_KE + 8192, &tmBig, &bar.m3_full, 64, 192 * rec + 128);
+        tma_load_2d(sm + S_QK, &tmSmall, &bar.m3_full, 0, 128 * rec + 64);
+        if (!mbar_wait(&bar.v_free, par, err)) { *abort_flag = 1; break; }
+        mbar_arrive_expect_tx(&bar.v_full, 16384 + 512);
+        tma_load_2d(sm + S_V, &tmV, &bar.v_full, h * DK, (int)(tok0 + c * C));
+        bulk_load(sm + S_D, dend + (size_t)rec * DK, 512, &bar.v_full);
+      }
     }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t sb = smem_u32(sm + S_SB), xs = smem_u32(sm + S_XS), us = smem_u32(sm + S_US);
+      const uint32_t tt = smem_u32(sm + S_TT), qk = smem_u32(sm + S_QK), ke = smem_u32(sm + S_KE);
+      bool ok = true;
+      for (int c = 0; ok && c < nchunks && !*abort_flag; ++c) {
+        const int bf = c & 1;
+        const uint32_t par = c & 1;
+        // X^T | O1^T = S^T [K~; Q~]^T
+        if (!mbar_wait(&bar.kq_full[bf], (c >> 1) & 1, err) || !mbar_wait(&bar.s_ready, par, err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t kq = smem_u32(sm + S_KQ + bf * 32768);
+#pragma unroll
+        for (int kk = 0; kk < DK / 16; ++kk)
+          umma_f16(tmem + TM_X, smem_desc_sw128(sb + (kk >> 2) * 16384 + (kk & 3) * 32),
+                   smem_desc_sw128(kq + (kk >> 2) * 16384 + (kk & 3) * 32), IDESC_N128, kk != 0);
+        umma_commit(&bar.x_full);
+        umma_commit(&bar.kq_free[bf]);
+        // U^T = X^T T^T
+        if (!mbar_wait(&bar.t_full, par, err) || !mbar_wait(&bar.xs_ready, par, err)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < C / 16; ++kk)
+          umma_f16(tmem + TM_U, smem_desc_sw128(xs + kk * 32), smem_desc_sw128(tt + kk * 32), IDESC_N64, kk != 0);
+        umma_commit(&bar.u_full);
+        umma_commit(&bar.t_free);
+        // O^T += U^T QK^T ; S^T += U^T K^
+        if (!mbar_wait(&bar.m3_full, par, err) || !mbar_wait(&bar.us_ready, par, err)) { ok = false; break; }
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < C / 16; ++kk)
+          umma_f16(tmem + TM_O, smem_desc_sw128(us + kk * 32), smem_desc_sw128(qk + kk * 32), IDESC_N64, 1);
+#pragma unroll
+        for (int kk = 0; kk < C / 16; ++kk)
+          umma_f16(tmem + TM_S, smem_desc_sw128(us + kk * 32), smem_desc_sw128_mn(ke + kk * 2048, 8192),
+                   IDESC_N128_BMN, 1);
+        umma_commit(&bar.o_full);
+        umma_commit(&bar.m3_free);
+      }
+      if (!ok) *abort_flag = 1;
+    }
+  } else {
+    // element-wise warps: TMEM lane quarter qd = warp % 4 (value columns
+    // v = 32 qd + lane); `half` selects token columns [32 half, +32) of X, U,
+    // O and key rows [64 half, +64) of the state
+    const int qd = warp & 3, half = (warp - 2) >> 2;
+    const int v = qd * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(qd * 32) << 16;
+    const float qscale = rsqrtf((float)DK);
+    float* st_g = state ? state + (size_t)bh * DK * DK : nullptr;
+    const uint16_t* sV = reinterpret_cast<const uint16_t*>(sm + S_V);
+    const float* sD = reinterpret_cast<const float*>(sm + S_D);
+    bool ok = true;
+    // initial state: S^T[v][i] = S[i][v]
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const int i0 = half * 64 + p * 32;
+      uint32_t r[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(st_g ? st_g[(size_t)(i0 + i) * DK + v] : 0.0f);
+      tmem_st32(tmem + lane_off + TM_S + i0, r);
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        *reinterpret_cast<uint4*>(sm + S_SB + half * 16384 + sw128(v, p * 4 + g)) =
+            make_uint4(pack_bf16x2(__uint_as_float(r[8 * g]), __uint_as_float(r[8 * g + 1])),
+                       pack_bf16x2(__uint_as_float(r[8 * g + 2]), __uint_as_float(r[8 * g + 3])),
+                       pack_bf16x2(__uint_as_float(r[8 * g + 4]), __uint_as_float(r[8 * g + 5])),
+                       pack_bf16x2(__uint_as_float(r[8 * g + 6]), __uint_as_float(r[8 * g + 7])));
+    }
+    tmem_st_wait();
+    fence_proxy_async();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&bar.s_ready);
+
+    for (int c = 0; c < nchunks; ++c) {
+      const uint32_t par = c & 1;
+      const int t0 = c * C;
+      // ---- X^T = V^T - S^T K~^T -> bf16; S^T *= e^Gc_C ----
+      if (!mbar_wait(&bar.x_full, par, err) || !mbar_wait(&bar.v_full, par, err)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + TM_X + half * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int t = half * 32 + 8 * g + 2 * j;
+            pk[j] = pack_bf16x2(bf16_to_f32(sV[t * DK + v]) - __uint_as_float(r[8 * g + 2 * j]),
+                                bf16_to_f32(sV[(t + 1) * DK + v]) - __uint_as_float(r[8 * g + 2 * j + 1]));
+          }
+          *reinterpret_cast<uint4*>(sm + S_XS + sw128(v, half * 4 + g)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+      }
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int i0 = half * 64 + p * 32;
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + TM_S + i0, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * sD[i0 + i]);
+        tmem_st32(tmem + lane_off + TM_S + i0, r);
+      }
+      tmem_st_wait();
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) { mbar_arrive(&bar.xs_ready); mbar_arrive(&bar.v_free); }
+      // ---- U^T -> bf16 ----
+      if (!mbar_wait(&bar.u_full, par, err)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + TM_U + half * 32, r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int g = 0; g < 4; ++g)
+          *reinterpret_cast<uint4*>(sm + S_US + sw128(v, half * 4 + g)) =
+              make_uint4(pack_bf16x2(__uint_as_float(r[8 * g]), __uint_as_float(r[8 * g + 1])),
+                         pack_bf16x2(__uint_as_float(r[8 * g + 2]), __uint_as_float(r[8 * g + 3])),
+                         pack_bf16x2(__uint_as_float(r[8 * g + 4]), __uint_as_float(r[8 * g + 5])),
+                         pack_bf16x2(__uint_as_float(r[8 * g + 6]), __uint_as_float(r[8 * g + 7])));
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar.us_ready);
+      // ---- O out; S^T -> bf16 copy for the next chunk ----
+      if (!mbar_wait(&bar.o_full, par, err)) { ok = false; break; }
+      tc_fence_after();
+      {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + TM_O + half * 32, r);
+        tmem_ld_wait();
+        uint16_t* orow = og + (tok0 + t0 + half * 32) * ldo + h * DK + v;
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (t0 + half * 32 + j < seq) orow[(long long)j * ldo] = f32_to_bf16_rne(__uint_as_float(r[j]) * qscale);
+      }
+      const bool last = c == nchunks - 1;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int i0 = half * 64 + p * 32;
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_off + TM_S + i0, r);
+        tmem_ld_wait();
+        if (last) {
+          if (st_g)
+#pragma unroll
+            for (int i = 0; i < 32; ++i) st_g[(size_t)(i0 + i) * DK + v] = __uint_as_float(r[i]);
+        } else {
+#pragma unroll
+          for (int g = 0; g < 4; ++g)
+            *reinterpret_cast<uint4*>(sm + S_SB + half * 16384 + sw128(v, p * 4 + g)) =
+                make_uint4(pack_bf16x2(__uint_as_float(r[8 * g]), __uint_as_float(r[8 * g + 1])),
+                           pack_bf16x2(__uint_as_float(r[8 * g + 2]), __uint_as_float(r[8 * g + 3])),
+                           pack_bf16x2(__uint_as_float(r[8 * g + 4]), __uint_as_float(r[8 * g + 5])),
+                           pack_bf16x2(__uint_as_float(r[8 * g + 6]), __uint_as_float(r[8 * g + 7])));
+        }
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0 && !last) mbar_arrive(&bar.s_ready);
+    }
+    if (!ok) *abort_flag = 1;
   }
   __syncthreads();
-  if (st_g)
-    for (int i = tid; i < DK * SV; i += 128) st_g[(i / SV) * DK + j0 + (i % SV)] = s.Sf[i / SV][i % SV];
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
 }
 
 bool g_attr[64];
@@ -550,25 +701,38 @@ int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t*
   const size_t need = kda_workspace_bytes(batch, seq, heads);
   if (!workspace || workspace_bytes < need)
     return set_error(ENNX_B200_INVALID_ARGUMENT, "kda: workspace of %zu bytes required", need);
+  if (!raw && (!g || !beta)) return set_error(ENNX_B200_INVALID_ARGUMENT, "kda: g and beta are required");
+  const long long rows = (long long)batch * seq;
+  if (rows > 0x7fffffffLL) return set_error(ENNX_B200_UNSUPPORTED, "kda: too many tokens");
+  const int nchunks = (seq + C - 1) / C;
+  const size_t R = (size_t)batch * heads * nchunks;
+  if (R * 192 > 0xffffffffull) return set_error(ENNX_B200_UNSUPPORTED, "kda: too many chunks");
+  uint16_t* big = reinterpret_cast<uint16_t*>(workspace);
+  uint16_t* small = reinterpret_cast<uint16_t*>(reinterpret_cast<uint8_t*>(workspace) + R * kBigRecBytes);
+  float* dend = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) + R * (kBigRecBytes + kSmallRecBytes));
+  CUtensorMap tb, ts, tv;
+  ENNX_TRY(make_tmap_2d_bf16(&tb, big, DK, R * 192, DK, 64, 64, true));
+  ENNX_TRY(make_tmap_2d_bf16(&ts, small, C, R * 128, C, 64, 64, true));
+  ENNX_TRY(make_tmap_2d_bf16(&tv, v, (uint64_t)heads * DK, (uint64_t)rows, (uint64_t)ld_qkv, DK, C, false));
+  int* err = device_error_word();
+  if (!err) return set_error(ENNX_B200_CUDA_ERROR, "kda: no device error word");
   int dev = 0;
   cudaGetDevice(&dev);
   if (!g_attr[dev]) {
-    ENNX_CUDA(cudaFuncSetAttribute(kda_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(PrepSmem)),
+    ENNX_CUDA(cudaFuncSetAttribute(kda_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM),
               "kda prep smem");
-    ENNX_CUDA(cudaFuncSetAttribute(kda_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sizeof(ScanSmem)),
+    ENNX_CUDA(cudaFuncSetAttribute(kda_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM),
               "kda scan smem");
     g_attr[dev] = true;
   }
-  const int nchunks = (seq + C - 1) / C;
   KdaRawGate rg;
   memset(&rg, 0, sizeof(rg));
   if (raw) rg = *raw;
-  if (!raw && (!g || !beta)) return set_error(ENNX_B200_INVALID_ARGUMENT, "kda: g and beta are required");
-  kda_prep_kernel<<<dim3(nchunks, batch * heads), 256, sizeof(PrepSmem), s>>>(
-      q, k, ld_qkv, g, (long long)heads * DK, beta, seq, heads, nchunks, rg, (uint8_t*)workspace);
+  kda_prep_kernel<<<dim3(nchunks, batch * heads), PREP_THREADS, PREP_SMEM, s>>>(
+      q, k, ld_qkv, g, (long long)heads * DK, beta, seq, heads, nchunks, rg, big, small, dend, err);
   ENNX_LAUNCH_CHECK("kda prep");
-  kda_scan_kernel<<<dim3(DK / SV, batch * heads), 128, sizeof(ScanSmem), s>>>(v, ld_qkv, (const uint8_t*)workspace,
-                                                                               state, o, ldo, seq, heads, nchunks);
+  kda_scan_kernel<<<batch * heads, SCAN_THREADS, SCAN_SMEM, s>>>(tb, ts, tv, dend, state, o, ldo, seq, heads, nchunks,
+                                                                 err);
   ENNX_LAUNCH_CHECK("kda scan");
   return ENNX_B200_OK;
 }

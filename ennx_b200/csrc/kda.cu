@@ -25,7 +25,8 @@
 //     and runs the four intra-chunk products D_b = A B_b^T on tcgen05 with
 //     fp32 accumulators in TMEM: rows 0..63 of D_b give QK, rows 64..127
 //     give A', each read for the rows of block b.  Then
-//     T = (I + diag(beta) A')^-1 diag(beta) in fp32 on the CUDA cores.
+//     T = (I + diag(beta) A')^-1 diag(beta) in fp32 on the CUDA cores
+//     (blocked: 16x16 diagonal inverses, then 32x32, then 64x64).
 //   kda_scan_kernel -- one CTA per (sequence, head) walks the chunks in order
 //     in transposed form, TMEM lane = value column v:
 //       X^T = S^T K~^T, O^T = S^T Q~^T              (one MMA, N = 128)
@@ -100,10 +101,11 @@ constexpr int P_FB = P_GC + C * DK * 4;    // fp32 [4][128] block-to-block decay
 constexpr int P_BETA = P_FB + 4 * DK * 4;  // fp32 [64]
 constexpr int P_BAR = P_BETA + C * 4;      // mbarrier + TMEM slot
 constexpr int PREP_SMEM = P_BAR + 64 + 1024;
-// after the MMAs complete, the A operand region holds L and the diagonal inverses
+// after the MMAs complete, the A operand region holds L (then T) and the B
+// operand region the temporaries of the inverse
 constexpr int P_L = P_XA;
-constexpr int P_TD = P_XA + C * LF * 4;
-static_assert(P_TD + 4 * 16 * 17 * 4 <= P_YB, "L and diagonal inverses must fit the A operand region");
+static_assert(C * LF * 4 <= P_YB - P_XA, "L must fit the A operand region");
+static_assert(2 * 16 * 17 * 4 <= 40960 && 32 * 33 * 4 <= 40960, "inverse temporaries must fit the B region");
 
 __host__ __device__ constexpr int yb_off(int b) { return P_YB + 4096 * (b * (b + 1) / 2); }
 __host__ __device__ constexpr int yb_rows(int b) { return 16 * (b + 1); }
@@ -146,6 +148,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
     const bool set0 = b < raw.split_seq;
     const uint16_t* tb = set0 ? raw.tb0 : raw.tb1;
     const float dscale = __expf(bf16_to_f32((set0 ? raw.decay0 : raw.decay1)[h]));
+#pragma unroll
     for (int i = tid; i < C * (DK / 8); i += PREP_THREADS) {
       const int r = i >> 4, c = (i & 15) * 8;
       float gv[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -163,6 +166,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       beta[tid] = t0 + tid < seq ? 1.0f / (1.0f + __expf(-bf16_to_f32(raw.rbeta[(tok0 + t0 + tid) * raw.ldb + h])))
                                  : 0.0f;
   } else {
+#pragma unroll
     for (int i = tid; i < C * (DK / 4); i += PREP_THREADS) {
       const int r = i >> 5, c = (i & 31) * 4;
       float4 gv = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -201,18 +205,26 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
   }
   __syncthreads();
 
-  // ---- operands: a half-warp per token row, one 8-channel chunk per lane ----
+  // ---- operands: a half-warp per token row, one 8-channel chunk per lane;
+  // the q/k loads of the next row run one iteration ahead ----
+  auto load_qk = [&](int it, uint4& qv, uint4& kv) {
+    const int t = it * (PREP_THREADS / 16) + (tid >> 4), c0 = (tid & 15) * 8;
+    qv = kv = make_uint4(0, 0, 0, 0);
+    if (t0 + t < seq) {
+      qv = __ldg(reinterpret_cast<const uint4*>(qg + (tok0 + t0 + t) * ld + h * DK + c0));
+      kv = __ldg(reinterpret_cast<const uint4*>(kg + (tok0 + t0 + t) * ld + h * DK + c0));
+    }
+  };
+  uint4 qn, kn;
+  load_qk(0, qn, kn);
+#pragma unroll 1
   for (int it = 0; it < C * 16 / PREP_THREADS; ++it) {
     const int t = it * (PREP_THREADS / 16) + (tid >> 4), cc = tid & 15, c0 = cc * 8;
     const int blk = t >> 4, r = blk * 16;
     float q[8], k[8];
-    if (t0 + t < seq) {
-      unpack8(*reinterpret_cast<const uint4*>(qg + (tok0 + t0 + t) * ld + h * DK + c0), q);
-      unpack8(*reinterpret_cast<const uint4*>(kg + (tok0 + t0 + t) * ld + h * DK + c0), k);
-    } else {
-#pragma unroll
-      for (int j = 0; j < 8; ++j) q[j] = k[j] = 0.0f;
-    }
+    unpack8(qn, q);
+    unpack8(kn, k);
+    if (it + 1 < C * 16 / PREP_THREADS) load_qk(it + 1, qn, kn);
     if (raw.active) {
       // per-token L2 normalisation, 1/max(|x|, 1e-6), rounded to bf16 (kda_moe.metal:510-534)
       float sq = 0.0f, sk = 0.0f;
@@ -287,7 +299,6 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
 
   // ---- read D_b: warp w reads TMEM lanes 32(w%4).., block 2((w%4)&1) + w/4 ----
   float(*L)[LF] = reinterpret_cast<float(*)[LF]>(sm + P_L);
-  float(*Td)[16][17] = reinterpret_cast<float(*)[16][17]>(sm + P_TD);
   {
     const int qd = warp & 3, R = qd * 32 + lane;
     const int bl = 2 * (qd & 1) + (warp >> 2);
@@ -329,9 +340,16 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
   tc_fence_before();
   __syncthreads();
 
-  // ---- T = (I + L)^-1: 16x16 diagonal inverses, then block rows in order ----
-  if (warp < 4 && lane < 16) {
-    const int d0 = warp * 16, jj = lane;
+  // ---- T = (I + L)^-1 in place in L, three levels:
+  //   (1) the four 16x16 diagonal blocks by forward substitution;
+  //   (2) the lower-left 16x16 block of each 32x32 half: T10 = -D1 (L10 D0);
+  //   (3) the lower-left 32x32 block: T_BA = -T_B (L_BA T_A).
+  // Blocks above the diagonal of L are zero and stay zero, so the products
+  // run over full ranges.  Temporaries P live in the dead B operand region.
+  float(*P16)[16][17] = reinterpret_cast<float(*)[16][17]>(sm + P_YB);
+  float(*P32)[33] = reinterpret_cast<float(*)[33]>(sm + P_YB);
+  if (tid < 64) {
+    const int d0 = (tid >> 4) * 16, jj = tid & 15;
     float x[16];
 #pragma unroll
     for (int t = 0; t < 16; ++t) {
@@ -340,62 +358,63 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
       for (int u = 0; u < t; ++u) v -= L[d0 + t][d0 + u] * x[u];
       x[t] = v;
     }
+    __syncwarp();
 #pragma unroll
-    for (int t = 0; t < 16; ++t) Td[warp][t][jj] = x[t];
+    for (int t = 0; t < 16; ++t) L[d0 + t][d0 + jj] = x[t];
   }
   __syncthreads();
-  // block row bi of T (bj < bi): T_ij = -T_ii sum_{k=j}^{i-1} L_ik T_kj.  Rows
-  // < bi of L already hold T; row bi of L still holds L until overwritten.
-  for (int bi = 1; bi < 4; ++bi) {
-    float mval[3];
-    const int n = bi * 256;
+  {  // (2a) P = L10 D0 for both halves: thread -> (half, row, 2 columns)
+    const int hb = tid >> 7, rr = (tid >> 3) & 15, c0 = (tid & 7) * 2, o = 32 * hb;
+    float a0 = 0.0f, a1 = 0.0f;
 #pragma unroll
-    for (int q = 0; q < 3; ++q) {
-      const int i = tid + q * 256;
-      mval[q] = 0.0f;
-      if (i < n) {
-        const int bj = i / 256, e = i % 256, rr = e / 16, c2 = e % 16;
-        float acc = 0.0f;
-        for (int kx = bj * 16; kx < bi * 16; ++kx) {
-          const float tkj = (kx < (bj + 1) * 16) ? Td[bj][kx - bj * 16][c2] : L[kx][bj * 16 + c2];
-          acc += L[bi * 16 + rr][kx] * tkj;
-        }
-        mval[q] = acc;
-      }
+    for (int k = 0; k < 16; ++k) {
+      const float l = L[o + 16 + rr][o + k];
+      a0 += l * L[o + k][o + c0];
+      a1 += l * L[o + k][o + c0 + 1];
     }
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < 3; ++q) {
-      const int i = tid + q * 256;
-      if (i < n) {
-        const int bj = i / 256, e = i % 256, rr = e / 16, c2 = e % 16;
-        L[bi * 16 + rr][bj * 16 + c2] = mval[q];  // M_ij, temporarily
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < 3; ++q) {
-      const int i = tid + q * 256;
-      mval[q] = 0.0f;
-      if (i < n) {
-        const int bj = i / 256, e = i % 256, rr = e / 16, c2 = e % 16;
-        float acc = 0.0f;
-#pragma unroll 4
-        for (int kx = 0; kx < 16; ++kx) acc -= Td[bi][rr][kx] * L[bi * 16 + kx][bj * 16 + c2];
-        mval[q] = acc;
-      }
-    }
-    __syncthreads();
-#pragma unroll
-    for (int q = 0; q < 3; ++q) {
-      const int i = tid + q * 256;
-      if (i < n) {
-        const int bj = i / 256, e = i % 256, rr = e / 16, c2 = e % 16;
-        L[bi * 16 + rr][bj * 16 + c2] = mval[q];
-      }
-    }
-    __syncthreads();
+    P16[hb][rr][c0] = a0;
+    P16[hb][rr][c0 + 1] = a1;
   }
+  __syncthreads();
+  {  // (2b) T10 = -D1 P
+    const int hb = tid >> 7, rr = (tid >> 3) & 15, c0 = (tid & 7) * 2, o = 32 * hb;
+    float a0 = 0.0f, a1 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      const float d = L[o + 16 + rr][o + 16 + k];
+      a0 += d * P16[hb][k][c0];
+      a1 += d * P16[hb][k][c0 + 1];
+    }
+    L[o + 16 + rr][o + c0] = -a0;
+    L[o + 16 + rr][o + c0 + 1] = -a1;
+  }
+  __syncthreads();
+  {  // (3a) P = L_BA T_A: thread -> (row, 4 columns)
+    const int rr = tid >> 3, c0 = (tid & 7) * 4;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float l = L[32 + rr][k];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] += l * L[k][c0 + j];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) P32[rr][c0 + j] = acc[j];
+  }
+  __syncthreads();
+  {  // (3b) T_BA = -T_B P
+    const int rr = tid >> 3, c0 = (tid & 7) * 4;
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll 8
+    for (int k = 0; k < 32; ++k) {
+      const float d = L[32 + rr][32 + k];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[j] += d * P32[k][c0 + j];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) L[32 + rr][c0 + j] = -acc[j];
+  }
+  __syncthreads();
   // T diag(beta) -> record (lower triangle incl. diagonal), 8 columns per thread
   for (int i = tid; i < C * C / 8; i += PREP_THREADS) {
     const int rr = i >> 3, c0 = (i & 7) * 8;
@@ -403,9 +422,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
       const int c2 = c0 + u;
-      float tv = 0.0f;
-      if (c2 <= rr) tv = (c2 >> 4) == (rr >> 4) ? Td[rr >> 4][rr & 15][c2 & 15] : L[rr][c2];
-      f[u] = tv * beta[c2];
+      f[u] = c2 <= rr ? L[rr][c2] * beta[c2] : 0.0f;
     }
     *reinterpret_cast<uint4*>(smallr + (size_t)rr * C + c0) = pack8(f);
   }

@@ -79,8 +79,9 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 // ---------------------------------------------------------------------------
 // Population noise: Philox4x32-10 (Salmon et al., SC'11) + Box-Muller.
 // Element e of tensor t for antithetic pair p under population seed s is the
-// (e % 4)-th normal of block e / 4, counter {lo(blk), hi(blk), t, p},
-// key {lo(s), hi(s)}.
+// (e % 8)-th normal of block e / 8: counter {lo(blk), hi(blk), t, p}, key
+// {lo(s), hi(s)}; each of the four output words w gives one Box-Muller pair
+// from its two 16-bit halves (radius from the low half, angle from the high).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
 #pragma unroll
@@ -97,28 +98,26 @@ __device__ __forceinline__ void philox4x32_10(uint32_t c[4], uint32_t k0, uint32
   }
 }
 
-// Box-Muller on two Philox words: u1 = ((a >> 9) + 1/2) / 2^23 lies in (0, 1)
-// and is exact in fp32 (a 24-bit numerator would round 2^24 - 1/2 up to 1,
-// giving ln(u1) = 0 and a NaN from 0 * rsqrt(0)); angle
-// 2*pi*((b >> 8) / 2^24 - 1/2) in [-pi, pi).  Uses the SFU approximations
-// (log2, rsqrt, sin/cos on [-pi, pi]); values agree with the fp64 oracle to ~1e-6.
-__device__ __forceinline__ void box_muller(uint32_t a, uint32_t b, float& z0, float& z1) {
-  float u1 = __fmul_rn(__fadd_rn((float)(a >> 9), 0.5f), 1.1920928955078125e-07f);
-  float u2 = __fmul_rn((float)(b >> 8), 5.9604644775390625e-08f);
-  float x = __fmul_rn(-1.3862943611198906f, __log2f(u1));  // -2 ln(u1) = -2 ln2 log2(u1) >= 0
-  float r = x > 0.0f ? __fmul_rn(x, rsqrtf(x)) : 0.0f;
+// Box-Muller on the two 16-bit halves of one Philox word: u1 = (lo + 1/2) / 2^16
+// lies in (0, 1) exactly (radius at most sqrt(2 ln 2^17) = 4.86), angle
+// 2*pi*(hi / 2^16 - 1/2) in [-pi, pi).  Uses the SFU approximations (log2,
+// rsqrt, sin/cos on [-pi, pi]); values agree with the fp64 oracle to ~1e-6.
+__device__ __forceinline__ void box_muller16(uint32_t w, float& z0, float& z1) {
+  const float u1 = __fmul_rn(__fadd_rn((float)(w & 0xffffu), 0.5f), 1.52587890625e-05f);
+  const float u2 = __fmul_rn((float)(w >> 16), 1.52587890625e-05f);
+  const float x = __fmul_rn(-1.3862943611198906f, __log2f(u1));  // -2 ln(u1) = -2 ln2 log2(u1) > 0
+  const float r = x > 0.0f ? __fmul_rn(x, rsqrtf(x)) : 0.0f;
   float s, c;
   __sincosf(__fmul_rn(6.283185307179586f, __fsub_rn(u2, 0.5f)), &s, &c);
   z0 = __fmul_rn(r, c);
   z1 = __fmul_rn(r, s);
 }
 
-__device__ __forceinline__ void noise4(uint64_t seed, uint32_t pair, uint32_t tensor, uint64_t block,
-                                       float z[4]) {
+__device__ __forceinline__ void noise8(uint64_t seed, uint32_t pair, uint32_t tensor, uint64_t block, float z[8]) {
   uint32_t c[4] = {(uint32_t)block, (uint32_t)(block >> 32), tensor, pair};
   philox4x32_10(c, (uint32_t)seed, (uint32_t)(seed >> 32));
-  box_muller(c[0], c[1], z[0], z[1]);
-  box_muller(c[2], c[3], z[2], z[3]);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) box_muller16(c[j], z[2 * j], z[2 * j + 1]);
 }
 
 // ---------------------------------------------------------------------------

@@ -183,8 +183,8 @@ __global__ void dense_linear_kernel(const float* __restrict__ x, const float* __
   }
 }
 
-// Population noise: each thread owns 8 consecutive elements (two Philox
-// blocks) per step, 16-byte loads and stores; W +/- sigma*eps with two fp32
+// Population noise: each thread owns 8 consecutive elements (one Philox
+// block) per step, 16-byte loads and stores; W +/- sigma*eps with two fp32
 // roundings, RNE.  Blocks cover a fixed 8192-element span and retire quickly,
 // so the block scheduler can interleave them with the compute stream's
 // kernels on the same SMs (this kernel runs on a low-priority stream).
@@ -200,8 +200,7 @@ __global__ void __launch_bounds__(256) perturb_bf16_kernel(const uint16_t* __res
     if (g >= groups) return;
     uint64_t e0 = g * 8;
     float z[8];
-    noise4(seed, pair, tensor, 2 * g, z);
-    noise4(seed, pair, tensor, 2 * g + 1, z + 4);
+    noise8(seed, pair, tensor, g, z);
     if (e0 + 8 <= n) {
       uint4 raw = *reinterpret_cast<const uint4*>(w + e0);
       uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};

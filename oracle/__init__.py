@@ -77,7 +77,7 @@ def lib():
             "eo_trial_hash": (u32, [u32, u32, u32]),
             "eo_perturb_code": (u32, [u32, u32, u32, u32, u32, u32, u32]),
             "eo_philox4x32_10": (None, [P, P, P]),
-            "eo_noise4": (None, [u64, u32, u32, u64, P]),
+            "eo_noise8": (None, [u64, u32, u32, u64, P]),
             "eo_perturb_bf16": (None, [P, sz, u64, u32, u32, f32, ctypes.c_int, P]),
             "eo_rmsnorm": (None, [P, P, sz, sz, f32, P]),
             "eo_router_logits": (None, [P, P, sz, sz, sz, P]),
@@ -202,13 +202,13 @@ def philox4x32_10(ctr, key):
 
 
 def noise(seed: int, pair: int, tensor: int, n: int, start: int = 0) -> np.ndarray:
-    """N(0,1) draws for elements [start, start+n) of one tensor (start % 4 == 0)."""
-    assert start % 4 == 0
-    out = np.zeros(((n + 3) // 4) * 4, np.float32)
-    buf = np.zeros(4, np.float32)
-    for blk in range((n + 3) // 4):
-        lib().eo_noise4(seed, pair, tensor, start // 4 + blk, _p(buf))
-        out[4 * blk:4 * blk + 4] = buf
+    """N(0,1) draws for elements [start, start+n) of one tensor (start % 8 == 0)."""
+    assert start % 8 == 0
+    out = np.zeros(((n + 7) // 8) * 8, np.float32)
+    buf = np.zeros(8, np.float32)
+    for blk in range((n + 7) // 8):
+        lib().eo_noise8(seed, pair, tensor, start // 8 + blk, _p(buf))
+        out[8 * blk:8 * blk + 8] = buf
     return out[:n]
 
 

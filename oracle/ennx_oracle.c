@@ -289,35 +289,37 @@ void eo_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out
     out[0] = c0; out[1] = c1; out[2] = c2; out[3] = c3;
 }
 
-/* Box-Muller on two Philox words (23-bit u1 in (0,1), 24-bit angle); computed in double so
- * the oracle is the exactly rounded value the device approximates. */
-static void box_muller(uint32_t a, uint32_t b, float* z0, float* z1) {
-    float u1 = ((float)(a >> 9) + 0.5f) * 1.1920928955078125e-07f; /* 2^-23: exact, < 1 */
-    float u2 = (float)(b >> 8) * 5.9604644775390625e-08f;
+/* Box-Muller on the two 16-bit halves of one Philox word: u1 = (lo + 1/2) / 2^16 in (0,1),
+ * angle 2 pi (hi / 2^16 - 1/2); computed in double so the oracle is the exactly rounded
+ * value the device approximates. */
+static void box_muller16(uint32_t w, float* z0, float* z1) {
+    float u1 = ((float)(w & 0xffffu) + 0.5f) * 1.52587890625e-05f; /* 2^-16: exact, < 1 */
+    float u2 = (float)(w >> 16) * 1.52587890625e-05f;
     double r = sqrt(-2.0 * log((double)u1));
     double th = 2.0 * M_PI * ((double)u2 - 0.5);
     *z0 = (float)(r * cos(th));
     *z1 = (float)(r * sin(th));
 }
 
-/* Four N(0,1) draws for element block `block` (elements 4*block .. 4*block+3)
- * of tensor `tensor`, antithetic pair `pair`, population seed `seed`. */
-void eo_noise4(uint64_t seed, uint32_t pair, uint32_t tensor, uint64_t block, float out[4]) {
+/* Eight N(0,1) draws for element block `block` (elements 8*block .. 8*block+7)
+ * of tensor `tensor`, antithetic pair `pair`, population seed `seed`: one
+ * Philox4x32-10 call, counter {lo(block), hi(block), tensor, pair}, key
+ * {lo(seed), hi(seed)}; word j gives draws 2j and 2j+1. */
+void eo_noise8(uint64_t seed, uint32_t pair, uint32_t tensor, uint64_t block, float out[8]) {
     uint32_t ctr[4] = {(uint32_t)block, (uint32_t)(block >> 32), tensor, pair};
     uint32_t key[2] = {(uint32_t)seed, (uint32_t)(seed >> 32)};
     uint32_t x[4];
     eo_philox4x32_10(ctr, key, x);
-    box_muller(x[0], x[1], &out[0], &out[1]);
-    box_muller(x[2], x[3], &out[2], &out[3]);
+    for (int j = 0; j < 4; ++j) box_muller16(x[j], &out[2 * j], &out[2 * j + 1]);
 }
 
 /* W~ = bf16(W + sign * (sigma * eps)), two fp32 roundings then RNE. */
 void eo_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor,
                      float sigma, int sign, uint16_t* out) {
-    float z[4];
+    float z[8];
     for (size_t i = 0; i < n; ++i) {
-        if ((i & 3) == 0 || i == 0) eo_noise4(seed, pair, tensor, i >> 2, z);
-        float step = sigma * z[i & 3];
+        if ((i & 7) == 0) eo_noise8(seed, pair, tensor, i >> 3, z);
+        float step = sigma * z[i & 7];
         float v = sign >= 0 ? eo_bf16_decode(w[i]) + step : eo_bf16_decode(w[i]) - step;
         out[i] = eo_bf16_encode(v);
     }

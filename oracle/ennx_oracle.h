@@ -61,7 +61,7 @@ uint32_t eo_perturb_code(uint32_t code, uint32_t seed_low, uint32_t seed_high, u
 
 /* ---- population noise (builder-defined; no reference counterpart) ---- */
 void eo_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);
-void eo_noise4(uint64_t seed, uint32_t pair, uint32_t tensor, uint64_t block, float out[4]);
+void eo_noise8(uint64_t seed, uint32_t pair, uint32_t tensor, uint64_t block, float out[8]);
 void eo_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor,
                      float sigma, int sign, uint16_t* out);
 

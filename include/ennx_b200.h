@@ -166,12 +166,12 @@ ENNX_B200_API int32_t ennx_b200_gemm_bf16(const ennx_b200_gemm_params* params, c
 ENNX_B200_API int32_t ennx_b200_rmsnorm_bf16(const uint16_t* x, const uint16_t* w, int64_t rows, int32_t width,
                                              float eps, uint16_t* out, void* stream);
 
-/* Router logits (fp32, fixed reduction order, bit-identical to the CPU
- * oracle), top-k with strict '>' (ties keep the lower expert index) and
- * softmax over the kept logits.  Replaces moe_router_topk
- * (kda_moe.metal:570-621); top_k <= 8 as KdaMoeLayerRequest::validate
- * (forward_program.rs:428).  x bf16 [tokens, hidden], w_router bf16
- * [experts, hidden], hidden in {256, 512, 1024, 2048, 4096}, experts <= 256.
+/* Router logits (fp32, one serial fma chain over the hidden index per logit,
+ * the reference's loop order, bit-identical to the CPU oracle), top-k with
+ * strict '>' (ties keep the lower expert index) and softmax over the kept
+ * logits.  Replaces moe_router_topk (kda_moe.metal:570-621); top_k <= 8 as
+ * KdaMoeLayerRequest::validate (forward_program.rs:428).  x bf16 [tokens,
+ * hidden], w_router bf16 [experts, hidden], hidden % 32 == 0, experts <= 256.
  * logits (nullable) f32 [tokens, experts]; index i32 / gate f32 [tokens, top_k]. */
 ENNX_B200_API int32_t ennx_b200_moe_route(const uint16_t* x, const uint16_t* w_router, int64_t tokens,
                                           int32_t hidden, int32_t experts, int32_t top_k, float* logits,

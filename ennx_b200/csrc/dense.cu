@@ -189,14 +189,15 @@ __global__ void dense_linear_kernel(const float* __restrict__ x, const float* __
 // so the block scheduler can interleave them with the compute stream's
 // kernels on the same SMs (this kernel runs on a low-priority stream).
 constexpr int kPerturbGroupsPerThread = 4;
-__global__ void __launch_bounds__(256) perturb_bf16_kernel(const uint16_t* __restrict__ w, uint64_t n, uint64_t seed,
+constexpr int kPerturbThreads = 128;
+__global__ void __launch_bounds__(kPerturbThreads) perturb_bf16_kernel(const uint16_t* __restrict__ w, uint64_t n, uint64_t seed,
                                                            uint32_t pair, uint32_t tensor, float sigma,
                                                            uint16_t* __restrict__ plus, uint16_t* __restrict__ minus) {
   const uint64_t groups = (n + 7) / 8;
-  const uint64_t g0 = (uint64_t)blockIdx.x * (256 * kPerturbGroupsPerThread) + threadIdx.x;
+  const uint64_t g0 = (uint64_t)blockIdx.x * (kPerturbThreads * kPerturbGroupsPerThread) + threadIdx.x;
 #pragma unroll
   for (int it = 0; it < kPerturbGroupsPerThread; ++it) {
-    const uint64_t g = g0 + (uint64_t)it * 256;
+    const uint64_t g = g0 + (uint64_t)it * kPerturbThreads;
     if (g >= groups) return;
     uint64_t e0 = g * 8;
     float z[8];
@@ -385,10 +386,10 @@ int32_t ennx_b200_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint3
     return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16 buffers must be 16-byte aligned");
   if (!isfinite(sigma)) return set_error(ENNX_B200_INVALID_ARGUMENT, "sigma must be finite");
   uint64_t groups = (n + 7) / 8;
-  uint64_t per_block = 256 * kPerturbGroupsPerThread;
+  uint64_t per_block = kPerturbThreads * kPerturbGroupsPerThread;
   uint64_t blocks = (groups + per_block - 1) / per_block;
   if (blocks > 0x7fffffffull) return set_error(ENNX_B200_UNSUPPORTED, "perturb_bf16: tensor too large");
-  perturb_bf16_kernel<<<(unsigned)blocks, 256, 0, s>>>(w, n, seed, pair, tensor, sigma, plus, minus);
+  perturb_bf16_kernel<<<(unsigned)blocks, kPerturbThreads, 0, s>>>(w, n, seed, pair, tensor, sigma, plus, minus);
   ENNX_LAUNCH_CHECK("perturb_bf16 launch");
   return ENNX_B200_OK;
 }

@@ -108,7 +108,7 @@ __device__ __forceinline__ TileInfo decode_tile(const Smem& s, const Args& a, in
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
 template <bool PAIR>
-__global__ void __launch_bounds__(THREADS, 1)
+__global__ void __launch_bounds__(THREADS, 2)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      const __grid_constant__ CUtensorMap tmC, Args a) {
   extern __shared__ uint8_t smem_raw[];

@@ -16,15 +16,31 @@ namespace ennx {
 // Router: a register-blocked fp32 SIMT GEMM.  A block owns RT consecutive
 // tokens of one weight set and all experts (in tiles of RE); K is staged
 // through shared memory in chunks of RK, converted from bf16 to fp32 once.
-// Thread (ty, tx) accumulates tokens 4*ty..4*ty+3 x experts 4*tx..4*tx+3,
+// Thread (ty, tx) accumulates tokens 8*ty..8*ty+7 x experts 4*tx..4*tx+3,
 // each logit one serial fma chain over k = 0, 1, ..., H-1 starting from 0 --
 // the order of the reference's per-token loop (kda_moe.metal:589-595) and of
-// the CPU oracle, so logits are bit-identical.  The logits of the block's
-// tokens are kept in shared memory; one thread per token then runs the
-// insertion top-k and the gate softmax.
-constexpr int RT = 32, RE = 64, RK = 32, kRouterThreads = 128;
+// the CPU oracle, so logits are bit-identical.  The serial chain rules out
+// splitting K; the parallelism comes from 32 independent chains per thread,
+// issued as 16 packed fma.rn.f32x2 per k-step (two independent IEEE fma.rn
+// each), with operands loaded one k-step ahead.  The logits of the block's tokens
+// are kept in shared memory; one thread per token then runs the insertion
+// top-k and the gate softmax.
+constexpr int RT = 64, RE = 64, RK = 32, kRouterThreads = 128;
 
-__global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+// two independent IEEE fma.rn in one instruction (sm_100)
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+constexpr int kStageLoads = RK * RT / 8 / kRouterThreads;  // uint4 per thread per chunk (x, and w alike)
+
+__global__ void __launch_bounds__(kRouterThreads, 1) router_topk_kernel(
     const uint16_t* __restrict__ x, long long ldx, const uint16_t* __restrict__ w0, const uint16_t* __restrict__ w1,
     long long split, long long tokens, int hidden, int experts, int top_k, float* __restrict__ logits,
     int* __restrict__ idx, float* __restrict__ gate) {
@@ -43,62 +59,73 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
     tb = split + ((long long)blockIdx.x - nb0) * RT; te = min(tokens, tb + RT); w = w1;
   }
   const int nchunks = hidden / RK;
-  // global -> register staging: x: one uint4 (8 k of one token); w: two
-  const int xt = tid % RT, xq = tid / RT;  // token, 8-wide k group
   for (int e0 = 0; e0 < experts; e0 += RE) {
-    uint4 rx, rw[2];
+    // global -> register staging, uint4 (8 k of one token / expert) each
+    uint4 rx[kStageLoads], rw[kStageLoads];
     auto fetch = [&](int c) {
-      const long long t = tb + xt;
-      rx = t < te ? __ldg(reinterpret_cast<const uint4*>(x + t * ldx + c * RK + 8 * xq)) : make_uint4(0, 0, 0, 0);
 #pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int li = tid + i * kRouterThreads, e = e0 + li % RE, q = li / RE;
-        rw[i] = e < experts ? __ldg(reinterpret_cast<const uint4*>(w + (long long)e * hidden + c * RK + 8 * q))
+      for (int i = 0; i < kStageLoads; ++i) {
+        const int li = tid + i * kRouterThreads, t = li % RT, q = li / RT;
+        rx[i] = tb + t < te ? __ldg(reinterpret_cast<const uint4*>(x + (tb + t) * ldx + c * RK + 8 * q))
+                            : make_uint4(0, 0, 0, 0);
+        const int e = e0 + li % RE, qe = li / RE;
+        rw[i] = e < experts ? __ldg(reinterpret_cast<const uint4*>(w + (long long)e * hidden + c * RK + 8 * qe))
                             : make_uint4(0, 0, 0, 0);
       }
     };
     auto stash = [&](int buf) {
       float* a = As + buf * RK * RT;
       float* bb = Bs + buf * RK * RE;
-      const uint32_t xv[4] = {rx.x, rx.y, rx.z, rx.w};
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        a[(8 * xq + 2 * h) * RT + xt] = bf16_to_f32((uint16_t)(xv[h] & 0xffffu));
-        a[(8 * xq + 2 * h + 1) * RT + xt] = bf16_to_f32((uint16_t)(xv[h] >> 16));
-      }
-#pragma unroll
-      for (int i = 0; i < 2; ++i) {
-        const int li = tid + i * kRouterThreads, e = li % RE, q = li / RE;
+      for (int i = 0; i < kStageLoads; ++i) {
+        const int li = tid + i * kRouterThreads;
+        const int t = li % RT, q = li / RT, e = li % RE, qe = li / RE;
+        const uint32_t xv[4] = {rx[i].x, rx[i].y, rx[i].z, rx[i].w};
         const uint32_t wv[4] = {rw[i].x, rw[i].y, rw[i].z, rw[i].w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
-          bb[(8 * q + 2 * h) * RE + e] = bf16_to_f32((uint16_t)(wv[h] & 0xffffu));
-          bb[(8 * q + 2 * h + 1) * RE + e] = bf16_to_f32((uint16_t)(wv[h] >> 16));
+          a[(8 * q + 2 * h) * RT + t] = bf16_to_f32((uint16_t)(xv[h] & 0xffffu));
+          a[(8 * q + 2 * h + 1) * RT + t] = bf16_to_f32((uint16_t)(xv[h] >> 16));
+          bb[(8 * qe + 2 * h) * RE + e] = bf16_to_f32((uint16_t)(wv[h] & 0xffffu));
+          bb[(8 * qe + 2 * h + 1) * RE + e] = bf16_to_f32((uint16_t)(wv[h] >> 16));
         }
       }
     };
-    float acc[4][4];
+    uint64_t accp[4][4];  // accp[i][j] = (logit of token 8ty+2i, of token 8ty+2i+1) for expert 4tx+j
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[i][j] = 0.0f;
+      for (int j = 0; j < 4; ++j) accp[i][j] = 0ull;
     __syncthreads();  // previous expert tile's readers are done with the buffers
     fetch(0);
     stash(0);
     __syncthreads();
     for (int c = 0; c < nchunks; ++c) {
       if (c + 1 < nchunks) fetch(c + 1);
-      const float* a = As + (c & 1) * RK * RT + 4 * ty;
+      const float* a = As + (c & 1) * RK * RT + 8 * ty;
       const float* bb = Bs + (c & 1) * RK * RE + 4 * tx;
+      // operands one k-step ahead; the FMAs run as packed pairs over tokens
+      // (fma.rn.f32x2: two independent fma.rn per instruction)
+      float4 a0 = *reinterpret_cast<const float4*>(a), a1 = *reinterpret_cast<const float4*>(a + 4);
+      float4 b0 = *reinterpret_cast<const float4*>(bb);
 #pragma unroll
       for (int k = 0; k < RK; ++k) {
-        const float4 av = *reinterpret_cast<const float4*>(a + k * RT);
-        const float4 bv = *reinterpret_cast<const float4*>(bb + k * RE);
-        const float ar[4] = {av.x, av.y, av.z, av.w}, br[4] = {bv.x, bv.y, bv.z, bv.w};
+        float4 na0, na1, nb0v;
+        if (k + 1 < RK) {
+          na0 = *reinterpret_cast<const float4*>(a + (k + 1) * RT);
+          na1 = *reinterpret_cast<const float4*>(a + (k + 1) * RT + 4);
+          nb0v = *reinterpret_cast<const float4*>(bb + (k + 1) * RE);
+        }
+        const uint64_t ap[4] = {pack_f32x2(a0.x, a0.y), pack_f32x2(a0.z, a0.w), pack_f32x2(a1.x, a1.y),
+                                pack_f32x2(a1.z, a1.w)};
+        const float br[4] = {b0.x, b0.y, b0.z, b0.w};
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int j = 0; j < 4; ++j) {
+          const uint64_t bj = pack_f32x2(br[j], br[j]);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(ar[i], br[j], acc[i][j]);
+          for (int i = 0; i < 4; ++i) accp[i][j] = fma_f32x2(ap[i], bj, accp[i][j]);
+        }
+        if (k + 1 < RK) { a0 = na0; a1 = na1; b0 = nb0v; }
       }
       if (c + 1 < nchunks) stash((c + 1) & 1);
       __syncthreads();
@@ -106,7 +133,10 @@ __global__ void __launch_bounds__(kRouterThreads) router_topk_kernel(
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) Ls[(4 * ty + i) * lds + e0 + 4 * tx + j] = acc[i][j];
+      for (int j = 0; j < 4; ++j) {
+        Ls[(8 * ty + 2 * i) * lds + e0 + 4 * tx + j] = __uint_as_float((uint32_t)accp[i][j]);
+        Ls[(8 * ty + 2 * i + 1) * lds + e0 + 4 * tx + j] = __uint_as_float((uint32_t)(accp[i][j] >> 32));
+      }
   }
   __syncthreads();
   if (logits) {

@@ -193,33 +193,40 @@ constexpr int kPerturbThreads = 128;
 __global__ void __launch_bounds__(kPerturbThreads) perturb_bf16_kernel(const uint16_t* __restrict__ w, uint64_t n, uint64_t seed,
                                                            uint32_t pair, uint32_t tensor, float sigma,
                                                            uint16_t* __restrict__ plus, uint16_t* __restrict__ minus) {
-  const uint64_t groups = (n + 7) / 8;
+  const uint64_t groups = (n + 7) / 8, full = n / 8;
   const uint64_t g0 = (uint64_t)blockIdx.x * (kPerturbThreads * kPerturbGroupsPerThread) + threadIdx.x;
+  // all of this thread's loads first (streaming: the base weights are read
+  // once per pair and do not fit in L2), then the noise and the stores
+  uint4 raw[kPerturbGroupsPerThread];
+#pragma unroll
+  for (int it = 0; it < kPerturbGroupsPerThread; ++it) {
+    const uint64_t g = g0 + (uint64_t)it * kPerturbThreads;
+    raw[it] = g < full ? __ldcs(reinterpret_cast<const uint4*>(w) + g) : make_uint4(0, 0, 0, 0);
+  }
 #pragma unroll
   for (int it = 0; it < kPerturbGroupsPerThread; ++it) {
     const uint64_t g = g0 + (uint64_t)it * kPerturbThreads;
     if (g >= groups) return;
-    uint64_t e0 = g * 8;
+    const uint64_t e0 = g * 8;
     float z[8];
     noise8(seed, pair, tensor, g, z);
-    if (e0 + 8 <= n) {
-      uint4 raw = *reinterpret_cast<const uint4*>(w + e0);
-      uint32_t in[4] = {raw.x, raw.y, raw.z, raw.w};
+    if (g < full) {
+      const uint32_t in[4] = {raw[it].x, raw[it].y, raw[it].z, raw[it].w};
       uint32_t p[4], m[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        float a = bf16_to_f32((uint16_t)(in[j] & 0xffffu));
-        float b = bf16_to_f32((uint16_t)(in[j] >> 16));
-        float sa = __fmul_rn(sigma, z[2 * j]), sb = __fmul_rn(sigma, z[2 * j + 1]);
-        p[j] = (uint32_t)f32_to_bf16_rne(__fadd_rn(a, sa)) | ((uint32_t)f32_to_bf16_rne(__fadd_rn(b, sb)) << 16);
-        m[j] = (uint32_t)f32_to_bf16_rne(__fsub_rn(a, sa)) | ((uint32_t)f32_to_bf16_rne(__fsub_rn(b, sb)) << 16);
+        const float a = bf16_to_f32((uint16_t)(in[j] & 0xffffu));
+        const float b = bf16_to_f32((uint16_t)(in[j] >> 16));
+        const float sa = __fmul_rn(sigma, z[2 * j]), sb = __fmul_rn(sigma, z[2 * j + 1]);
+        p[j] = pack_bf16x2(__fadd_rn(a, sa), __fadd_rn(b, sb));
+        m[j] = pack_bf16x2(__fsub_rn(a, sa), __fsub_rn(b, sb));
       }
-      *reinterpret_cast<uint4*>(plus + e0) = make_uint4(p[0], p[1], p[2], p[3]);
-      if (minus) *reinterpret_cast<uint4*>(minus + e0) = make_uint4(m[0], m[1], m[2], m[3]);
+      __stcs(reinterpret_cast<uint4*>(plus) + g, make_uint4(p[0], p[1], p[2], p[3]));
+      if (minus) __stcs(reinterpret_cast<uint4*>(minus) + g, make_uint4(m[0], m[1], m[2], m[3]));
     } else {
       for (uint64_t e = e0; e < n; ++e) {
-        float a = bf16_to_f32(w[e]);
-        float sg = __fmul_rn(sigma, z[e - e0]);
+        const float a = bf16_to_f32(w[e]);
+        const float sg = __fmul_rn(sigma, z[e - e0]);
         plus[e] = f32_to_bf16_rne(__fadd_rn(a, sg));
         if (minus) minus[e] = f32_to_bf16_rne(__fsub_rn(a, sg));
       }

@@ -35,6 +35,9 @@ POP = 32          # candidates (16 antithetic pairs)
 BATCH, SEQ = 4, 1024
 SIGMA = 1e-3
 METRIC = "Qwen-hybrid forward tokens/s at 1/2/4/8 B200; kernel % of roofline"
+# DRAM bytes per tcgen05 GEMM launch over one full forward step (2416 launches,
+# 849.15 GB), from the ncu capture summarised in profiles/gemm_forward_traffic.md.
+GEMM_DRAM_BYTES_PER_LAUNCH = 351.47e6
 CONFIG = {"workload": "hybrid KDA/GQA-MoE forward, 32 antithetic candidates (sigma 1e-3, Philox), "
                       "batch 4 x seq 1024 each, mean CE fitness",
           "layers": 24, "hidden": 2048, "pattern": "[KDA,KDA,KDA,GQA]x6", "q_heads": 16, "kv_heads": 4,
@@ -314,7 +317,9 @@ def run_ours(args):
                                                           "GEMMs)",
                              "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s", "frac": achieved / tf_sust,
                              "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
-                             "traffic": None,
+                             "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,
+                             "traffic_unit": "bytes per launch (ncu dram__bytes_read+write, one forward step)",
+                             "algorithmic_bytes_per_launch": g_bytes / max(1, g_launch),
                              "algorithmic_flops_per_launch": g_flops / max(1, g_launch),
                              "avg_launch_ms": g_ms / max(1, g_launch)},
                 "kernel_breakdown": breakdown,

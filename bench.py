@@ -211,6 +211,10 @@ def run_ours(args):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     if world > 1:
+        # The only collectives are a 128-byte fitness gather and an 8-byte seed
+        # broadcast per step: NVLink SHARP (multicast) buffers bring nothing
+        # for them, so their setup is skipped.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     _abi.check(_abi.lib().ennx_b200_device_check(), "device_check")
     pairs = POP // 2

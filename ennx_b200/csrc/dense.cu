@@ -190,9 +190,13 @@ __global__ void dense_linear_kernel(const float* __restrict__ x, const float* __
 // kernels on the same SMs (this kernel runs on a low-priority stream).
 constexpr int kPerturbGroupsPerThread = 4;
 constexpr int kPerturbThreads = 128;
+// cols == 0: outputs are contiguous like the input; otherwise element e of the
+// row-major [n / cols, cols] tensor goes to (e / cols) * dld + e % cols of the
+// outputs (a block of a wider matrix; cols % 8 == 0).
 __global__ void __launch_bounds__(kPerturbThreads) perturb_bf16_kernel(const uint16_t* __restrict__ w, uint64_t n, uint64_t seed,
                                                            uint32_t pair, uint32_t tensor, float sigma,
-                                                           uint16_t* __restrict__ plus, uint16_t* __restrict__ minus) {
+                                                           uint16_t* __restrict__ plus, uint16_t* __restrict__ minus,
+                                                           uint32_t cols, uint64_t dld) {
   const uint64_t groups = (n + 7) / 8, full = n / 8;
   const uint64_t g0 = (uint64_t)blockIdx.x * (kPerturbThreads * kPerturbGroupsPerThread) + threadIdx.x;
   // all of this thread's loads first (streaming: the base weights are read
@@ -221,14 +225,16 @@ __global__ void __launch_bounds__(kPerturbThreads) perturb_bf16_kernel(const uin
         p[j] = pack_bf16x2(__fadd_rn(a, sa), __fadd_rn(b, sb));
         m[j] = pack_bf16x2(__fsub_rn(a, sa), __fsub_rn(b, sb));
       }
-      __stcs(reinterpret_cast<uint4*>(plus) + g, make_uint4(p[0], p[1], p[2], p[3]));
-      if (minus) __stcs(reinterpret_cast<uint4*>(minus) + g, make_uint4(m[0], m[1], m[2], m[3]));
+      const uint64_t d = cols ? (e0 / cols) * dld + e0 % cols : e0;
+      __stcs(reinterpret_cast<uint4*>(plus + d), make_uint4(p[0], p[1], p[2], p[3]));
+      if (minus) __stcs(reinterpret_cast<uint4*>(minus + d), make_uint4(m[0], m[1], m[2], m[3]));
     } else {
       for (uint64_t e = e0; e < n; ++e) {
         const float a = bf16_to_f32(w[e]);
         const float sg = __fmul_rn(sigma, z[e - e0]);
-        plus[e] = f32_to_bf16_rne(__fadd_rn(a, sg));
-        if (minus) minus[e] = f32_to_bf16_rne(__fsub_rn(a, sg));
+        const uint64_t d = cols ? (e / cols) * dld + e % cols : e;
+        plus[d] = f32_to_bf16_rne(__fadd_rn(a, sg));
+        if (minus) minus[d] = f32_to_bf16_rne(__fsub_rn(a, sg));
       }
     }
   }
@@ -306,6 +312,26 @@ int grid_for(uint64_t n, int threads) {
 }  // namespace ennx
 
 using namespace ennx;
+
+namespace ennx {
+int32_t launch_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor, float sigma,
+                            uint16_t* plus, uint16_t* minus, uint32_t cols, uint64_t dld, cudaStream_t s) {
+  if (!w || !plus || n == 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16 needs input and output");
+  if (((uintptr_t)w | (uintptr_t)plus | (uintptr_t)minus) & 15u)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16 buffers must be 16-byte aligned");
+  if (!isfinite(sigma)) return set_error(ENNX_B200_INVALID_ARGUMENT, "sigma must be finite");
+  if (cols && (cols % 8 || n % cols || dld % 8 || dld < cols))
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16: strided output needs cols %% 8 == 0 and dld >= cols");
+  uint64_t groups = (n + 7) / 8;
+  uint64_t per_block = kPerturbThreads * kPerturbGroupsPerThread;
+  uint64_t blocks = (groups + per_block - 1) / per_block;
+  if (blocks > 0x7fffffffull) return set_error(ENNX_B200_UNSUPPORTED, "perturb_bf16: tensor too large");
+  perturb_bf16_kernel<<<(unsigned)blocks, kPerturbThreads, 0, s>>>(w, n, seed, pair, tensor, sigma, plus, minus,
+                                                                    cols, dld);
+  ENNX_LAUNCH_CHECK("perturb_bf16 launch");
+  return ENNX_B200_OK;
+}
+}  // namespace ennx
 
 extern "C" {
 
@@ -387,18 +413,7 @@ int32_t ennx_b200_dense_linear_f32(const float* input, size_t columns, const flo
 
 int32_t ennx_b200_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor,
                                float sigma, uint16_t* plus, uint16_t* minus, void* stream) {
-  cudaStream_t s = (cudaStream_t)stream;
-  if (!w || !plus || n == 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16 needs input and output");
-  if (((uintptr_t)w | (uintptr_t)plus | (uintptr_t)minus) & 15u)
-    return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16 buffers must be 16-byte aligned");
-  if (!isfinite(sigma)) return set_error(ENNX_B200_INVALID_ARGUMENT, "sigma must be finite");
-  uint64_t groups = (n + 7) / 8;
-  uint64_t per_block = kPerturbThreads * kPerturbGroupsPerThread;
-  uint64_t blocks = (groups + per_block - 1) / per_block;
-  if (blocks > 0x7fffffffull) return set_error(ENNX_B200_UNSUPPORTED, "perturb_bf16: tensor too large");
-  perturb_bf16_kernel<<<(unsigned)blocks, kPerturbThreads, 0, s>>>(w, n, seed, pair, tensor, sigma, plus, minus);
-  ENNX_LAUNCH_CHECK("perturb_bf16 launch");
-  return ENNX_B200_OK;
+  return ennx::launch_perturb_bf16(w, n, seed, pair, tensor, sigma, plus, minus, 0, 0, (cudaStream_t)stream);
 }
 
 }  // extern "C"

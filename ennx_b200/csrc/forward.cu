@@ -21,6 +21,8 @@
 #include <algorithm>
 #include <vector>
 
+#include <stdlib.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -162,13 +164,32 @@ Shapes layer_shapes(const ennx_b200_model_config& c, bool gqa) {
 
 size_t align_elems(long long n) { return (size_t)((n + 127) / 128 * 128); }  // 256-byte granules of bf16
 
+// Scratch layout of the perturbed copies of one layer.  On KDA layers the
+// QKV projection and the control projection share one region, [W_qkv; W_ctl]
+// per sign, so one GEMM of N = rows(qkv) + rows(ctl) computes both; the
+// forget and output-gate projections share a block-diagonal [2*hw, 2*r]
+// matrix [[W_f, 0], [0, W_o]] per sign, so one GEMM with K = 2r over
+// ctl[:, 0:2r] computes [f | og].  The off-diagonal blocks are zeroed once
+// per call and never written.
+long long field_elems(const Shapes& sh, int f) {
+  switch (f) {
+    case F_QKV: return (sh.rows[F_QKV] + sh.rows[F_CTL]) * sh.cols[F_QKV];
+    case F_CTL: return 0;
+    case F_FORGET: return 4 * sh.rows[F_FORGET] * sh.cols[F_FORGET];
+    case F_OGATE: return 0;
+    default: return sh.rows[f] * sh.cols[f];
+  }
+}
+// leading dimension of the fused QKV(+control) GEMM output
+long long qkv_ld(const Shapes& sh) { return (sh.rows[F_QKV] + sh.rows[F_CTL] + 7) / 8 * 8; }
+
 struct Work {
   const int* tokens;       // caller's [batch, seq + 1] token ids
   uint16_t *emb_scr[2];    // two slots of [2][V*H] (plus, minus)
   uint16_t *fnorm_scr[2];  // two slots of [2][H]
   uint16_t *layer_scr[2];  // two slots of per-field [2][n] areas
   size_t field_off[F_COUNT];  // element offsets into layer_scr (for the plus copy; minus follows)
-  uint16_t *hidden, *xn, *qkv, *ctl, *fg, *og, *o, *post;
+  uint16_t *hidden, *xn, *qkv, *fg, *o, *post;
   float *gate, *beta;
   int *inp, *tgt;
   float *lse, *tlogit, *row_loss;
@@ -204,22 +225,19 @@ void carve_work(const ennx_b200_model_config& c, int batch, int seq, uint8_t* ba
   for (int g = 0; g < 2; ++g) {
     Shapes sh = layer_shapes(c, g == 1);
     for (int f = 0; f < F_COUNT; ++f) {
-      size_t n = align_elems(sh.rows[f] * sh.cols[f]);
+      size_t n = align_elems(field_elems(sh, f));
       if (n > per_field_max[f]) per_field_max[f] = n;
     }
   }
   size_t off = 0;
   for (int f = 0; f < F_COUNT; ++f) { w.field_off[f] = off; off += 2 * per_field_max[f]; }
   for (int k = 0; k < 2; ++k) w.layer_scr[k] = cv.take<uint16_t>(off);
-  const long long qkv_cols = std::max(3LL * c.kda_heads, (long long)(c.q_heads + 2 * c.kv_heads)) * HD;
+  const long long qkv_cols = std::max(qkv_ld(layer_shapes(c, false)), qkv_ld(layer_shapes(c, true)));
   const long long heads_max = std::max(c.kda_heads, c.q_heads);
-  const long long ctl_cols = (2LL * c.gate_rank + c.kda_heads + 7) / 8 * 8;
   w.hidden = cv.take<uint16_t>(T * H);
   w.xn = cv.take<uint16_t>(T * H);
   w.qkv = cv.take<uint16_t>(T * qkv_cols);
-  w.ctl = cv.take<uint16_t>(T * ctl_cols);
-  w.fg = cv.take<uint16_t>(T * c.kda_heads * HD);
-  w.og = cv.take<uint16_t>(T * c.kda_heads * HD);
+  w.fg = cv.take<uint16_t>(T * 2 * c.kda_heads * HD);  // [forget | output gate]
   w.o = cv.take<uint16_t>(T * heads_max * HD);
   w.post = cv.take<uint16_t>(T * c.kda_heads * HD);
   w.gate = cv.take<float>(T * c.kda_heads * HD);
@@ -255,14 +273,14 @@ const uint16_t* field_ptr(const ennx_b200_layer_weights& L, int f) {
 }
 
 int32_t perturb_pair(const uint16_t* src, long long n, uint64_t seed, uint32_t pair, uint32_t tensor, float sigma,
-                     uint16_t* dst_plus, uint16_t* dst_minus, cudaStream_t s) {
+                     uint16_t* dst_plus, uint16_t* dst_minus, cudaStream_t s, uint32_t cols = 0, long long dld = 0) {
   if (!src) return set_error(ENNX_B200_INVALID_ARGUMENT, "missing weight tensor %u", tensor);
   ProfScope ps("perturb", s, 0, 6.0 * n);
-  return ennx_b200_perturb_bf16(src, (size_t)n, seed, pair, tensor, sigma, dst_plus, dst_minus, s);
+  return launch_perturb_bf16(src, (size_t)n, seed, pair, tensor, sigma, dst_plus, dst_minus, cols, (uint64_t)dld, s);
 }
 
 int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* b, long long n, long long k, void* c, long long ldc,
-              long long rows, const uint16_t* residual, cudaStream_t s) {
+              long long rows, const uint16_t* residual, cudaStream_t s, double useful_flops = 0.0) {
   ennx_b200_gemm_params p;
   memset(&p, 0, sizeof(p));
   p.m = (int)rows; p.n = (int)n; p.k = (int)k;
@@ -270,7 +288,8 @@ int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* b, long long n, 
   p.groups = 2; p.b_group_rows = (int)n;
   p.epilogue = ENNX_B200_EPI_BF16; p.alpha = 1.0f;
   p.residual = residual; p.ldr = ldc;
-  ProfScope ps("gemm", s, 2.0 * rows * n * k, 2.0 * (rows * k + 2.0 * n * k + rows * n * (residual ? 2 : 1)));
+  ProfScope ps("gemm", s, useful_flops > 0.0 ? useful_flops : 2.0 * rows * n * k,
+               2.0 * (rows * k + 2.0 * n * k + rows * n * (residual ? 2 : 1)));
   return gemm_bf16(&p, a, b, c, s);
 }
 
@@ -311,11 +330,21 @@ LayerPtrs layer_ptrs(const ennx_b200_model_config& c, int l, const Work& w, int 
   for (int f = 0; f < F_COUNT; ++f) {
     long long n = sh.rows[f] * sh.cols[f];
     lp.P[f] = lp.M[f] = nullptr;
-    if (n == 0) continue;
+    if (n == 0 || f == F_CTL || f == F_OGATE) continue;
     lp.P[f] = w.layer_scr[slot] + w.field_off[f];
     // minus copy directly after plus (GEMM operands: n % 64 == 0, so the
     // B row-block stride between the two signs is exactly `rows`)
-    lp.M[f] = lp.P[f] + (n % 8 == 0 ? (size_t)n : align_elems(n));
+    const long long fn = field_elems(sh, f);
+    lp.M[f] = lp.P[f] + (fn % 8 == 0 ? (size_t)fn : align_elems(fn));
+  }
+  if (sh.rows[F_CTL]) {  // control rows follow the QKV rows of each sign
+    lp.P[F_CTL] = lp.P[F_QKV] + sh.rows[F_QKV] * sh.cols[F_QKV];
+    lp.M[F_CTL] = lp.M[F_QKV] + sh.rows[F_QKV] * sh.cols[F_QKV];
+  }
+  if (sh.rows[F_OGATE]) {  // output-gate block: rows [hw, 2hw), columns [r, 2r)
+    const long long hw = sh.rows[F_FORGET], r = sh.cols[F_FORGET];
+    lp.P[F_OGATE] = lp.P[F_FORGET] + hw * 2 * r + r;
+    lp.M[F_OGATE] = lp.M[F_FORGET] + hw * 2 * r + r;
   }
   return lp;
 }
@@ -329,7 +358,10 @@ int32_t perturb_layer(const ennx_b200_model_config& c, const ennx_b200_model_wei
   for (int f = 0; f < F_COUNT; ++f) {
     long long n = sh.rows[f] * sh.cols[f];
     if (n == 0) continue;
-    ENNX_TRY(perturb_pair(field_ptr(L, f), n, seed, pair, 16 + 16 * l + f, sigma, lp.P[f], lp.M[f], s));
+    // forget / output-gate weights land as blocks of the block-diagonal matrix
+    const bool blk = f == F_FORGET || f == F_OGATE;
+    ENNX_TRY(perturb_pair(field_ptr(L, f), n, seed, pair, 16 + 16 * l + f, sigma, lp.P[f], lp.M[f], s,
+                          blk ? (uint32_t)sh.cols[f] : 0u, blk ? 2 * sh.cols[f] : 0));
   }
   return ENNX_B200_OK;
 }
@@ -343,8 +375,9 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
   uint16_t* const* P = lp.P;
   uint16_t* const* M = lp.M;
   ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_ATTN_NORM], M[F_ATTN_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
-  const long long qkv_cols = sh.rows[F_QKV];
-  ENNX_TRY(gemm2(w.xn, H, P[F_QKV], qkv_cols, H, w.qkv, qkv_cols, T, nullptr, s));
+  // one GEMM: [q | k | v] (and on KDA layers the control projection after them)
+  const long long qkv_cols = qkv_ld(sh);
+  ENNX_TRY(gemm2(w.xn, H, P[F_QKV], sh.rows[F_QKV] + sh.rows[F_CTL], H, w.qkv, qkv_cols, T, nullptr, s));
   if (gqa) {
     const long long kd = (long long)c.q_heads * HD, vd = kd + (long long)c.kv_heads * HD;
     ENNX_TRY(launch_rope(w.qkv, qkv_cols, c.q_heads, HD, T, seq, c.rope_theta, s));
@@ -358,15 +391,14 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
     ENNX_TRY(gemm2(w.o, kd, P[F_WO], H, kd, w.hidden, H, T, w.hidden, s));
   } else {
     const long long hw = (long long)c.kda_heads * HD, r = c.gate_rank;
-    const long long ctl_cols = sh.rows[F_CTL];
-    const long long ldctl = (ctl_cols + 7) / 8 * 8;
-    ENNX_TRY(gemm2(w.xn, H, P[F_CTL], ctl_cols, H, w.ctl, ldctl, T, nullptr, s));
-    ENNX_TRY(gemm2(w.ctl, ldctl, P[F_FORGET], hw, r, w.fg, hw, T, nullptr, s));
-    ENNX_TRY(gemm2(w.ctl + r, ldctl, P[F_OGATE], hw, r, w.og, hw, T, nullptr, s));
+    const uint16_t* ctl = w.qkv + sh.rows[F_QKV];  // [forget state | output state | beta], row stride qkv_cols
+    // [f | og] = ctl[:, 0:2r] . [[W_f, 0], [0, W_o]]^T
+    ENNX_TRY(gemm2(ctl, qkv_cols, P[F_FORGET], 2 * hw, 2 * r, w.fg, 2 * hw, T, nullptr, s,
+                   2.0 * 2.0 * T * hw * r));  // the zero blocks are not counted as work
     {
       KdaRawGate rg;
-      rg.f = w.fg; rg.ldf = hw;
-      rg.rbeta = w.ctl + 2 * r; rg.ldb = ldctl;
+      rg.f = w.fg; rg.ldf = 2 * hw;
+      rg.rbeta = ctl + 2 * r; rg.ldb = qkv_cols;
       rg.decay0 = P[F_DECAY]; rg.decay1 = M[F_DECAY];
       rg.tb0 = P[F_TB]; rg.tb1 = M[F_TB];
       rg.split_seq = batch;
@@ -376,7 +408,8 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
       ENNX_TRY(launch_kda_chunked(w.qkv, w.qkv + hw, w.qkv + 2 * hw, qkv_cols, nullptr, nullptr, nullptr, w.o, hw,
                                   2 * batch, seq, c.kda_heads, w.kda_ws, w.kda_ws_bytes, s, &rg));
     }
-    ENNX_TRY(launch_kda_post(w.o, w.og, hw, P[F_OUT_NORM], M[F_OUT_NORM], Tc, c.kda_heads, T, c.rms_eps, w.post, s));
+    ENNX_TRY(launch_kda_post(w.o, w.fg + hw, 2 * hw, P[F_OUT_NORM], M[F_OUT_NORM], Tc, c.kda_heads, T, c.rms_eps,
+                             w.post, s));
     ENNX_TRY(gemm2(w.post, hw, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s));
   }
   ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_MOE_NORM], M[F_MOE_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
@@ -395,6 +428,13 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
   PipeStreams* ps = nullptr;
   ENNX_TRY(pipe_streams(&ps));
   cudaStream_t cs = ps->compute, ns = ps->noise;
+  // ENNX_B200_NOISE_STREAM=0 runs the perturbation on the compute stream
+  // (serialised with the layers) instead of overlapping it on its own stream
+  static const bool noise_overlap = [] {
+    const char* e = getenv("ENNX_B200_NOISE_STREAM");
+    return !(e && e[0] == '0');
+  }();
+  if (!noise_overlap) ns = cs;
   cudaEvent_t ev_start = ps->ev[0], ev_done_noise = ps->ev[1];
   cudaEvent_t ready[2] = {ps->ev[2], ps->ev[3]}, freed[2] = {ps->ev[4], ps->ev[5]};
   cudaEvent_t emb_freed[2] = {ps->ev[6], ps->ev[7]};
@@ -405,6 +445,13 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
   ENNX_CUDA(cudaEventRecord(ev_start, caller), "fork");
   ENNX_CUDA(cudaStreamWaitEvent(cs, ev_start, 0), "fork compute");
   ENNX_CUDA(cudaStreamWaitEvent(ns, ev_start, 0), "fork noise");
+  {  // zero the block-diagonal forget/output-gate areas; perturbation fills only the diagonal blocks
+    const long long blkdiag = field_elems(layer_shapes(c, false), F_FORGET);
+    if (blkdiag > 0)
+      for (int k = 0; k < 2; ++k)
+        ENNX_CUDA(cudaMemsetAsync(w.layer_scr[k] + w.field_off[F_FORGET], 0, 2 * (size_t)blkdiag * sizeof(uint16_t), ns),
+                  "zero gate blocks");
+  }
   targets_kernel<<<(unsigned)((Tc + 255) / 256), 256, 0, cs>>>(w.tokens, batch, seq, w.inp, w.tgt);
   ENNX_LAUNCH_CHECK("targets");
 

@@ -65,6 +65,11 @@ int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t*
                            int seq, int heads, void* workspace, size_t workspace_bytes, cudaStream_t s,
                            const KdaRawGate* raw = nullptr);
 
+// dense.cu: W +/- sigma*eps; cols > 0 writes the [n/cols, cols] result as a
+// block of a matrix with row stride dld (noise indexed by the source element)
+int32_t launch_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor, float sigma,
+                            uint16_t* plus, uint16_t* minus, uint32_t cols, uint64_t dld, cudaStream_t s);
+
 // gemm.cu (internal form of ennx_b200_gemm_bf16)
 int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* a, const uint16_t* b, void* c, cudaStream_t s);
 

@@ -9,6 +9,7 @@
 #include <string.h>
 
 #include "common.cuh"
+#include "kernels.cuh"
 
 namespace ennx {
 namespace {
@@ -190,15 +191,16 @@ __global__ void dense_linear_kernel(const float* __restrict__ x, const float* __
 // kernels on the same SMs (this kernel runs on a low-priority stream).
 constexpr int kPerturbGroupsPerThread = 4;
 constexpr int kPerturbThreads = 128;
+// One 8-element group span of a perturbation: block `blk` of the tensor.
 // cols == 0: outputs are contiguous like the input; otherwise element e of the
 // row-major [n / cols, cols] tensor goes to (e / cols) * dld + e % cols of the
 // outputs (a block of a wider matrix; cols % 8 == 0).
-__global__ void __launch_bounds__(kPerturbThreads) perturb_bf16_kernel(const uint16_t* __restrict__ w, uint64_t n, uint64_t seed,
-                                                           uint32_t pair, uint32_t tensor, float sigma,
-                                                           uint16_t* __restrict__ plus, uint16_t* __restrict__ minus,
-                                                           uint32_t cols, uint64_t dld) {
+__device__ __forceinline__ void perturb_block(const uint16_t* __restrict__ w, uint64_t n, uint64_t seed,
+                                              uint32_t pair, uint32_t tensor, float sigma,
+                                              uint16_t* __restrict__ plus, uint16_t* __restrict__ minus,
+                                              uint32_t cols, uint64_t dld, uint64_t blk) {
   const uint64_t groups = (n + 7) / 8, full = n / 8;
-  const uint64_t g0 = (uint64_t)blockIdx.x * (kPerturbThreads * kPerturbGroupsPerThread) + threadIdx.x;
+  const uint64_t g0 = blk * (kPerturbThreads * kPerturbGroupsPerThread) + threadIdx.x;
   // all of this thread's loads first (streaming: the base weights are read
   // once per pair and do not fit in L2), then the noise and the stores
   uint4 raw[kPerturbGroupsPerThread];
@@ -238,6 +240,24 @@ __global__ void __launch_bounds__(kPerturbThreads) perturb_bf16_kernel(const uin
       }
     }
   }
+}
+
+__global__ void __launch_bounds__(kPerturbThreads) perturb_bf16_kernel(const uint16_t* __restrict__ w, uint64_t n,
+                                                                       uint64_t seed, uint32_t pair, uint32_t tensor,
+                                                                       float sigma, uint16_t* __restrict__ plus,
+                                                                       uint16_t* __restrict__ minus, uint32_t cols,
+                                                                       uint64_t dld) {
+  perturb_block(w, n, seed, pair, tensor, sigma, plus, minus, cols, dld, blockIdx.x);
+}
+
+// Several tensors of one antithetic pair in one launch (a layer's weights):
+// block b belongs to the job j with block0[j] <= b < block0[j + 1].
+__global__ void __launch_bounds__(kPerturbThreads) perturb_batch_kernel(const __grid_constant__ PerturbBatch batch) {
+  int j = 0;
+  while (j + 1 < batch.count && blockIdx.x >= batch.block0[j + 1]) ++j;
+  const PerturbJob& jb = batch.job[j];
+  perturb_block(jb.w, jb.n, batch.seed, batch.pair, jb.tensor, batch.sigma, jb.plus, jb.minus, jb.cols, jb.dld,
+                blockIdx.x - batch.block0[j]);
 }
 
 // ---------------------------------------------------------------------------
@@ -331,6 +351,31 @@ int32_t launch_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t
   ENNX_LAUNCH_CHECK("perturb_bf16 launch");
   return ENNX_B200_OK;
 }
+
+int32_t launch_perturb_batch(const PerturbBatch& batch, cudaStream_t s) {
+  if (batch.count <= 0) return ENNX_B200_OK;
+  if (batch.count > kMaxPerturbJobs) return set_error(ENNX_B200_UNSUPPORTED, "perturb batch: too many tensors");
+  if (!isfinite(batch.sigma)) return set_error(ENNX_B200_INVALID_ARGUMENT, "sigma must be finite");
+  PerturbBatch b = batch;
+  const uint64_t per_block = kPerturbThreads * kPerturbGroupsPerThread;
+  uint64_t blocks = 0;
+  for (int j = 0; j < b.count; ++j) {
+    const PerturbJob& jb = b.job[j];
+    if (!jb.w || !jb.plus || jb.n == 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb batch: empty job %d", j);
+    if (((uintptr_t)jb.w | (uintptr_t)jb.plus | (uintptr_t)jb.minus) & 15u)
+      return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb batch: buffers must be 16-byte aligned");
+    if (jb.cols && (jb.cols % 8 || jb.n % jb.cols || jb.dld % 8 || jb.dld < jb.cols))
+      return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb batch: bad strided output");
+    b.block0[j] = (uint32_t)blocks;
+    blocks += ((jb.n + 7) / 8 + per_block - 1) / per_block;
+  }
+  if (blocks > 0x7fffffffull) return set_error(ENNX_B200_UNSUPPORTED, "perturb batch: too many blocks");
+  b.block0[b.count] = (uint32_t)blocks;
+  perturb_batch_kernel<<<(unsigned)blocks, kPerturbThreads, 0, s>>>(b);
+  ENNX_LAUNCH_CHECK("perturb batch launch");
+  return ENNX_B200_OK;
+}
+
 }  // namespace ennx
 
 extern "C" {

@@ -272,13 +272,6 @@ const uint16_t* field_ptr(const ennx_b200_layer_weights& L, int f) {
   }
 }
 
-int32_t perturb_pair(const uint16_t* src, long long n, uint64_t seed, uint32_t pair, uint32_t tensor, float sigma,
-                     uint16_t* dst_plus, uint16_t* dst_minus, cudaStream_t s, uint32_t cols = 0, long long dld = 0) {
-  if (!src) return set_error(ENNX_B200_INVALID_ARGUMENT, "missing weight tensor %u", tensor);
-  ProfScope ps("perturb", s, 0, 6.0 * n);
-  return launch_perturb_bf16(src, (size_t)n, seed, pair, tensor, sigma, dst_plus, dst_minus, cols, (uint64_t)dld, s);
-}
-
 int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* b, long long n, long long k, void* c, long long ldc,
               long long rows, const uint16_t* residual, cudaStream_t s, double useful_flops = 0.0) {
   ennx_b200_gemm_params p;
@@ -350,18 +343,25 @@ LayerPtrs layer_ptrs(const ennx_b200_model_config& c, int l, const Work& w, int 
 }
 
 // noise stream: W +/- sigma*eps of every tensor of layer l into scratch `slot`
-int32_t perturb_layer(const ennx_b200_model_config& c, const ennx_b200_model_weights& W, int l, uint64_t seed,
-                      float sigma, uint32_t pair, const Work& w, int slot, cudaStream_t s) {
+// (appended to `batch`; one launch per layer)
+int32_t add_layer_jobs(const ennx_b200_model_config& c, const ennx_b200_model_weights& W, int l, const Work& w,
+                       int slot, PerturbBatch& batch) {
   const ennx_b200_layer_weights& L = W.layers[l];
   Shapes sh = layer_shapes(c, is_gqa(c, l));
   LayerPtrs lp = layer_ptrs(c, l, w, slot);
   for (int f = 0; f < F_COUNT; ++f) {
     long long n = sh.rows[f] * sh.cols[f];
     if (n == 0) continue;
+    const uint16_t* src = field_ptr(L, f);
+    if (!src) return set_error(ENNX_B200_INVALID_ARGUMENT, "missing weight tensor %d of layer %d", f, l);
+    if (batch.count == kMaxPerturbJobs) return set_error(ENNX_B200_UNSUPPORTED, "too many tensors per layer");
     // forget / output-gate weights land as blocks of the block-diagonal matrix
     const bool blk = f == F_FORGET || f == F_OGATE;
-    ENNX_TRY(perturb_pair(field_ptr(L, f), n, seed, pair, 16 + 16 * l + f, sigma, lp.P[f], lp.M[f], s,
-                          blk ? (uint32_t)sh.cols[f] : 0u, blk ? 2 * sh.cols[f] : 0));
+    PerturbJob& j = batch.job[batch.count++];
+    j.w = src; j.plus = lp.P[f]; j.minus = lp.M[f]; j.n = (uint64_t)n;
+    j.tensor = 16u + 16u * (uint32_t)l + (uint32_t)f;
+    j.cols = blk ? (uint32_t)sh.cols[f] : 0u;
+    j.dld = blk ? 2 * (uint64_t)sh.cols[f] : 0u;
   }
   return ENNX_B200_OK;
 }
@@ -463,10 +463,27 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
     if (l == 0) {
       const int es = i % 2;
       if (emb_freed_recorded[es]) ENNX_CUDA(cudaStreamWaitEvent(ns, emb_freed[es], 0), "wait emb slot");
-      ENNX_TRY(perturb_pair(W.embedding, V * H, seed, pair, 0, sigma, w.emb_scr[es], w.emb_scr[es] + V * H, ns));
-      ENNX_TRY(perturb_pair(W.final_norm, H, seed, pair, 1, sigma, w.fnorm_scr[es], w.fnorm_scr[es] + H, ns));
     }
-    ENNX_TRY(perturb_layer(c, W, l, seed, sigma, pair, w, slot, ns));
+    PerturbBatch batch;
+    memset(&batch, 0, sizeof(batch));
+    batch.seed = seed; batch.pair = pair; batch.sigma = sigma;
+    if (l == 0) {
+      const int es = i % 2;
+      PerturbJob& je = batch.job[batch.count++];
+      je.w = W.embedding; je.plus = w.emb_scr[es]; je.minus = w.emb_scr[es] + V * H; je.n = (uint64_t)(V * H);
+      je.tensor = 0;
+      PerturbJob& jn = batch.job[batch.count++];
+      jn.w = W.final_norm; jn.plus = w.fnorm_scr[es]; jn.minus = w.fnorm_scr[es] + H; jn.n = (uint64_t)H;
+      jn.tensor = 1;
+      if (!W.embedding || !W.final_norm) return set_error(ENNX_B200_INVALID_ARGUMENT, "missing embedding / final norm");
+    }
+    ENNX_TRY(add_layer_jobs(c, W, l, w, slot, batch));
+    {
+      double elems = 0;
+      for (int q = 0; q < batch.count; ++q) elems += (double)batch.job[q].n;
+      ProfScope pp("perturb", ns, 0, 6.0 * elems);
+      ENNX_TRY(launch_perturb_batch(batch, ns));
+    }
     ENNX_CUDA(cudaEventRecord(ready[slot], ns), "ready");
     return ENNX_B200_OK;
   };

@@ -70,6 +70,24 @@ int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t*
 int32_t launch_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor, float sigma,
                             uint16_t* plus, uint16_t* minus, uint32_t cols, uint64_t dld, cudaStream_t s);
 
+// several tensors of one antithetic pair in one launch
+constexpr int kMaxPerturbJobs = 16;
+struct PerturbJob {
+  const uint16_t* w;
+  uint16_t *plus, *minus;
+  uint64_t n, dld;
+  uint32_t tensor, cols;
+};
+struct PerturbBatch {
+  int count;
+  uint32_t pair;
+  uint64_t seed;
+  float sigma;
+  PerturbJob job[kMaxPerturbJobs];
+  uint32_t block0[kMaxPerturbJobs + 1];  // filled by launch_perturb_batch
+};
+int32_t launch_perturb_batch(const PerturbBatch& batch, cudaStream_t s);
+
 // gemm.cu (internal form of ennx_b200_gemm_bf16)
 int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* a, const uint16_t* b, void* c, cudaStream_t s);
 

@@ -51,12 +51,25 @@ class GemmParams(ctypes.Structure):
                 ("lse_partial", ctypes.c_void_p), ("target_logit", ctypes.c_void_p)]
 
 
+class PackedLinear(ctypes.Structure):
+    """ennx_b200_packed_linear: field order of KdaPackedLinear (forward_program.rs:224-235)."""
+    _fields_ = [("byte_offset", ctypes.c_uint64), ("scale_offset", ctypes.c_uint64),
+                ("bias_offset", ctypes.c_uint64), ("input_width", ctypes.c_uint64),
+                ("output_width", ctypes.c_uint64), ("bits", ctypes.c_uint32), ("group_size", ctypes.c_uint32),
+                ("element_offset", ctypes.c_uint64), ("perturb_whole", ctypes.c_uint32),
+                ("perturb_threshold", ctypes.c_uint32)]
+
+
+class PerturbSeed(ctypes.Structure):
+    _fields_ = [("low", ctypes.c_uint32), ("high", ctypes.c_uint32), ("enabled", ctypes.c_uint32)]
+
+
 class ModelConfig(ctypes.Structure):
     _fields_ = [("layers", ctypes.c_int32), ("hidden", ctypes.c_int32), ("vocab", ctypes.c_int32),
                 ("attn_period", ctypes.c_int32), ("q_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
                 ("kda_heads", ctypes.c_int32), ("gate_rank", ctypes.c_int32), ("experts", ctypes.c_int32),
                 ("top_k", ctypes.c_int32), ("expert_width", ctypes.c_int32), ("rms_eps", ctypes.c_float),
-                ("rope_theta", ctypes.c_float)]
+                ("rope_theta", ctypes.c_float), ("residual_scale", ctypes.c_float)]
 
 
 LAYER_FIELDS = ("attn_norm", "w_qkv", "w_ctl", "w_forget", "w_ogate", "decay", "time_bias", "out_norm", "w_o",
@@ -101,6 +114,10 @@ SIGNATURES = {
     "ennx_b200_kda_chunked_noalloc": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P]),
     "ennx_b200_population_workspace_size": (_SZ, [_P, _I32, _I32]),
     "ennx_b200_population_forward": (_I32, [_P, _P, _U64, _F32, _I32, _I32, _P, _I32, _I32, _P, _P, _SZ, _P]),
+    "ennx_b200_packed_dequantize_bf16": (_I32, [_P, _P, _P, _P, PerturbSeed, _P, _P]),
+    "ennx_b200_packed_dequantize_f32": (_I32, [_P, _P, _P, _P, PerturbSeed, _P, _P]),
+    "ennx_b200_packed_linear_workspace_size": (_SZ, [_P]),
+    "ennx_b200_packed_linear_bf16": (_I32, [_P, ctypes.c_int64, _P, _P, _P, _P, PerturbSeed, _P, _P, _SZ, _P]),
     "ennx_b200_profile_begin": (_I32, []),
     "ennx_b200_profile_end": (_I32, [_P, _I32, _P]),
     "ennx_b200_launch_count": (_U64, []),

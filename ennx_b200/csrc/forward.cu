@@ -85,7 +85,7 @@ void carve_moe(Carver& c, long long tokens, int hidden, int experts, int top_k, 
 // expert block 0 of the weights, the rest block 1 (block stride = experts).
 int32_t run_moe(const uint16_t* x, const uint16_t* wr0, const uint16_t* wr1, const uint16_t* wgu, const uint16_t* wd,
                 long long tokens, long long split, int sets, int hidden, int experts, int top_k, int width,
-                const uint16_t* residual, uint16_t* out, MoeBuffers& m, cudaStream_t s) {
+                const uint16_t* residual, uint16_t* out, MoeBuffers& m, cudaStream_t s, float residual_scale = 1.0f) {
   if (width % 128) return set_error(ENNX_B200_UNSUPPORTED, "moe: expert width %d must be a multiple of 128", width);
   long long rows = tokens * top_k;
   {
@@ -93,7 +93,7 @@ int32_t run_moe(const uint16_t* x, const uint16_t* wr0, const uint16_t* wr1, con
                  2.0 * tokens * hidden + 2.0 * sets * experts * hidden + 4.0 * rows * hidden);
     ENNX_TRY(launch_router_topk(x, hidden, wr0, sets > 1 ? wr1 : nullptr, split, tokens, hidden, experts, top_k,
                                 m.logits, m.idx, m.gate, s));
-    ENNX_TRY(launch_moe_permute(m.idx, m.gate, tokens, top_k, experts, split, sets, m.counters, m.offsets,
+    ENNX_TRY(launch_moe_permute(m.idx, m.gate, residual_scale, tokens, top_k, experts, split, sets, m.counters, m.offsets,
                                 m.perm_pos, m.src_row, m.perm_gate, s));
     ENNX_TRY(launch_gather_rows(x, hidden, m.src_row, rows, hidden, m.xperm, s));
   }
@@ -211,6 +211,10 @@ int32_t validate_config(const ennx_b200_model_config* c, int batch, int seq) {
   if (c->top_k < 1 || c->top_k > 8 || c->top_k > c->experts)
     return set_error(ENNX_B200_INVALID_ARGUMENT, "top_k must be in [1, min(8, experts)]");
   if (2 * c->experts > 256) return set_error(ENNX_B200_UNSUPPORTED, "at most 128 experts");
+  if (!isfinite(c->residual_scale) || !isfinite(c->rms_eps))  // KdaMoeLayerRequest::validate, forward_program.rs:431
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "residual scale and RMS epsilon must be finite");
+  if (c->residual_scale == 0.0f)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "residual scale 0 would drop every layer update");
   return ENNX_B200_OK;
 }
 
@@ -273,13 +277,13 @@ const uint16_t* field_ptr(const ennx_b200_layer_weights& L, int f) {
 }
 
 int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* b, long long n, long long k, void* c, long long ldc,
-              long long rows, const uint16_t* residual, cudaStream_t s, double useful_flops = 0.0) {
+              long long rows, const uint16_t* residual, cudaStream_t s, double useful_flops = 0.0, float alpha = 1.0f) {
   ennx_b200_gemm_params p;
   memset(&p, 0, sizeof(p));
   p.m = (int)rows; p.n = (int)n; p.k = (int)k;
   p.lda = lda; p.ldb = k; p.ldc = ldc;
   p.groups = 2; p.b_group_rows = (int)n;
-  p.epilogue = ENNX_B200_EPI_BF16; p.alpha = 1.0f;
+  p.epilogue = ENNX_B200_EPI_BF16; p.alpha = alpha;
   p.residual = residual; p.ldr = ldc;
   ProfScope ps("gemm", s, useful_flops > 0.0 ? useful_flops : 2.0 * rows * n * k,
                2.0 * (rows * k + 2.0 * n * k + rows * n * (residual ? 2 : 1)));
@@ -388,7 +392,7 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
       ENNX_TRY(launch_gqa_attention(w.qkv, qkv_cols, w.qkv + kd, qkv_cols, w.qkv + vd, qkv_cols, w.o, kd, 2 * batch,
                                     seq, c.q_heads, c.kv_heads, s));
     }
-    ENNX_TRY(gemm2(w.o, kd, P[F_WO], H, kd, w.hidden, H, T, w.hidden, s));
+    ENNX_TRY(gemm2(w.o, kd, P[F_WO], H, kd, w.hidden, H, T, w.hidden, s, 0.0, c.residual_scale));
   } else {
     const long long hw = (long long)c.kda_heads * HD, r = c.gate_rank;
     const uint16_t* ctl = w.qkv + sh.rows[F_QKV];  // [forget state | output state | beta], row stride qkv_cols
@@ -410,11 +414,11 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
     }
     ENNX_TRY(launch_kda_post(w.o, w.fg + hw, 2 * hw, P[F_OUT_NORM], M[F_OUT_NORM], Tc, c.kda_heads, T, c.rms_eps,
                              w.post, s));
-    ENNX_TRY(gemm2(w.post, hw, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s));
+    ENNX_TRY(gemm2(w.post, hw, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s, 0.0, c.residual_scale));
   }
   ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_MOE_NORM], M[F_MOE_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
   ENNX_TRY(run_moe(w.xn, P[F_ROUTER], M[F_ROUTER], P[F_GATE_UP], P[F_DOWN], T, Tc, 2, (int)H, c.experts, c.top_k,
-                   c.expert_width, w.hidden, w.hidden, w.moe, s));
+                   c.expert_width, w.hidden, w.hidden, w.moe, s, c.residual_scale));
   return ENNX_B200_OK;
 }
 

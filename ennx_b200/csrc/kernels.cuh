@@ -29,7 +29,9 @@ int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0,
 // set(t) * experts + idx[t, r] (set = t >= split).  Writes group_offsets
 // [sets*experts + 1], perm_pos[t*k + r] (row of (t, r) in permuted order),
 // src_row[pos], perm_gate[pos].  `counters` is scratch int[2*sets*experts].
-int32_t launch_moe_permute(const int* idx, const float* gate, long long tokens, int top_k, int experts, long long split,
+// perm_gate = gate_scale * gate (the residual scale of the layer folded into the combine weights)
+int32_t launch_moe_permute(const int* idx, const float* gate, float gate_scale, long long tokens, int top_k, int experts,
+                           long long split,
                            int sets, int* counters, int* group_offsets, int* perm_pos, int* src_row,
                            float* perm_gate, cudaStream_t s);
 int32_t launch_gather_rows(const uint16_t* x, long long ldx, const int* src_row, long long rows, int width,

@@ -215,7 +215,8 @@ __global__ void moe_scan_kernel(const int* __restrict__ counts, int groups, int*
   if (tid == groups - 1) offsets[groups] = buf[tid];
 }
 
-__global__ void moe_scatter_kernel(const int* __restrict__ idx, const float* __restrict__ gate, long long tokens,
+__global__ void moe_scatter_kernel(const int* __restrict__ idx, const float* __restrict__ gate, float gate_scale,
+                                   long long tokens,
                                    int top_k, int experts, long long split, const int* __restrict__ offsets,
                                    int* __restrict__ cursor, int* __restrict__ perm_pos, int* __restrict__ src_row,
                                    float* __restrict__ perm_gate) {
@@ -226,7 +227,7 @@ __global__ void moe_scatter_kernel(const int* __restrict__ idx, const float* __r
     int pos = offsets[g] + atomicAdd(&cursor[g], 1);
     perm_pos[i] = pos;
     src_row[pos] = (int)t;
-    perm_gate[pos] = gate[i];
+    perm_gate[pos] = gate_scale * gate[i];
   }
 }
 
@@ -310,7 +311,8 @@ int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0,
   return ENNX_B200_OK;
 }
 
-int32_t launch_moe_permute(const int* idx, const float* gate, long long tokens, int top_k, int experts, long long split,
+int32_t launch_moe_permute(const int* idx, const float* gate, float gate_scale, long long tokens, int top_k, int experts,
+                           long long split,
                            int sets, int* counters, int* group_offsets, int* perm_pos, int* src_row,
                            float* perm_gate, cudaStream_t s) {
   int groups = sets * experts;
@@ -320,7 +322,7 @@ int32_t launch_moe_permute(const int* idx, const float* gate, long long tokens, 
   long long n = tokens * top_k;
   moe_count_kernel<<<stride_grid(n, 256), 256, 0, s>>>(idx, tokens, top_k, experts, split, counters);
   moe_scan_kernel<<<1, 1024, 0, s>>>(counters, groups, group_offsets, counters + groups);
-  moe_scatter_kernel<<<stride_grid(n, 256), 256, 0, s>>>(idx, gate, tokens, top_k, experts, split, group_offsets,
+  moe_scatter_kernel<<<stride_grid(n, 256), 256, 0, s>>>(idx, gate, gate_scale, tokens, top_k, experts, split, group_offsets,
                                                           counters + groups, perm_pos, src_row, perm_gate);
   note_launch(2);
   ENNX_LAUNCH_CHECK("moe_permute");

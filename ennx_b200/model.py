@@ -33,6 +33,7 @@ class HybridConfig:
     expert_width: int = 768
     rms_eps: float = 1e-6
     rope_theta: float = 1e6
+    residual_scale: float = 1.0   # decoder_residual scale s (forward_program.rs:356; 0.22 in its tests)
 
     def is_gqa(self, layer: int) -> bool:
         return self.attn_period > 0 and layer % self.attn_period == self.attn_period - 1

@@ -81,6 +81,36 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-6, out: torch.Tens
     return out
 
 
+def packed_dequantize(weights: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor, linear: _abi.PackedLinear,
+                      seed: tuple[int, int, int] = (0, 0, 0), dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+    """Dequantised (and, when seed[2] != 0, code-perturbed) packed weights
+    [output_width, input_width] (see ``ennx_b200_packed_dequantize_*``).
+    weights: uint8 arena, scales/biases: float32 arenas, all on the device."""
+    _check_dev(weights, scales, biases)
+    out = torch.empty(linear.output_width, linear.input_width, device=weights.device, dtype=dtype)
+    fn = "ennx_b200_packed_dequantize_bf16" if dtype == torch.bfloat16 else "ennx_b200_packed_dequantize_f32"
+    if dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("packed_dequantize dtype must be bfloat16 or float32")
+    _abi.call(fn, _ptr(weights), _ptr(scales), _ptr(biases), ctypes.byref(linear), _abi.PerturbSeed(*seed), _ptr(out),
+              _stream())
+    return out
+
+
+def packed_linear(x: torch.Tensor, weights: torch.Tensor, scales: torch.Tensor, biases: torch.Tensor,
+                  linear: _abi.PackedLinear, seed: tuple[int, int, int] = (0, 0, 0)) -> torch.Tensor:
+    """out[t, r] = sum_c x[t, c] * W'[r, c] with the packed (perturbed) weights, bf16 in/out."""
+    _check_dev(x, weights, scales, biases)
+    if x.dtype != torch.bfloat16 or x.dim() != 2 or x.shape[1] != linear.input_width:
+        raise ValueError("packed_linear input must be bfloat16 [tokens, input_width]")
+    x = x.contiguous()
+    out = torch.empty(x.shape[0], linear.output_width, device=x.device, dtype=torch.bfloat16)
+    n = _abi.lib().ennx_b200_packed_linear_workspace_size(ctypes.byref(linear))
+    ws = torch.empty(max(n, 16), device=x.device, dtype=torch.uint8)
+    _abi.call("ennx_b200_packed_linear_bf16", _ptr(x), x.shape[0], _ptr(weights), _ptr(scales), _ptr(biases),
+              ctypes.byref(linear), _abi.PerturbSeed(*seed), _ptr(out), _ptr(ws), ws.numel(), _stream())
+    return out
+
+
 def moe_route(x: torch.Tensor, w_router: torch.Tensor, top_k: int, with_logits: bool = False):
     """Routing indices (bit-exact with the CPU oracle) and renormalised gates."""
     _check_dev(x, w_router)

@@ -244,6 +244,8 @@ typedef struct {
     int32_t kda_heads, gate_rank;    /* KDA, head_dim 128 */
     int32_t experts, top_k, expert_width;
     float rms_eps, rope_theta;
+    float residual_scale;  /* h + s*u at both residual adds of a layer (decoder_residual,
+                              kda_moe.metal:556-565); finite; 1 for the plain residual */
 } ennx_b200_model_config;
 
 /* Device pointers, bf16.  KDA layers use every field; GQA layers use
@@ -289,6 +291,54 @@ ENNX_B200_API int32_t ennx_b200_population_forward(const ennx_b200_model_config*
                                                    const int32_t* tokens, int32_t batch, int32_t seq,
                                                    float* fitness, void* workspace, size_t workspace_bytes,
                                                    void* stream);
+
+/* ---- packed int4/int8 linear (KdaPackedLinear) ------------------------- */
+
+/* Packed affine weights of the reference's native KDA-MoE model: field order
+ * of KdaPackedLinear (rust/crates/ennx/src/forward_program.rs:224-235); the
+ * arenas (`weights` u8, `scales`/`biases` f32) are indexed by the offsets.
+ * Code of (row, column): bits 4 -> two codes per byte, low nibble first;
+ * bits 8 -> one byte; rows start every ceil(input_width * bits / 8) bytes.
+ * Weight = code' * scale[row, group] + bias[row, group] (one fused
+ * multiply-add), group = min(column / group_size, groups - 1). */
+typedef struct {
+    uint64_t byte_offset, scale_offset, bias_offset;
+    uint64_t input_width, output_width;
+    uint32_t bits;          /* 4 or 8 */
+    uint32_t group_size;
+    uint64_t element_offset;
+    uint32_t perturb_whole, perturb_threshold;
+} ennx_b200_packed_linear;
+
+/* PerturbSeed of kda_moe.metal:56-61: when `enabled`, code' is the integer
+ * code moved by whole (+1 with probability threshold/2^32) with reflection at
+ * the code range, driven by the Metal perturb_hash of (seed, element_offset +
+ * row * input_width + column) in 32-bit arithmetic (kda_moe.metal:63-96). */
+typedef struct {
+    uint32_t low, high, enabled;
+} ennx_b200_perturb_seed;
+
+/* Dequantise (and perturb) all rows into out[output_width, input_width]:
+ * packed_dequantize_row_half / _float (kda_moe.metal:451-476) for every row.
+ * Errors as KdaPackedLinear::validate (forward_program.rs:238-249). */
+ENNX_B200_API int32_t ennx_b200_packed_dequantize_bf16(const uint8_t* weights, const float* scales,
+                                                       const float* biases, const ennx_b200_packed_linear* linear,
+                                                       ennx_b200_perturb_seed seed, uint16_t* out, void* stream);
+ENNX_B200_API int32_t ennx_b200_packed_dequantize_f32(const uint8_t* weights, const float* scales,
+                                                      const float* biases, const ennx_b200_packed_linear* linear,
+                                                      ennx_b200_perturb_seed seed, float* out, void* stream);
+
+/* out[t, r] = sum_c x[t, c] * W'[r, c] for tokens x bf16 [tokens,
+ * input_width]: decoder_project_packed (kda_moe.metal:399-420) for M
+ * tokens, as dequantise-into-workspace + tcgen05 GEMM (fp32 accumulation,
+ * bf16 out).  input_width % 64 == 0.  workspace >=
+ * ennx_b200_packed_linear_workspace_size(linear) bytes. */
+ENNX_B200_API size_t ennx_b200_packed_linear_workspace_size(const ennx_b200_packed_linear* linear);
+ENNX_B200_API int32_t ennx_b200_packed_linear_bf16(const uint16_t* x, int64_t tokens, const uint8_t* weights,
+                                                   const float* scales, const float* biases,
+                                                   const ennx_b200_packed_linear* linear,
+                                                   ennx_b200_perturb_seed seed, uint16_t* out, void* workspace,
+                                                   size_t workspace_bytes, void* stream);
 
 /* ---- measurement (CUDA-event timing per kernel class, the counterpart of
  *      the reference's AskProfile / ENNX_CUDA_PROFILE, cuda/src/lib.rs:165-171,

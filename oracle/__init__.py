@@ -76,6 +76,8 @@ def lib():
             "eo_dense_linear_f32": (i32, [P, sz, P, sz, P, View, View, P, sz, P]),
             "eo_trial_hash": (u32, [u32, u32, u32]),
             "eo_perturb_code": (u32, [u32, u32, u32, u32, u32, u32, u32]),
+            "eo_packed_hash": (u32, [u32, u32, u32]),
+            "eo_packed_dequantize": (None, [P, P, P, P, u32, u32, u32, P]),
             "eo_philox4x32_10": (None, [P, P, P]),
             "eo_noise8": (None, [u64, u32, u32, u64, P]),
             "eo_perturb_bf16": (None, [P, sz, u64, u32, u32, f32, ctypes.c_int, P]),
@@ -183,6 +185,27 @@ def dense_linear_f32(x, weight, bias, weight_view, bias_view, terms):
 
 def trial_hash(lo: int, hi: int, element: int) -> int:
     return lib().eo_trial_hash(lo, hi, element)
+
+
+class PackedLinear(ctypes.Structure):
+    """eo_packed_linear: field order of KdaPackedLinear (forward_program.rs:224-235)."""
+    _fields_ = [("byte_offset", ctypes.c_uint64), ("scale_offset", ctypes.c_uint64),
+                ("bias_offset", ctypes.c_uint64), ("input_width", ctypes.c_uint64),
+                ("output_width", ctypes.c_uint64), ("bits", ctypes.c_uint32), ("group_size", ctypes.c_uint32),
+                ("element_offset", ctypes.c_uint64), ("perturb_whole", ctypes.c_uint32),
+                ("perturb_threshold", ctypes.c_uint32)]
+
+
+def packed_hash(lo: int, hi: int, element: int) -> int:
+    return int(lib().eo_packed_hash(lo, hi, element))
+
+
+def packed_dequantize(weights, scales, biases, linear: "PackedLinear", seed=(0, 0, 0)) -> np.ndarray:
+    """float32 [output_width, input_width] of the (perturbed) packed weights."""
+    w, sc, bi = _c(weights, np.uint8), _c(scales, np.float32), _c(biases, np.float32)
+    out = np.zeros((linear.output_width, linear.input_width), np.float32)
+    lib().eo_packed_dequantize(_p(w), _p(sc), _p(bi), ctypes.byref(linear), seed[0], seed[1], seed[2], _p(out))
+    return out
 
 
 def perturb_code(code, lo, hi, element, bits, whole, threshold) -> int:

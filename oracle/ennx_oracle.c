@@ -268,6 +268,60 @@ uint32_t eo_perturb_code(uint32_t code, uint32_t seed_low, uint32_t seed_high, u
 }
 
 /* ------------------------------------------------------------------------ */
+/* Packed int4/int8 affine weights (Metal only in the reference).            */
+/* ------------------------------------------------------------------------ */
+
+/* Metal perturb_hash, kda_moe.metal:63-71 (seed.high XORed last). */
+uint32_t eo_packed_hash(uint32_t low, uint32_t high, uint32_t element) {
+    uint32_t v = low ^ (element * 0x9E3779B9u);
+    v ^= v >> 16;
+    v *= 0x7FEB352Du;
+    v ^= v >> 15;
+    v *= 0x846CA68Bu;
+    v ^= v >> 15;
+    return v ^ high;
+}
+
+/* packed_weight_device (kda_moe.metal:351-395) for every (row, column):
+ * code from the byte arena (int4: low nibble first), integer-code step when
+ * the seed is enabled (kda_moe.metal:73-96, 32-bit element index), then
+ * code * scale + bias as one fused multiply-add. */
+void eo_packed_dequantize(const uint8_t* weights, const float* scales, const float* biases,
+                          const eo_packed_linear* l, uint32_t seed_low, uint32_t seed_high,
+                          uint32_t enabled, float* out) {
+    uint64_t row_bytes = (l->input_width * l->bits + 7) / 8;
+    uint64_t groups = (l->input_width + l->group_size - 1) / l->group_size;
+    uint32_t max_code = (1u << l->bits) - 1u;
+    for (uint64_t r = 0; r < l->output_width; ++r) {
+        for (uint64_t c = 0; c < l->input_width; ++c) {
+            uint32_t epb = l->bits == 4 ? 2u : 1u;
+            uint32_t shift = l->bits == 4 ? (uint32_t)(c & 1u) * 4u : 0u;
+            uint32_t code = ((uint32_t)weights[l->byte_offset + r * row_bytes + c / epb] >> shift) & max_code;
+            if (enabled) {
+                uint32_t element = (uint32_t)l->element_offset + (uint32_t)r * (uint32_t)l->input_width +
+                                   (uint32_t)c;
+                uint32_t random = eo_packed_hash(seed_low, seed_high, element);
+                uint32_t amount = l->perturb_whole + (uint32_t)((random >> 1) < (l->perturb_threshold >> 1));
+                if (amount != 0u) {
+                    if ((random & 1u) == 0u) {
+                        if (code >= amount) code -= amount;
+                        else code = code + amount < max_code ? code + amount : max_code;
+                    } else if (code + amount <= max_code) {
+                        code += amount;
+                    } else {
+                        code = code >= amount ? code - amount : 0u;
+                    }
+                }
+            }
+            uint64_t g = c / l->group_size;
+            if (g > groups - 1) g = groups - 1;
+            uint64_t si = r * groups + g;
+            out[r * l->input_width + c] = fmaf((float)code, scales[l->scale_offset + si], biases[l->bias_offset + si]);
+        }
+    }
+}
+
+/* ------------------------------------------------------------------------ */
 /* Population noise: Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11) with  */
 /* Box-Muller.  Builder-defined -- the reference draws Rademacher signs.     */
 /* ------------------------------------------------------------------------ */

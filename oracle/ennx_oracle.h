@@ -16,7 +16,8 @@
  *     tests/golden/make_golden.py.
  *   - The KDA serial recurrence is pinned by the decode known-answer test of
  *     buck2/tests/metal.rs:371-414.
- *   - RMSNorm, router top-k, SwiGLU, KDA gate/beta and post-norm restate
+ *   - RMSNorm, router top-k, SwiGLU, KDA gate/beta, post-norm and the packed
+ *     int4/int8 dequantisation with its Metal perturb_hash restate
  *     kda_moe.metal; the reference has no CPU test of them (unpinned).
  *   - Philox noise, RoPE, GQA attention, chunked KDA, LM-head cross-entropy
  *     have no reference implementation at all: parity unpinned, the functions
@@ -58,6 +59,18 @@ int32_t eo_dense_linear_f32(const float* input, size_t columns, const float* wei
 uint32_t eo_trial_hash(uint32_t seed_low, uint32_t seed_high, uint32_t element);
 uint32_t eo_perturb_code(uint32_t code, uint32_t seed_low, uint32_t seed_high, uint32_t element,
                          uint32_t bits, uint32_t whole, uint32_t threshold);
+
+/* ---- packed int4/int8 weights (kda_moe.metal, Metal only in the reference) ---- */
+typedef struct {
+    uint64_t byte_offset, scale_offset, bias_offset, input_width, output_width;
+    uint32_t bits, group_size;
+    uint64_t element_offset;
+    uint32_t perturb_whole, perturb_threshold;
+} eo_packed_linear;
+uint32_t eo_packed_hash(uint32_t low, uint32_t high, uint32_t element);
+void eo_packed_dequantize(const uint8_t* weights, const float* scales, const float* biases,
+                          const eo_packed_linear* l, uint32_t seed_low, uint32_t seed_high,
+                          uint32_t enabled, float* out);
 
 /* ---- population noise (builder-defined; no reference counterpart) ---- */
 void eo_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);

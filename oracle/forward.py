@@ -44,6 +44,7 @@ def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pa
     S = S1 - 1
     T = B * S
     H = cfg.hidden
+    rs = float(np.float32(getattr(cfg, "residual_scale", 1.0)))  # decoder_residual scale (kda_moe.metal:556-565)
     inp = tokens[:, :S].reshape(-1)
     tgt = tokens[:, 1:].reshape(-1)
     emb = perturbed(W["embedding"], seed, pair, 0, sigma, sign)
@@ -60,7 +61,7 @@ def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pa
             q = round_bf16(rope(q, cfg.rope_theta))
             k = round_bf16(rope(k, cfg.rope_theta))
             o = round_bf16(gqa_attention(q, k, v)).reshape(T, hq * HEAD_DIM)
-            h = round_bf16((h + gemm(o, P["w_o"])).astype(np.float32))
+            h = round_bf16((h + rs * gemm(o, P["w_o"])).astype(np.float32))
         else:
             nh, r = cfg.kda_heads, cfg.gate_rank
             hw = nh * HEAD_DIM
@@ -81,7 +82,7 @@ def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pa
             inv = 1.0 / np.sqrt((o * o).mean(-1, keepdims=True) + cfg.rms_eps)
             post = o * inv * P["out_norm"].astype(np.float64) * _sig(og.reshape(T, nh, HEAD_DIM).astype(np.float64))
             post = round_bf16(post.reshape(T, hw).astype(np.float32))
-            h = round_bf16((h + gemm(post, P["w_o"])).astype(np.float32))
+            h = round_bf16((h + rs * gemm(post, P["w_o"])).astype(np.float32))
         # MoE
         x = round_bf16(rmsnorm(h, P["moe_norm"], cfg.rms_eps))
         logits = router_logits(to_bf16_bits(x), to_bf16_bits(P["w_router"]))
@@ -94,7 +95,7 @@ def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pa
                 continue
             xe = x[rows]
             act = round_bf16((silu(gemm(xe, wg_[e])) * gemm(xe, wu_[e])).astype(np.float32))
-            out = round_bf16((gemm(act, P["w_down"][e]) * gate[rows, ranks][:, None]).astype(np.float32))
+            out = round_bf16((gemm(act, P["w_down"][e]) * (rs * gate[rows, ranks])[:, None]).astype(np.float32))
             np.add.at(y, rows, out.astype(np.float64))
         h = round_bf16(y.astype(np.float32))
     fnorm = perturbed(W["final_norm"], seed, pair, 1, sigma, sign)

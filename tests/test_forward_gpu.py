@@ -49,6 +49,19 @@ def test_population_forward_matches_oracle(sigma):
     assert np.all(np.abs(fit - np.log(cfg.vocab)) < 1.0)
 
 
+def test_population_forward_residual_scale():
+    # the reference's layer scales both residual updates (residual_scale 0.22
+    # in forward_program.rs:836); same oracle comparison as above
+    import dataclasses
+    cfg = dataclasses.replace(SMALL, residual_scale=0.22)
+    w = init_weights(cfg, seed=5, std=0.05)
+    B, S = 1, 130
+    tok = tokens_for(cfg, B, S, 6)
+    fit = PopulationEvaluator(cfg, w, B, S)(tok.cuda(), seed=11, sigma=1e-3, first_pair=0, num_pairs=1).cpu().numpy()
+    ref = OF.population_forward(cfg, to_bits(w), tok.numpy(), 11, 1e-3, 0, 1)
+    np.testing.assert_allclose(fit, ref, rtol=2e-3, atol=2e-3)
+
+
 def test_population_forward_deterministic():
     cfg = SMALL
     w = init_weights(cfg, seed=2)

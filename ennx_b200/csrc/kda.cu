@@ -96,22 +96,34 @@ __device__ __forceinline__ uint4 pack8(const float f[8]) {
 constexpr int PREP_THREADS = 256;
 constexpr int P_XA = 0;                    // A operand, 2 sub-tiles of 128 rows x 128 B
 constexpr int P_YB = 32768;                // B_b operands, 16(b+1) rows each, 2 sub-tiles
-constexpr int P_GC = P_YB + 40960;         // fp32 [64][128] cumulative log2 decay
+constexpr int P_GC = P_YB + 40960;         // fp32 [64][128] log2 decay, then in-block products X
 constexpr int P_FB = P_GC + C * DK * 4;    // fp32 [4][128] block-to-block decay factors
-constexpr int P_BETA = P_FB + 4 * DK * 4;  // fp32 [64]
+constexpr int P_EB = P_FB + 4 * DK * 4;    // fp32 [4][128] 2^Gc at each block's reference token
+constexpr int P_SB = P_EB + 4 * DK * 4;    // fp32 [4][128] 2^(Gc_C - Gc) at each block's reference token
+constexpr int P_BETA = P_SB + 4 * DK * 4;  // fp32 [64]
+// scratch of the decay-factor phase, in the B operand region (written later)
+constexpr int P_AR = P_YB;                 // fp32 [4][128] per-step factor of each reference token
+constexpr int P_XE = P_YB + 4 * DK * 4;    // fp32 [4][128] in-block product at each block's last token
 constexpr int P_BAR = P_BETA + C * 4;      // mbarrier + TMEM slot
 constexpr int PREP_SMEM = P_BAR + 64 + 1024;
 // after the MMAs complete, the A operand region holds L (then T) and the B
 // operand region the temporaries of the inverse
 constexpr int P_L = P_XA;
 static_assert(C * LF * 4 <= P_YB - P_XA, "L must fit the A operand region");
+static_assert(2 * (PREP_SMEM + 1024) <= 232448, "two prep CTAs per SM");
 static_assert(2 * 16 * 17 * 4 <= 40960 && 32 * 33 * 4 <= 40960, "inverse temporaries must fit the B region");
 
 __host__ __device__ constexpr int yb_off(int b) { return P_YB + 4096 * (b * (b + 1) / 2); }
 __host__ __device__ constexpr int yb_rows(int b) { return 16 * (b + 1); }
 __host__ __device__ constexpr int d_col(int b) { return 8 * b * (b + 1); }  // TMEM column of D_b
 
-__device__ __forceinline__ float softplus_stable(float x) { return fmaxf(x, 0.0f) + log1pf(__expf(-fabsf(x))); }
+// max(x, 0) + log(1 + e^-|x|) on the SFU (log2 / exp2 approximations)
+__device__ __forceinline__ float softplus_stable(float x) { return fmaxf(x, 0.0f) + __logf(1.0f + __expf(-fabsf(x))); }
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __global__ void __launch_bounds__(PREP_THREADS, 2)
     kda_prep_kernel(const uint16_t* __restrict__ qg, const uint16_t* __restrict__ kg, long long ld,
@@ -177,33 +189,47 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
     if (tid < C) beta[tid] = t0 + tid < seq ? bg[(tok0 + t0 + tid) * heads + h] : 0.0f;
   }
   __syncthreads();
-  // ---- inclusive prefix over the chunk's tokens per channel: thread
-  // (channel, half) scans 32 tokens, the upper half then adds the lower total
+  // ---- decay factors in product form: per step a_t = 2^(g_t log2 e);
+  // within each 16-token block b (reference token r_b = 16b) the running
+  // product X_t = 2^(Gc_t - Gc_r) (X_r = 1, >= 2^-108 for g >= -5), and per
+  // block the scalars 2^Gc_r (Eb), 2^(Gc_C - Gc_r) (Sb) and the block-to-block
+  // factor fb.  Thread (channel, half) owns the two blocks of its half.
   {
+    float(*Ar)[DK] = reinterpret_cast<float(*)[DK]>(sm + P_AR);
+    float(*Xe)[DK] = reinterpret_cast<float(*)[DK]>(sm + P_XE);
     const int c = tid & 127, half = tid >> 7;
-    float v[32];
+    float x[32];
 #pragma unroll
-    for (int t = 0; t < 32; ++t) v[t] = Gc[half * 32 + t][c];
+    for (int t = 0; t < 32; ++t) x[t] = ex2(Gc[half * 32 + t][c]);
 #pragma unroll
-    for (int t = 1; t < 32; ++t) v[t] += v[t - 1];
-    if (half == 0) {
+    for (int b2 = 0; b2 < 2; ++b2) {
+      Ar[2 * half + b2][c] = x[16 * b2];
+      x[16 * b2] = 1.0f;
 #pragma unroll
-      for (int t = 0; t < 32; ++t) Gc[t][c] = v[t];
+      for (int t = 1; t < 16; ++t) x[16 * b2 + t] = fmaxf(x[16 * b2 + t] * x[16 * b2 + t - 1], 7.52316e-37f);  // >= 2^-120
+      Xe[2 * half + b2][c] = x[16 * b2 + 15];
     }
-    __syncthreads();
-    if (half == 1) {
-      const float base = Gc[31][c];
 #pragma unroll
-      for (int t = 0; t < 32; ++t) Gc[32 + t][c] = v[t] + base;
+    for (int t = 0; t < 32; ++t) Gc[half * 32 + t][c] = x[t];  // Gc now holds X
+    __syncthreads();
+    if (tid < DK) {
+      float(*Eb)[DK] = reinterpret_cast<float(*)[DK]>(sm + P_EB);
+      float(*Sb)[DK] = reinterpret_cast<float(*)[DK]>(sm + P_SB);
+      float f[4];
+#pragma unroll
+      for (int bb = 1; bb < 4; ++bb) f[bb] = Xe[bb - 1][tid] * Ar[bb][tid];  // 2^(Gc_r(bb) - Gc_r(bb-1))
+      float e = Ar[0][tid];
+      Eb[0][tid] = e;
+#pragma unroll
+      for (int bb = 1; bb < 4; ++bb) { e *= f[bb]; Eb[bb][tid] = e; fb[bb][tid] = f[bb]; }
+      dend[rec * DK + tid] = e * Xe[3][tid];
+      float sv = Xe[3][tid];
+      Sb[3][tid] = sv;
+#pragma unroll
+      for (int bb = 2; bb >= 0; --bb) { sv *= f[bb + 1]; Sb[bb][tid] = sv; }
     }
     __syncthreads();
   }
-  if (tid < DK) {
-    dend[rec * DK + tid] = ex2(Gc[C - 1][tid]);
-#pragma unroll
-    for (int bb = 1; bb < 4; ++bb) fb[bb][tid] = ex2(Gc[16 * bb][tid] - Gc[16 * (bb - 1)][tid]);
-  }
-  __syncthreads();
 
   // ---- operands: a half-warp per token row, one 8-channel chunk per lane;
   // the q/k loads of the next row run one iteration ahead ----
@@ -220,7 +246,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
 #pragma unroll 1
   for (int it = 0; it < C * 16 / PREP_THREADS; ++it) {
     const int t = it * (PREP_THREADS / 16) + (tid >> 4), cc = tid & 15, c0 = cc * 8;
-    const int blk = t >> 4, r = blk * 16;
+    const int blk = t >> 4;
     float q[8], k[8];
     unpack8(qn, q);
     unpack8(kn, k);
@@ -242,24 +268,24 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
         k[j] = bf16_to_f32(f32_to_bf16_rne(k[j] * ik));
       }
     }
-    float gt[8], gr[8], gC[8];
-    *reinterpret_cast<float4*>(gt) = *reinterpret_cast<const float4*>(&Gc[t][c0]);
-    *reinterpret_cast<float4*>(gt + 4) = *reinterpret_cast<const float4*>(&Gc[t][c0 + 4]);
-    *reinterpret_cast<float4*>(gr) = *reinterpret_cast<const float4*>(&Gc[r][c0]);
-    *reinterpret_cast<float4*>(gr + 4) = *reinterpret_cast<const float4*>(&Gc[r][c0 + 4]);
-    *reinterpret_cast<float4*>(gC) = *reinterpret_cast<const float4*>(&Gc[C - 1][c0]);
-    *reinterpret_cast<float4*>(gC + 4) = *reinterpret_cast<const float4*>(&Gc[C - 1][c0 + 4]);
+    float X[8], eb[8], sb[8];
+    *reinterpret_cast<float4*>(X) = *reinterpret_cast<const float4*>(&Gc[t][c0]);
+    *reinterpret_cast<float4*>(X + 4) = *reinterpret_cast<const float4*>(&Gc[t][c0 + 4]);
+    *reinterpret_cast<float4*>(eb) = *reinterpret_cast<const float4*>(sm + P_EB + (blk * DK + c0) * 4);
+    *reinterpret_cast<float4*>(eb + 4) = *reinterpret_cast<const float4*>(sm + P_EB + (blk * DK + c0 + 4) * 4);
+    *reinterpret_cast<float4*>(sb) = *reinterpret_cast<const float4*>(sm + P_SB + (blk * DK + c0) * 4);
+    *reinterpret_cast<float4*>(sb + 4) = *reinterpret_cast<const float4*>(sm + P_SB + (blk * DK + c0 + 4) * 4);
     float ks[8], qs[8], ke[8], xq[8], xk[8], y[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float e = ex2(gt[j]);
+      const float rx = rcp_approx(X[j]);
+      const float e = eb[j] * X[j];  // 2^Gc_t
       ks[j] = k[j] * e;
       qs[j] = q[j] * e;
-      ke[j] = k[j] * ex2(gC[j] - gt[j]);
-      const float x = ex2(gt[j] - gr[j]);
-      xq[j] = q[j] * x;
-      xk[j] = k[j] * x;
-      y[j] = k[j] * ex2(gr[j] - gt[j]);
+      ke[j] = k[j] * (sb[j] * rx);    // 2^(Gc_C - Gc_t)
+      xq[j] = q[j] * X[j];            // 2^(Gc_t - Gc_r)
+      xk[j] = k[j] * X[j];
+      y[j] = k[j] * rx;               // 2^(Gc_r - Gc_t)
     }
     *reinterpret_cast<uint4*>(bigr + (size_t)t * DK + c0) = pack8(ks);
     *reinterpret_cast<uint4*>(bigr + (size_t)(64 + t) * DK + c0) = pack8(qs);

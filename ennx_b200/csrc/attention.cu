@@ -39,7 +39,7 @@ constexpr int SUB = 128 * 128;             // bytes of one 128-row x 64-column b
 constexpr int TILE = 2 * SUB;              // 128 rows x 128 columns
 constexpr int SOFTMAX_WARPS = 16;
 constexpr int THREADS = 64 + 32 * SOFTMAX_WARPS;  // producer, MMA, 2 x 8 softmax warps
-constexpr int SMEM = 2 * TILE /*Q_A, Q_B*/ + 2 * TILE /*K*/ + 2 * TILE /*V*/ + 1024 + 3072;
+constexpr int SMEM = 2 * TILE /*Q_A, Q_B*/ + 2 * TILE /*K*/ + 2 * TILE /*V*/ + 1024 + 5120;
 constexpr uint32_t IDESC_QK = idesc_bf16_f32(128, 128);
 constexpr uint32_t IDESC_PV = idesc_bf16_f32(128, 128) | (1u << 16);  // B (V) MN-major
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: rescale O only when the max grows by > 2^8
@@ -70,9 +70,11 @@ struct Bars {
   uint64_t q_full, kv_full[2], kv_free[2], s_full[2], p_full[2], o_done[2];
   uint32_t tmem_base;
   int abort_flag;
-  float red[2][2][128];  // [tile][half][row]: partial row max / sum exchanged by the two warps of a row
+  // [tile][parity of the key tile][half][row]: partial row max / sum exchanged
+  // by the two warps of a row; double-buffered so one barrier per tile suffices
+  float red[2][2][2][128];
 };
-static_assert(sizeof(Bars) <= 3072, "barrier block must fit the reserved 3 KB");
+static_assert(sizeof(Bars) <= 5120, "barrier block must fit the reserved 5 KB");
 
 __global__ void __launch_bounds__(THREADS, 1)
     gqa_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
@@ -187,8 +189,6 @@ __global__ void __launch_bounds__(THREADS, 1)
     const uint32_t s_col = tmem + lane_off + x * 256;  // S_X (P_X over its first 64 columns)
     const uint32_t o_col = s_col + 128;                 // O_X
     const int pair_bar = 1 + 4 * x + q;                 // shared with the warp owning the other half of these rows
-    float* red_mine = bar.red[x][half];
-    float* red_other = bar.red[x][half ^ 1];
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nt[x]; ++j) {
@@ -210,9 +210,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         v1[i] = __float_as_uint(c);
         mt = fmaxf(mt, fmaxf(a, c));
       }
-      red_mine[r] = mt;
+      // buffer j & 1: the partner's read of this slot two tiles ago preceded
+      // its arrival at the barrier of the tile in between
+      bar.red[x][j & 1][half][r] = mt;
       named_bar_sync(pair_bar, 64);  // also: both halves have read S before P overwrites it
-      mt = fmaxf(mt, red_other[r]);
+      mt = fmaxf(mt, bar.red[x][j & 1][half ^ 1][r]);
       const float m_new = fmaxf(m, mt);
       const bool rescale = m == -INFINITY ? true : (m_new > m + kRescaleThreshold);
       const float m_use = rescale ? m_new : m;
@@ -249,13 +251,12 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar.p_full[x]);
-      named_bar_sync(pair_bar, 64);  // red[] is rewritten next iteration
     }
     if (nt[x] > 0) {
       // row sum over both halves
-      red_mine[r] = l;
+      bar.red[x][nt[x] & 1][half][r] = l;
       named_bar_sync(pair_bar, 64);
-      const float l_tot = l + red_other[r];
+      const float l_tot = l + bar.red[x][nt[x] & 1][half ^ 1][r];
       if (ok && mbar_wait(&bar.o_done[x], (nt[x] - 1) & 1, err)) {
         tc_fence_after();
         const float inv = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;

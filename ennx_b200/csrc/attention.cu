@@ -62,6 +62,22 @@ __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+__device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add_f32x2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __device__ __forceinline__ void named_bar_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -200,16 +216,18 @@ __global__ void __launch_bounds__(THREADS, 1)
       tmem_ld32(s_col + half * 64, v0);
       tmem_ld32(s_col + half * 64 + 32, v1);
       tmem_ld_wait();
+      if (diag) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          if (k0 + i > qpos || k0 + i >= seq) v0[i] = 0xff800000u;  // -inf
+          if (k0 + 32 + i > qpos || k0 + 32 + i >= seq) v1[i] = 0xff800000u;
+        }
+      }
+      // row max of the raw scores (the positive scale commutes with max)
       float mt = -INFINITY;
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        float a = __uint_as_float(v0[i]) * scale_log2, c = __uint_as_float(v1[i]) * scale_log2;
-        if (diag && (k0 + i > qpos || k0 + i >= seq)) a = -INFINITY;
-        if (diag && (k0 + 32 + i > qpos || k0 + 32 + i >= seq)) c = -INFINITY;
-        v0[i] = __float_as_uint(a);
-        v1[i] = __float_as_uint(c);
-        mt = fmaxf(mt, fmaxf(a, c));
-      }
+      for (int i = 0; i < 32; ++i) mt = fmaxf(mt, fmaxf(__uint_as_float(v0[i]), __uint_as_float(v1[i])));
+      mt *= scale_log2;
       // buffer j & 1: the partner's read of this slot two tiles ago preceded
       // its arrival at the barrier of the tile in between
       bar.red[x][j & 1][half][r] = mt;
@@ -219,19 +237,23 @@ __global__ void __launch_bounds__(THREADS, 1)
       const bool rescale = m == -INFINITY ? true : (m_new > m + kRescaleThreshold);
       const float m_use = rescale ? m_new : m;
       const float alpha = (rescale && m != -INFINITY) ? ex2(m - m_use) : 1.0f;
-      // P = exp2(s - m): keys [64 half, +64) -> packed columns [32 half, +32) of S_X
-      float ls = 0.0f;
+      // P = exp2(s * scale - m) as one packed fma per pair of scores; a row
+      // with no unmasked score so far uses m = 0 (every exp2 argument is -inf)
+      const float nm = m_use == -INFINITY ? 0.0f : -m_use;
+      const uint64_t c2 = pack_f32x2(scale_log2, scale_log2), nm2 = pack_f32x2(nm, nm);
+      uint64_t ls2 = 0ull;
       uint32_t pk[32];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float p0 = m_use == -INFINITY ? 0.0f : ex2(__uint_as_float(v0[2 * i]) - m_use);
-        const float p1 = m_use == -INFINITY ? 0.0f : ex2(__uint_as_float(v0[2 * i + 1]) - m_use);
-        const float p2 = m_use == -INFINITY ? 0.0f : ex2(__uint_as_float(v1[2 * i]) - m_use);
-        const float p3 = m_use == -INFINITY ? 0.0f : ex2(__uint_as_float(v1[2 * i + 1]) - m_use);
-        ls += (p0 + p1) + (p2 + p3);
+        const uint64_t t01 = fma_f32x2(((uint64_t)v0[2 * i + 1] << 32) | v0[2 * i], c2, nm2);
+        const uint64_t t23 = fma_f32x2(((uint64_t)v1[2 * i + 1] << 32) | v1[2 * i], c2, nm2);
+        const float p0 = ex2(__uint_as_float((uint32_t)t01)), p1 = ex2(__uint_as_float((uint32_t)(t01 >> 32)));
+        const float p2 = ex2(__uint_as_float((uint32_t)t23)), p3 = ex2(__uint_as_float((uint32_t)(t23 >> 32)));
+        ls2 = add_f32x2(ls2, add_f32x2(pack_f32x2(p0, p1), pack_f32x2(p2, p3)));
         pk[i] = pack_bf16x2(p0, p1);
         pk[16 + i] = pack_bf16x2(p2, p3);
       }
+      const float ls = __uint_as_float((uint32_t)ls2) + __uint_as_float((uint32_t)(ls2 >> 32));
       tmem_st32(s_col + half * 32, pk);
       l = l * alpha + ls;
       m = m_use;

@@ -643,6 +643,11 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
           *reinterpret_cast<uint4*>(sm + S_XS + sw128(v, half * 4 + g)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         }
       }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&bar.xs_ready);
+      // S^T *= e^Gc_C: only the O/S MMAs of this chunk (after us_ready) need
+      // it, so it overlaps U^T = X^T T^T
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         const int i0 = half * 64 + p * 32;
@@ -654,10 +659,8 @@ __global__ void __launch_bounds__(SCAN_THREADS, 1)
         tmem_st32(tmem + lane_off + TM_S + i0, r);
       }
       tmem_st_wait();
-      fence_proxy_async();
-      tc_fence_before();
       __syncwarp();
-      if (lane == 0) { mbar_arrive(&bar.xs_ready); mbar_arrive(&bar.v_free); }
+      if (lane == 0) mbar_arrive(&bar.v_free);  // V and e^Gc_C consumed
       // ---- U^T -> bf16 ----
       if (!mbar_wait(&bar.u_full, par, err)) { ok = false; break; }
       tc_fence_after();

@@ -61,7 +61,7 @@ __global__ void targets_kernel(const int* __restrict__ tokens, int batch, int se
 // ---------------------------------------------------------------------------
 struct MoeBuffers {
   float* logits;
-  int *idx, *counters, *offsets, *perm_pos, *src_row;
+  int *idx, *counters, *offsets, *perm_pos;
   float *gate, *perm_gate;
   uint16_t *xperm, *act, *yperm;
 };
@@ -73,7 +73,6 @@ void carve_moe(Carver& c, long long tokens, int hidden, int experts, int top_k, 
   m.counters = c.take<int>(2 * sets * experts);
   m.offsets = c.take<int>(sets * experts + 1);
   m.perm_pos = c.take<int>(rows);
-  m.src_row = c.take<int>(rows);
   m.perm_gate = c.take<float>(rows);
   m.xperm = c.take<uint16_t>(rows * hidden);
   m.act = c.take<uint16_t>(rows * width);
@@ -91,11 +90,13 @@ int32_t run_moe(const uint16_t* x, const uint16_t* wr0, const uint16_t* wr1, con
   {
     ProfScope ps("moe_routing", s, 2.0 * tokens * hidden * experts,
                  2.0 * tokens * hidden + 2.0 * sets * experts * hidden + 4.0 * rows * hidden);
+    // pick counts (router) -> slots and row copies in expert-major order (one pass)
+    ENNX_CUDA(cudaMemsetAsync(m.counters, 0, sizeof(int) * 2 * sets * experts, s), "moe counters");
     ENNX_TRY(launch_router_topk(x, hidden, wr0, sets > 1 ? wr1 : nullptr, split, tokens, hidden, experts, top_k,
-                                m.logits, m.idx, m.gate, s));
-    ENNX_TRY(launch_moe_permute(m.idx, m.gate, residual_scale, tokens, top_k, experts, split, sets, m.counters, m.offsets,
-                                m.perm_pos, m.src_row, m.perm_gate, s));
-    ENNX_TRY(launch_gather_rows(x, hidden, m.src_row, rows, hidden, m.xperm, s));
+                                m.logits, m.idx, m.gate, s, m.counters));
+    ENNX_TRY(launch_moe_scatter_gather(m.idx, m.gate, residual_scale, tokens, top_k, experts, split, sets, m.counters,
+                                       m.offsets, m.counters + sets * experts, m.perm_pos, m.perm_gate, x, hidden,
+                                       hidden, m.xperm, s));
   }
   ennx_b200_gemm_params p;
   memset(&p, 0, sizeof(p));

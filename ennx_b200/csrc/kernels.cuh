@@ -24,18 +24,18 @@ int32_t launch_rope(uint16_t* base, long long ld, int heads, int dim, long long 
 // moe.cu
 int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0, const uint16_t* w1, long long split,
                            long long tokens, int hidden, int experts, int top_k, float* logits, int* idx,
-                           float* gate, cudaStream_t s);
-// Builds the expert-major permutation.  Group of (token t, rank r) is
-// set(t) * experts + idx[t, r] (set = t >= split).  Writes group_offsets
-// [sets*experts + 1], perm_pos[t*k + r] (row of (t, r) in permuted order),
-// src_row[pos], perm_gate[pos].  `counters` is scratch int[2*sets*experts].
-// perm_gate = gate_scale * gate (the residual scale of the layer folded into the combine weights)
-int32_t launch_moe_permute(const int* idx, const float* gate, float gate_scale, long long tokens, int top_k, int experts,
-                           long long split,
-                           int sets, int* counters, int* group_offsets, int* perm_pos, int* src_row,
-                           float* perm_gate, cudaStream_t s);
-int32_t launch_gather_rows(const uint16_t* x, long long ldx, const int* src_row, long long rows, int width,
-                           uint16_t* out, cudaStream_t s);
+                           float* gate, cudaStream_t s,
+                           int* counts = nullptr);
+// Expert-major permutation and row copy in one pass.  Group of (token t,
+// rank r) is set(t) * experts + idx[t, r] (set = t >= split); `counts` are the
+// per-group picks (launch_router_topk with counts), `cursor` int[groups]
+// zeroed.  Writes offsets[groups + 1], perm_pos[t*k + r] (row of (t, r) in
+// permuted order), perm_gate[pos] = gate_scale * gate (the residual scale of
+// the layer folded into the combine weights) and xperm[pos] = x[t].
+int32_t launch_moe_scatter_gather(const int* idx, const float* gate, float gate_scale, long long tokens, int top_k,
+                                  int experts, long long split, int sets, const int* counts, int* offsets, int* cursor,
+                                  int* perm_pos, float* perm_gate, const uint16_t* x, long long ldx, int width,
+                                  uint16_t* xperm, cudaStream_t s);
 // hidden[t] = residual[t] + sum_r y[perm_pos[t*k + r]]
 int32_t launch_moe_combine(const uint16_t* y, const int* perm_pos, long long tokens, int top_k, int width,
                            const uint16_t* residual, uint16_t* out, cudaStream_t s);

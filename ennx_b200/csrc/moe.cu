@@ -43,8 +43,9 @@ constexpr int kStageLoads = RK * RT / 8 / kRouterThreads;  // uint4 per thread p
 __global__ void __launch_bounds__(kRouterThreads, 1) router_topk_kernel(
     const uint16_t* __restrict__ x, long long ldx, const uint16_t* __restrict__ w0, const uint16_t* __restrict__ w1,
     long long split, long long tokens, int hidden, int experts, int top_k, float* __restrict__ logits,
-    int* __restrict__ idx, float* __restrict__ gate) {
+    int* __restrict__ idx, float* __restrict__ gate, int* __restrict__ counts) {
   extern __shared__ __align__(16) float rsm[];
+  __shared__ int hist[256];  // picks per expert of this block's tokens (counts != nullptr)
   float* As = rsm;                  // [2][RK][RT]
   float* Bs = As + 2 * RK * RT;     // [2][RK][RE]
   float* Ls = Bs + 2 * RK * RE;     // [RT][lds]
@@ -138,6 +139,7 @@ __global__ void __launch_bounds__(kRouterThreads, 1) router_topk_kernel(
         Ls[(8 * ty + 2 * i + 1) * lds + e0 + 4 * tx + j] = __uint_as_float((uint32_t)(accp[i][j] >> 32));
       }
   }
+  for (int e = tid; e < experts; e += kRouterThreads) hist[e] = 0;
   __syncthreads();
   if (logits) {
     for (int i = tid; i < RT * experts; i += kRouterThreads) {
@@ -180,66 +182,68 @@ __global__ void __launch_bounds__(kRouterThreads, 1) router_topk_kernel(
       if (r < top_k) {
         idx[t * top_k + r] = ids[r];
         gate[t * top_k + r] = ex[r] / den;
+        if (counts) atomicAdd(&hist[ids[r]], 1);
       }
   }
-}
-
-__global__ void moe_count_kernel(const int* __restrict__ idx, long long tokens, int top_k, int experts,
-                                 long long split, int* __restrict__ counts) {
-  long long n = tokens * top_k;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    long long t = i / top_k;
-    int g = (t >= split ? experts : 0) + idx[i];
-    atomicAdd(&counts[g], 1);
-  }
-}
-
-// single block: exclusive scan of counts into offsets, reset cursors
-__global__ void moe_scan_kernel(const int* __restrict__ counts, int groups, int* __restrict__ offsets,
-                                int* __restrict__ cursor) {
-  __shared__ int buf[1024];
-  int tid = threadIdx.x;
-  int v = tid < groups ? counts[tid] : 0;
-  buf[tid] = v;
-  __syncthreads();
-  for (int o = 1; o < blockDim.x; o <<= 1) {
-    int add = tid >= o ? buf[tid - o] : 0;
+  if (counts) {  // group = (weight set, expert); this block's tokens all use one set
     __syncthreads();
-    buf[tid] += add;
+    const int set = (long long)blockIdx.x < nb0 ? 0 : 1;
+    for (int e = tid; e < experts; e += kRouterThreads)
+      if (hist[e]) atomicAdd(&counts[set * experts + e], hist[e]);
+  }
+}
+
+// Expert-major permutation and row copy in one pass.  Every block rebuilds the
+// exclusive scan of the per-group pick counts in shared memory (block 0 also
+// publishes it for the grouped GEMM); a warp per token claims one slot per
+// pick in its group (order inside a group is arbitrary, results are not:
+// each slot is a whole row) and copies the token's row, read once, into all
+// of its slots.
+__global__ void __launch_bounds__(256) moe_scatter_gather_kernel(
+    const int* __restrict__ idx, const float* __restrict__ gate, float gate_scale, long long tokens, int top_k,
+    int experts, long long split, int groups, const int* __restrict__ counts, int* __restrict__ offsets,
+    int* __restrict__ cursor, int* __restrict__ perm_pos, float* __restrict__ perm_gate,
+    const uint16_t* __restrict__ x, long long ldx, int width, uint16_t* __restrict__ xperm) {
+  __shared__ int off[257];
+  __shared__ int wsum[8];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  {  // exclusive scan of counts[0 .. groups) (groups <= 256)
+    int v = tid < groups ? counts[tid] : 0;
+    int incl = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) wsum[warp] = incl;
     __syncthreads();
+    int base = 0;
+    for (int w = 0; w < warp; ++w) base += wsum[w];
+    off[tid] = base + incl - v;
+    if (tid == 255) off[256] = base + incl;
+    __syncthreads();
+    if (blockIdx.x == 0) {
+      if (tid < groups) offsets[tid] = off[tid];
+      if (tid == 0) offsets[groups] = off[groups];  // total (counts past `groups` read as 0)
+    }
   }
-  if (tid < groups) {
-    offsets[tid] = buf[tid] - v;
-    cursor[tid] = 0;
+  const long long t = (long long)blockIdx.x * 8 + warp;
+  if (t >= tokens) return;
+  int pos = 0;
+  if (lane < top_k) {
+    const int g = (t >= split ? experts : 0) + idx[t * top_k + lane];
+    pos = off[g] + atomicAdd(&cursor[g], 1);
+    perm_pos[t * top_k + lane] = pos;
+    perm_gate[pos] = gate_scale * gate[t * top_k + lane];
   }
-  if (tid == groups - 1) offsets[groups] = buf[tid];
-}
-
-__global__ void moe_scatter_kernel(const int* __restrict__ idx, const float* __restrict__ gate, float gate_scale,
-                                   long long tokens,
-                                   int top_k, int experts, long long split, const int* __restrict__ offsets,
-                                   int* __restrict__ cursor, int* __restrict__ perm_pos, int* __restrict__ src_row,
-                                   float* __restrict__ perm_gate) {
-  long long n = tokens * top_k;
-  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
-    long long t = i / top_k;
-    int g = (t >= split ? experts : 0) + idx[i];
-    int pos = offsets[g] + atomicAdd(&cursor[g], 1);
-    perm_pos[i] = pos;
-    src_row[pos] = (int)t;
-    perm_gate[pos] = gate_scale * gate[i];
+  const uint16_t* src = x + t * ldx;
+  for (int c = lane * 8; c < width; c += 256) {
+    const uint4 v = *reinterpret_cast<const uint4*>(src + c);
+    for (int r = 0; r < top_k; ++r) {
+      const int p = __shfl_sync(0xffffffffu, pos, r);
+      *reinterpret_cast<uint4*>(xperm + (long long)p * width + c) = v;
+    }
   }
-}
-
-__global__ void gather_rows_kernel(const uint16_t* __restrict__ x, long long ldx, const int* __restrict__ src,
-                                   long long rows, int width, uint16_t* __restrict__ out) {
-  long long r = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  int lane = threadIdx.x & 31;
-  if (r >= rows) return;
-  const uint16_t* s = x + (long long)src[r] * ldx;
-  uint16_t* d = out + r * width;
-  for (int c = lane * 8; c < width; c += 256)
-    *reinterpret_cast<uint4*>(d + c) = *reinterpret_cast<const uint4*>(s + c);
 }
 
 __global__ void moe_combine_kernel(const uint16_t* __restrict__ y, const int* __restrict__ perm_pos, long long tokens,
@@ -276,15 +280,9 @@ __global__ void moe_combine_kernel(const uint16_t* __restrict__ y, const int* __
   }
 }
 
-static int stride_grid(long long n, int threads) {
-  long long b = (n + threads - 1) / threads;
-  long long cap = (long long)sm_count() * 16;
-  return (int)(b < cap ? (b > 0 ? b : 1) : cap);
-}
-
 int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0, const uint16_t* w1, long long split,
                            long long tokens, int hidden, int experts, int top_k, float* logits, int* idx,
-                           float* gate, cudaStream_t s) {
+                           float* gate, cudaStream_t s, int* counts) {
   if (top_k < 1 || top_k > 8 || top_k > experts)
     return set_error(ENNX_B200_INVALID_ARGUMENT, "router: top_k must be in [1, min(8, experts)]");  // forward_program.rs:428
   if (experts > 256) return set_error(ENNX_B200_UNSUPPORTED, "router: at most 256 experts");
@@ -306,34 +304,23 @@ int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0,
     attr[dev] = true;
   }
   router_topk_kernel<<<(unsigned)blocks, kRouterThreads, smem, s>>>(x, ldx, w0, w1, split, tokens, hidden, experts,
-                                                                      top_k, logits, idx, gate);
+                                                                      top_k, logits, idx, gate, counts);
   ENNX_LAUNCH_CHECK("router_topk");
   return ENNX_B200_OK;
 }
 
-int32_t launch_moe_permute(const int* idx, const float* gate, float gate_scale, long long tokens, int top_k, int experts,
-                           long long split,
-                           int sets, int* counters, int* group_offsets, int* perm_pos, int* src_row,
-                           float* perm_gate, cudaStream_t s) {
-  int groups = sets * experts;
-  if (groups > 1024) return set_error(ENNX_B200_UNSUPPORTED, "moe: at most 1024 (set, expert) groups");
+int32_t launch_moe_scatter_gather(const int* idx, const float* gate, float gate_scale, long long tokens, int top_k,
+                                  int experts, long long split, int sets, const int* counts, int* offsets, int* cursor,
+                                  int* perm_pos, float* perm_gate, const uint16_t* x, long long ldx, int width,
+                                  uint16_t* xperm, cudaStream_t s) {
+  const int groups = sets * experts;
+  if (groups > 256) return set_error(ENNX_B200_UNSUPPORTED, "moe: at most 256 (set, expert) groups");
+  if (width % 256 || ldx % 8) return set_error(ENNX_B200_UNSUPPORTED, "moe: width must be a multiple of 256");
   if (sets == 1) split = tokens;
-  ENNX_CUDA(cudaMemsetAsync(counters, 0, sizeof(int) * groups, s), "moe counters");
-  long long n = tokens * top_k;
-  moe_count_kernel<<<stride_grid(n, 256), 256, 0, s>>>(idx, tokens, top_k, experts, split, counters);
-  moe_scan_kernel<<<1, 1024, 0, s>>>(counters, groups, group_offsets, counters + groups);
-  moe_scatter_kernel<<<stride_grid(n, 256), 256, 0, s>>>(idx, gate, gate_scale, tokens, top_k, experts, split, group_offsets,
-                                                          counters + groups, perm_pos, src_row, perm_gate);
-  note_launch(2);
-  ENNX_LAUNCH_CHECK("moe_permute");
-  return ENNX_B200_OK;
-}
-
-int32_t launch_gather_rows(const uint16_t* x, long long ldx, const int* src_row, long long rows, int width,
-                           uint16_t* out, cudaStream_t s) {
-  if (width % 256) return set_error(ENNX_B200_UNSUPPORTED, "gather: width must be a multiple of 256");
-  gather_rows_kernel<<<(unsigned)((rows + 7) / 8), 256, 0, s>>>(x, ldx, src_row, rows, width, out);
-  ENNX_LAUNCH_CHECK("gather_rows");
+  moe_scatter_gather_kernel<<<(unsigned)((tokens + 7) / 8), 256, 0, s>>>(idx, gate, gate_scale, tokens, top_k, experts,
+                                                                       split, groups, counts, offsets, cursor,
+                                                                       perm_pos, perm_gate, x, ldx, width, xperm);
+  ENNX_LAUNCH_CHECK("moe_scatter_gather");
   return ENNX_B200_OK;
 }
 

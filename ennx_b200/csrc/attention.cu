@@ -208,14 +208,24 @@ __global__ void __launch_bounds__(THREADS, 1)
     float m = -INFINITY, l = 0.0f;
     bool ok = true;
     for (int j = 0; j < nt[x]; ++j) {
-      if (!mbar_wait(&bar.s_full[x], j & 1, err)) { ok = false; break; }
+      // A failed (timed-out) wait does not leave the loop: the warp keeps
+      // meeting its partner at the named barrier, which has no timeout, and
+      // skips the work; the abort flag stops every other wait early.
+      if (ok) ok = !*abort_flag && mbar_wait(&bar.s_full[x], j & 1, err);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) *abort_flag = 1;
       tc_fence_after();
       const int k0 = j * BKV + half * 64;
       const bool diag = k0 + 63 > qx0 || k0 + 64 > seq;  // warp-uniform: this half needs the causal / length mask
       uint32_t v0[32], v1[32];
-      tmem_ld32(s_col + half * 64, v0);
-      tmem_ld32(s_col + half * 64 + 32, v1);
-      tmem_ld_wait();
+      if (ok) {
+        tmem_ld32(s_col + half * 64, v0);
+        tmem_ld32(s_col + half * 64 + 32, v1);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v0[i] = v1[i] = 0xff800000u;
+      }
       if (diag) {
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
@@ -233,6 +243,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       bar.red[x][j & 1][half][r] = mt;
       named_bar_sync(pair_bar, 64);  // also: both halves have read S before P overwrites it
       mt = fmaxf(mt, bar.red[x][j & 1][half ^ 1][r]);
+      if (!ok) continue;  // after the barrier: nothing below waits on the partner
       const float m_new = fmaxf(m, mt);
       const bool rescale = m == -INFINITY ? true : (m_new > m + kRescaleThreshold);
       const float m_use = rescale ? m_new : m;

@@ -35,9 +35,9 @@ POP = 32          # candidates (16 antithetic pairs)
 BATCH, SEQ = 4, 1024
 SIGMA = 1e-3
 METRIC = "Qwen-hybrid forward tokens/s at 1/2/4/8 B200; kernel % of roofline"
-# DRAM bytes per tcgen05 GEMM launch over one full forward step (2416 launches,
-# 849.15 GB), from the ncu capture summarised in profiles/gemm_forward_traffic.md.
-GEMM_DRAM_BYTES_PER_LAUNCH = 351.47e6
+# DRAM bytes per tcgen05 GEMM launch over one full forward step (1840 launches,
+# 870.23 GB), from the ncu capture summarised in profiles/gemm_forward_traffic.md.
+GEMM_DRAM_BYTES_PER_LAUNCH = 472.95e6
 CONFIG = {"workload": "hybrid KDA/GQA-MoE forward, 32 antithetic candidates (sigma 1e-3, Philox), "
                       "batch 4 x seq 1024 each, mean CE fitness",
           "layers": 24, "hidden": 2048, "pattern": "[KDA,KDA,KDA,GQA]x6", "q_heads": 16, "kv_heads": 4,

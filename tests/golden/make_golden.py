@@ -52,7 +52,9 @@ def bf16_bits(x: np.ndarray) -> np.ndarray:
 
 
 def main() -> None:
-    ref_root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        raise SystemExit("usage: python tests/golden/make_golden.py <path to the Kvutza/ennx checkout>")
+    ref_root = Path(sys.argv[1])
     ns = load_reference_functions(ref_root)
     out_dir = Path(__file__).resolve().parent
 

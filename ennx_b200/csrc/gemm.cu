@@ -1,17 +1,21 @@
 // gemm.cu -- persistent, warp-specialised tcgen05 GEMM for sm_100a.
 //
 // C = A . B^T, A [M, K] and B [N, K] bf16 with K contiguous ("K-major"), fp32
-// accumulation in tensor memory.  One CTA per SM loops over 128x256 output
-// tiles:
-//   warp 0      TMA producer: 64-wide K slices of A (128x64) and B (256x64)
-//               into a 4-stage ring of 128B-swizzled shared-memory tiles;
+// accumulation in tensor memory.  Persistent CTAs loop over output tiles:
+//   warp 0      TMA producer: 64-wide K slices of A and B into a ring of
+//               128B-swizzled shared-memory stages;
 //   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators)
-//               and issues tcgen05.mma (M=128, N=256, K=16) from one thread;
-//               tcgen05.commit frees a ring slot / publishes an accumulator;
-//   warps 2..5  epilogue: tcgen05.ld 32 columns at a time from their TMEM
-//               lane quarter, fused epilogue math, 16-byte global stores.
+//               and issues tcgen05.mma from one thread; tcgen05.commit frees
+//               a ring slot / publishes an accumulator;
+//   warps 2..9  epilogue, two warpgroups of 128 columns each: tcgen05.ld 32
+//               columns at a time from their TMEM lane quarter, fused
+//               epilogue math, per-warp 32x32 staging tiles and TMA stores.
+// Two variants: single CTA (128x256 tiles, 4 stages, M=128 MMAs) and, for
+// M >= 1024, a CTA pair (cta_group::2, 256x256 tiles over two SMs, each CTA
+// holding its 128 A rows and half of B, 6 stages, M=256 MMAs).
 // The two accumulators let tile i's epilogue overlap tile i+1's main loop.
-// No cluster, no multicast: every CTA loads its own tiles.
+// No multicast: every CTA loads its own tiles (the CTA-pair variant runs as
+// clusters of two that share the MMA, not the loads).
 //
 // Grouped mode runs several independent problems that share A/C rows
 // segments and use different B row blocks (MoE experts, antithetic

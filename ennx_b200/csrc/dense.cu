@@ -186,9 +186,10 @@ __global__ void dense_linear_kernel(const float* __restrict__ x, const float* __
 
 // Population noise: each thread owns 8 consecutive elements (one Philox
 // block) per step, 16-byte loads and stores; W +/- sigma*eps with two fp32
-// roundings, RNE.  Blocks cover a fixed 8192-element span and retire quickly,
-// so the block scheduler can interleave them with the compute stream's
-// kernels on the same SMs (this kernel runs on a low-priority stream).
+// roundings, RNE.  Blocks of 128 threads cover a fixed 4096-element span and
+// retire quickly, so the block scheduler can interleave them with the compute
+// stream's kernels on the same SMs (this kernel runs on a low-priority
+// stream); the batched form covers every tensor of a layer in one launch.
 constexpr int kPerturbGroupsPerThread = 4;
 constexpr int kPerturbThreads = 128;
 // One 8-element group span of a perturbation: block `blk` of the tensor.

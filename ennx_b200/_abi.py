@@ -100,6 +100,7 @@ SIGNATURES = {
     "ennx_b200_dense_apply_f32": (_I32, [_P, _SZ, _P, _SZ, _P, _SZ, _P, _P, _P]),
     "ennx_b200_dense_apply_bf16": (_I32, [_P, _SZ, _P, _SZ, _P, _SZ, _P, _P]),
     "ennx_b200_check_bf16": (_I32, [_P, _SZ, _P, _P]),
+    "ennx_b200_dense_dist2": (_I32, [_P, _SZ, _P, _SZ, _P, _SZ, _P]),
     "ennx_b200_dense_linear_f32": (_I32, [_P, _SZ, _P, _SZ, _P, DenseView, DenseView, _P, _SZ, _P, _P]),
     "ennx_b200_perturb_bf16": (_I32, [_P, _SZ, _U64, _U32, _U32, _F32, _P, _P, _P]),
     "ennx_b200_gemm_bf16": (_I32, [_P, _P, _P, _P, _P]),

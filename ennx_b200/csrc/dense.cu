@@ -457,6 +457,53 @@ int32_t ennx_b200_dense_linear_f32(const float* input, size_t columns, const flo
   return ENNX_B200_OK;
 }
 
+// Host arithmetic only: energy (sum of len * scale^2 over the leaves) times the
+// squared distance between the two coefficient vectors, each seed counted once,
+// left seeds first, then right-only seeds (zig/src/dense.zig:124-167).
+int32_t ennx_b200_dense_dist2(const ennx_b200_dense_leaf* leaves, size_t nl, const ennx_b200_dense_term* left,
+                              size_t nleft, const ennx_b200_dense_term* right, size_t nright, double* out) {
+  if (!out) return set_error(ENNX_B200_INVALID_ARGUMENT, "dense distance needs an output");
+  if (!leaves || nl == 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "at least one dense leaf is required");
+  if ((nleft && !left) || (nright && !right))
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "dense distance terms are null");
+  size_t end = 0;
+  double energy = 0.0;
+  for (size_t i = 0; i < nl; ++i) {
+    if (leaves[i].offset != end)
+      return set_error(ENNX_B200_INVALID_ARGUMENT, "dense leaf offset %zu does not continue parameter offset %zu",
+                       leaves[i].offset, end);
+    if (leaves[i].len == 0 || !isfinite(leaves[i].scale) || leaves[i].scale <= 0.0f)
+      return set_error(ENNX_B200_INVALID_ARGUMENT, "dense leaves require positive lengths and scales");
+    if (leaves[i].len > SIZE_MAX - end) return set_error(ENNX_B200_INVALID_ARGUMENT, "dense parameter count overflow");
+    end += leaves[i].len;
+    double sc = (double)leaves[i].scale;
+    energy += (double)leaves[i].len * sc * sc;
+  }
+  for (size_t i = 0; i < nleft; ++i)
+    if (!isfinite(left[i].coefficient))
+      return set_error(ENNX_B200_INVALID_ARGUMENT, "dense coefficients must be finite");
+  for (size_t i = 0; i < nright; ++i)
+    if (!isfinite(right[i].coefficient))
+      return set_error(ENNX_B200_INVALID_ARGUMENT, "dense coefficients must be finite");
+  auto seen = [](const ennx_b200_dense_term* t, size_t n, uint64_t seed) {
+    for (size_t i = 0; i < n; ++i) if (t[i].seed == seed) return true;
+    return false;
+  };
+  double d2 = 0.0;
+  for (size_t i = 0; i < nleft; ++i) {
+    if (seen(left, i, left[i].seed)) continue;
+    double d = coefficient_of(left, nleft, left[i].seed) - coefficient_of(right, nright, left[i].seed);
+    d2 += d * d;
+  }
+  for (size_t i = 0; i < nright; ++i) {
+    if (seen(right, i, right[i].seed) || seen(left, nleft, right[i].seed)) continue;
+    double c = coefficient_of(right, nright, right[i].seed);
+    d2 += c * c;
+  }
+  *out = energy * d2;
+  return ENNX_B200_OK;
+}
+
 int32_t ennx_b200_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor,
                                float sigma, uint16_t* plus, uint16_t* minus, void* stream) {
   return ennx::launch_perturb_bf16(w, n, seed, pair, tensor, sigma, plus, minus, 0, 0, (cudaStream_t)stream);

@@ -87,6 +87,15 @@ ENNX_B200_API int32_t ennx_b200_dense_apply_bf16(const uint16_t* base, size_t nu
                                    const ennx_b200_dense_term* terms, size_t num_terms,
                                    uint16_t* out, void* stream);
 
+/* *out_distance = (sum over leaves of len * scale^2) * sum over seeds of
+ * (c_left(seed) - c_right(seed))^2: the squared L2 distance between the two
+ * perturbations.  Replaces ennx_dense_dist2 (zig/include/ennx.h:46-53), same
+ * argument order; host memory only, no device work.  Empty term lists are
+ * allowed; leaves must be contiguous from offset 0. */
+ENNX_B200_API int32_t ennx_b200_dense_dist2(const ennx_b200_dense_leaf* leaves, size_t num_leaves,
+                              const ennx_b200_dense_term* left, size_t num_left,
+                              const ennx_b200_dense_term* right, size_t num_right, double* out_distance);
+
 /* *all_finite (host) = 1 iff every bf16 value is finite.  Replaces the
  * check_bf16 kernel path (cuda/kernels/src/lib.rs:2311-2354).  Synchronises. */
 ENNX_B200_API int32_t ennx_b200_check_bf16(const uint16_t* values, size_t num_values, int32_t* all_finite,

@@ -41,6 +41,28 @@ class DenseView(ctypes.Structure):
     _fields_ = [("key", ctypes.c_uint64), ("start", ctypes.c_uint64), ("scale", ctypes.c_float)]
 
 
+class Bf16Leaf(ctypes.Structure):
+    """ennx_b200_bf16_leaf = Bf16Leaf (cuda/kernels/src/bf16.rs:5-13)."""
+    _fields_ = [("key", ctypes.c_uint64), ("offset", ctypes.c_uint64), ("length", ctypes.c_uint64),
+                ("scale", ctypes.c_float), ("weight", ctypes.c_float)]
+
+
+class Selection(ctypes.Structure):
+    _fields_ = [("index", ctypes.c_uint32), ("score", ctypes.c_float)]
+
+
+class AskConfig(ctypes.Structure):
+    _fields_ = [("neighbors", ctypes.c_uint32), ("acquisition", ctypes.c_uint32),
+                ("epistemic_scale", ctypes.c_float), ("aleatoric_scale", ctypes.c_float),
+                ("y_scale", ctypes.c_float), ("beta", ctypes.c_float)]
+
+
+class TellSummary(ctypes.Structure):
+    _fields_ = [("length", ctypes.c_double), ("best", ctypes.c_float), ("best_variance", ctypes.c_float),
+                ("history", ctypes.c_uint32), ("restarts", ctypes.c_uint32), ("restarted", ctypes.c_uint32),
+                ("status", ctypes.c_uint32)]
+
+
 class GemmParams(ctypes.Structure):
     _fields_ = [("m", ctypes.c_int32), ("n", ctypes.c_int32), ("k", ctypes.c_int32),
                 ("lda", ctypes.c_int64), ("ldb", ctypes.c_int64), ("ldc", ctypes.c_int64),
@@ -101,6 +123,21 @@ SIGNATURES = {
     "ennx_b200_dense_apply_bf16": (_I32, [_P, _SZ, _P, _SZ, _P, _SZ, _P, _P]),
     "ennx_b200_check_bf16": (_I32, [_P, _SZ, _P, _P]),
     "ennx_b200_dense_dist2": (_I32, [_P, _SZ, _P, _SZ, _P, _SZ, _P]),
+    "ennx_b200_bf16_search_create": (_I32, [_P, _SZ, _P, _SZ, _SZ, _P, _P]),
+    "ennx_b200_bf16_search_destroy": (_I32, [_P]),
+    "ennx_b200_bf16_search_init": (_I32, [_P, _F32, _F32, _SZ, ctypes.c_double, ctypes.c_double, ctypes.c_double]),
+    "ennx_b200_bf16_search_copy_row": (_I32, [_P, _SZ, _SZ]),
+    "ennx_b200_bf16_search_ask": (_I32, [_P, _SZ, _SZ, _P, _SZ, _P, _SZ, _F32, _U64, _P, _P]),
+    "ennx_b200_bf16_search_ask_seeded": (_I32, [_P, _SZ, _P, _SZ, _SZ, _U64, _U64, _P]),
+    "ennx_b200_bf16_search_tell": (_I32, [_P, _P, _SZ, _P, _P, _I32, _SZ, _SZ]),
+    "ennx_b200_bf16_search_collect": (_I32, [_P, _SZ, _P, _P]),
+    "ennx_b200_bf16_search_row": (_I32, [_P, _SZ, _P]),
+    "ennx_b200_bf16_search_round": (_I32, [_P, _SZ, _P]),
+    "ennx_b200_bf16_search_gather": (_I32, [_P, _P, _SZ, _P]),
+    "ennx_b200_bf16_search_handoff": (_I32, [_P, _P, _I32]),
+    "ennx_b200_bf16_search_last_scores": (_I32, [_P, _P, _SZ, _P, _SZ]),
+    "ennx_b200_bf16_search_set_profiling": (_I32, [_P, _I32]),
+    "ennx_b200_bf16_search_last_profile": (_I32, [_P, _P, _P]),
     "ennx_b200_dense_linear_f32": (_I32, [_P, _SZ, _P, _SZ, _P, DenseView, DenseView, _P, _SZ, _P, _P]),
     "ennx_b200_perturb_bf16": (_I32, [_P, _SZ, _U64, _U32, _U32, _F32, _P, _P, _P]),
     "ennx_b200_gemm_bf16": (_I32, [_P, _P, _P, _P, _P]),

@@ -76,6 +76,22 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// splitmix64 finaliser of the seeded sign (rust/crates/ennx/src/dense.rs:428-433).
+__host__ __device__ __forceinline__ uint64_t mix64(uint64_t x) {
+  uint64_t v = x + 0x9e3779b97f4a7c15ull;
+  v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+  v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
+  return v ^ (v >> 31);
+}
+// One BF16 ulp toward `positive`, staying finite (dense/bf16.rs:276-292).
+__device__ __forceinline__ uint16_t bf16_next(uint16_t v, bool positive) {
+  if ((v & 0x7fffu) == 0) return positive ? 1u : 0x8001u;
+  bool grows = ((v & 0x8000u) == 0) == positive;
+  uint16_t cand = grows ? (uint16_t)(v + 1u) : (uint16_t)(v - 1u);
+  if ((cand & 0x7f80u) != 0x7f80u) return cand;
+  return grows ? (uint16_t)(v - 1u) : (uint16_t)(v + 1u);
+}
+
 // ---------------------------------------------------------------------------
 // Population noise: Philox4x32-10 (Salmon et al., SC'11) + Box-Muller.
 // Element e of tensor t for antithetic pair p under population seed s is the

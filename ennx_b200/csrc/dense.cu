@@ -27,13 +27,6 @@ struct DevTerm {
   uint32_t pad;
 };
 
-__host__ __device__ __forceinline__ uint64_t mix64(uint64_t x) {
-  uint64_t v = x + 0x9e3779b97f4a7c15ull;
-  v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
-  v = (v ^ (v >> 27)) * 0x94d049bb133111ebull;
-  return v ^ (v >> 31);
-}
-
 // dense.rs:367-379: sum of c*sign and the dominant term's direction.
 __device__ __forceinline__ float term_sum(const DevTerm* terms, int nt, uint64_t key_mix, uint64_t element,
                                           bool& positive) {
@@ -60,14 +53,6 @@ __device__ __forceinline__ float dense_next(float value, bool positive) {
   float cand = __uint_as_float(grows ? b + 1u : b - 1u);
   if (isfinite(cand)) return cand;
   return __uint_as_float(grows ? b - 1u : b + 1u);
-}
-
-__device__ __forceinline__ uint16_t bf16_next(uint16_t v, bool positive) {
-  if ((v & 0x7fffu) == 0) return positive ? 1u : 0x8001u;
-  bool grows = ((v & 0x8000u) == 0) == positive;
-  uint16_t cand = grows ? (uint16_t)(v + 1u) : (uint16_t)(v - 1u);
-  if ((cand & 0x7f80u) != 0x7f80u) return cand;
-  return grows ? (uint16_t)(v - 1u) : (uint16_t)(v + 1u);
 }
 
 // Leaf lookup by binary search over the (contiguous) leaf offsets.

@@ -404,3 +404,17 @@ def dense_linear(input, weight, weight_view, terms, bias=None, bias_view=None, d
     w, b, _, columns = _model(weight, bias, wv, bv)
     _eval_terms(_vector(input, "dense linear input"), columns, tm)
     return DenseLinear(w, weight_view, b, bias_view, device).eval(input, terms)
+
+
+# The resident search classes live in ennx_b200.search (which imports this
+# module's ParamBlock and DLPack import); they resolve here on first use, as
+# the reference's experimental namespace resolves its names lazily.
+_SEARCH_NAMES = ("Proposals", "SearchState", "turbo_enn")
+__all__ += list(_SEARCH_NAMES)
+
+
+def __getattr__(name: str):
+    if name in _SEARCH_NAMES:
+        from . import search
+        return getattr(search, name)
+    raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

@@ -349,6 +349,134 @@ ENNX_B200_API int32_t ennx_b200_packed_linear_bf16(const uint16_t* x, int64_t to
                                                    ennx_b200_perturb_seed seed, uint16_t* out, void* workspace,
                                                    size_t workspace_bytes, void* stream);
 
+/* ---- resident BF16 TuRBO search (replaces the Bf16SearchEngine of the
+ *      ennx-cuda crate, cuda/src/bf16_search.rs:129-1067, and its kernels
+ *      distance_bf16 / score_bf16 / draw_bf16 / seed_bf16 / pick_trial /
+ *      write_bf16 / tell_bf16 / check_search, cuda/kernels/src/lib.rs:1310-2308)
+ *
+ * A handle owns `slots` device rows of the model (slot 0 = incumbent, slots
+ * 1..capacity = trust-region history, the rest = pending trials), the
+ * history outcomes and the trust-region state, all in device memory, so
+ * that ask -> evaluate -> tell rounds need no host round trip.  Calls are
+ * enqueued on the stream given at creation; those documented as
+ * synchronising wait for it.  A handle is not thread-safe. ---------------- */
+
+/* Same layout as Bf16Leaf (cuda/kernels/src/bf16.rs:5-13). */
+typedef struct {
+    uint64_t key;
+    uint64_t offset;
+    uint64_t length;
+    float scale;
+    float weight;   /* multiplies the squared distance of this leaf's elements */
+} ennx_b200_bf16_leaf;
+
+/* Same layout as Selection (cuda/kernels/src/lib.rs:41-47). */
+typedef struct {
+    uint32_t index;   /* candidate index over all regions */
+    float score;
+} ennx_b200_selection;
+
+/* Acquisition settings of one ask (ennx_cuda::Ask, cuda/src/lib.rs).
+ * acquisition: 0 = UCB (mean + beta*se), 1 = Thompson (mean + se*N(0,1)),
+ * 2 = Pareto (mean + se). */
+typedef struct {
+    uint32_t neighbors;
+    uint32_t acquisition;
+    float epistemic_scale;
+    float aleatoric_scale;
+    float y_scale;
+    float beta;
+} ennx_b200_ask_config;
+
+/* Same fields as TellSummary (cuda/kernels/src/bf16.rs:63-72). */
+typedef struct {
+    double length;
+    float best;
+    float best_variance;
+    uint32_t history;
+    uint32_t restarts;
+    uint32_t restarted;
+    uint32_t status;   /* nonzero: the proposals or rewards were invalid */
+} ennx_b200_tell_summary;
+
+typedef struct ennx_b200_bf16_search ennx_b200_bf16_search;
+
+/* Copy `len` BF16 values from device memory `base` into slot 0 of a new
+ * handle with `slots` rows (>= 2).  Leaves must tile [0, len) contiguously,
+ * with positive finite scales and weights; base values must be finite.
+ * Bf16SearchEngine::from_device (cuda/src/bf16_search.rs:166-188).
+ * Synchronises. */
+ENNX_B200_API int32_t ennx_b200_bf16_search_create(const uint16_t* base, size_t len,
+                                                   const ennx_b200_bf16_leaf* leaves, size_t num_leaves,
+                                                   size_t slots, void* stream, ennx_b200_bf16_search** out);
+ENNX_B200_API int32_t ennx_b200_bf16_search_destroy(ennx_b200_bf16_search* search);
+/* Trust-region state and a one-row history (slot 1, value base_value);
+ * init_search (bf16_search.rs:243-293).  capacity <= 128. */
+ENNX_B200_API int32_t ennx_b200_bf16_search_init(ennx_b200_bf16_search* search, float base_value,
+                                                 float base_variance, size_t capacity, double length_init,
+                                                 double length_min, double length_max);
+/* Device copy of one row slot onto another (copy_row, bf16_search.rs:889-904). */
+ENNX_B200_API int32_t ennx_b200_bf16_search_copy_row(ennx_b200_bf16_search* search, size_t source,
+                                                     size_t destination);
+/* Score regions*candidates_per_region seeded candidates (host `seeds`)
+ * around row `base_slot` with step `coefficient` against the first
+ * `history` rows of the history, pick the best per region and write it
+ * into `trial_slots[r]` and row r of the batch.  Writes `regions`
+ * selections (host).  On an overflowing candidate the trial rows are reset
+ * to the base row and ENNX_B200_OVERFLOW is returned.  Bf16SearchEngine::ask
+ * (bf16_search.rs:518-556).  Synchronises. */
+ENNX_B200_API int32_t ennx_b200_bf16_search_ask(ennx_b200_bf16_search* search, size_t base_slot, size_t history,
+                                                const uint32_t* trial_slots, size_t regions,
+                                                const uint64_t* seeds, size_t candidates_per_region,
+                                                float coefficient, uint64_t draw_seed,
+                                                const ennx_b200_ask_config* config,
+                                                ennx_b200_selection* selections);
+/* Resident round: seeds derived on the device from `seed_root`, step and
+ * history taken from the device state.  Asynchronous; errors of the
+ * candidates surface at the next tell.  ask_seeded (bf16_search.rs:558-594). */
+ENNX_B200_API int32_t ennx_b200_bf16_search_ask_seeded(ennx_b200_bf16_search* search, size_t base_slot,
+                                                       const uint32_t* trial_slots, size_t regions,
+                                                       size_t candidates_per_region, uint64_t seed_root,
+                                                       uint64_t draw_seed, const ennx_b200_ask_config* config);
+/* Record `count` rewards (host or device float arrays; variances nullable =
+ * zeros) for the trials in `trial_slots`, update the history, the incumbent
+ * row and the trust region on the device.  Asynchronous; read the outcome
+ * with ennx_b200_bf16_search_collect.  tell / queue_tell
+ * (bf16_search.rs:295-492). */
+ENNX_B200_API int32_t ennx_b200_bf16_search_tell(ennx_b200_bf16_search* search, const uint32_t* trial_slots,
+                                                 size_t count, const float* values, const float* variances,
+                                                 int32_t values_on_device, size_t capacity,
+                                                 size_t failure_tolerance);
+/* Synchronise and read the last tell: accepted[count] (host, 0/1) and the
+ * summary.  collect_tell (bf16_search.rs:494-516). */
+ENNX_B200_API int32_t ennx_b200_bf16_search_collect(ennx_b200_bf16_search* search, size_t count,
+                                                    uint8_t* accepted, ennx_b200_tell_summary* summary);
+/* Device pointer of one row slot (device_row) and of the batch of the last
+ * ask, `rows` x len contiguous (device_round). */
+ENNX_B200_API int32_t ennx_b200_bf16_search_row(ennx_b200_bf16_search* search, size_t slot,
+                                                const uint16_t** row);
+ENNX_B200_API int32_t ennx_b200_bf16_search_round(ennx_b200_bf16_search* search, size_t rows,
+                                                  const uint16_t** batch);
+/* Gather row slots into the batch, `count` x len (device_batch). */
+ENNX_B200_API int32_t ennx_b200_bf16_search_gather(ennx_b200_bf16_search* search, const uint32_t* slots,
+                                                   size_t count, const uint16_t** batch);
+/* Make `consumer` see all enqueued work: mode 0 synchronises, 1 does
+ * nothing, 2 makes `consumer` wait on an event (sync_stream,
+ * cuda/src/lib.rs:1014-1033). */
+ENNX_B200_API int32_t ennx_b200_bf16_search_handoff(ennx_b200_bf16_search* search, void* consumer,
+                                                    int32_t mode);
+/* Copy the per-candidate scores and summed distances (history stride 128)
+ * of the last ask to host memory; test and tracing aid. */
+ENNX_B200_API int32_t ennx_b200_bf16_search_last_scores(ennx_b200_bf16_search* search, float* scores,
+                                                        size_t num_scores, float* distances,
+                                                        size_t num_distances);
+/* CUDA-event timing of asks (AskProfile): out[0..3] = score, pick,
+ * materialize, total milliseconds of the last ask; *available = 0 when
+ * profiling was off.  Synchronises. */
+ENNX_B200_API int32_t ennx_b200_bf16_search_set_profiling(ennx_b200_bf16_search* search, int32_t enabled);
+ENNX_B200_API int32_t ennx_b200_bf16_search_last_profile(ennx_b200_bf16_search* search, float* out,
+                                                         int32_t* available);
+
 /* ---- measurement (CUDA-event timing per kernel class, the counterpart of
  *      the reference's AskProfile / ENNX_CUDA_PROFILE, cuda/src/lib.rs:165-171,
  *      977-1005) --------------------------------------------------------- */

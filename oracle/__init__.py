@@ -91,6 +91,10 @@ def lib():
             "eo_rope": (None, [P, sz, sz, sz, sz, ctypes.c_double]),
             "eo_gqa_attention": (None, [P, P, P, sz, sz, sz, sz, sz, P]),
             "eo_cross_entropy_rows": (None, [P, P, sz, sz, P]),
+            "eo_bf16_seed": (ctypes.c_uint16, [ctypes.c_uint16, u64, u64, u64, f32, f32]),
+            "eo_search_candidate": (i32, [P, sz, P, sz, u64, f32, P]),
+            "eo_search_distances": (i32, [P, sz, sz, P, sz, P, sz, sz, u64, f32, P]),
+            "eo_draw_normal": (ctypes.c_double, [u64, u32, u32]),
         }
         for name, (res, args) in sig.items():
             fn = getattr(L, name)

@@ -582,3 +582,78 @@ void eo_cross_entropy_rows(const float* logits, const int32_t* targets, size_t r
         loss[r] = mx + log(s) - (double)x[targets[r]];
     }
 }
+
+/* ------------------------------------------------------------------------ */
+/* Resident BF16 search (cuda/kernels/src/bf16.rs:160-330, lib.rs:316-343)  */
+/* ------------------------------------------------------------------------ */
+
+/* bf16_seed: v + (scale*coef)*sign rounded to BF16, or one ulp toward the
+ * step when that leaves v unchanged; cuda/kernels/src/bf16.rs:160-176 */
+uint16_t eo_bf16_seed(uint16_t v, uint64_t key, uint64_t element, uint64_t seed, float scale, float coef) {
+    float dir = eo_dense_sign(seed, key, element);
+    float step = (scale * coef) * dir;
+    uint16_t cand = eo_bf16_encode(eo_bf16_decode(v) + step);
+    if (coef == 0.0f || cand == v) return eo_bf16_next(v, (coef > 0.0f) == (dir > 0.0f));
+    return cand;
+}
+
+static size_t search_leaf_of(const eo_bf16_leaf* leaves, size_t nl, size_t e) {
+    size_t l = 0;
+    while (l + 1 < nl && leaves[l + 1].offset <= e) ++l;
+    return l;
+}
+
+/* The candidate row of one seed around `base`; returns 1 if any value is
+ * not finite (write_bf16, lib.rs:2053-2130). */
+int32_t eo_search_candidate(const uint16_t* base, size_t len, const eo_bf16_leaf* leaves, size_t nl,
+                            uint64_t seed, float coef, uint16_t* out) {
+    int32_t invalid = 0;
+    size_t l = 0;
+    for (size_t e = 0; e < len; ++e) {
+        while (l + 1 < nl && leaves[l + 1].offset <= e) ++l;
+        uint16_t r = eo_bf16_seed(base[e], leaves[l].key, (uint64_t)(e - leaves[l].offset), seed,
+                                  leaves[l].scale, coef);
+        if ((r & 0x7f80u) == 0x7f80u) invalid = 1;
+        out[e] = r;
+    }
+    return invalid;
+}
+
+/* Weighted squared distances of one seeded candidate to `history` rows,
+ * accumulated in double (tile_distances, bf16.rs:278-330, restated without
+ * its fp32 summation order).  Returns 1 (and +inf distances) if the
+ * candidate has a non-finite value. */
+int32_t eo_search_distances(const uint16_t* rows, size_t stride, size_t base_slot, const uint32_t* history_slots,
+                            size_t history, const eo_bf16_leaf* leaves, size_t nl, size_t len, uint64_t seed,
+                            float coef, double* out) {
+    for (size_t h = 0; h < history; ++h) out[h] = 0.0;
+    const uint16_t* base = rows + base_slot * stride;
+    for (size_t e = 0; e < len; ++e) {
+        size_t l = search_leaf_of(leaves, nl, e);
+        uint16_t c = eo_bf16_seed(base[e], leaves[l].key, (uint64_t)(e - leaves[l].offset), seed,
+                                  leaves[l].scale, coef);
+        if ((c & 0x7f80u) == 0x7f80u) {
+            for (size_t h = 0; h < history; ++h) out[h] = INFINITY;
+            return 1;
+        }
+        float cv = eo_bf16_decode(c);
+        for (size_t h = 0; h < history; ++h) {
+            float d = cv - eo_bf16_decode(rows[(size_t)history_slots[h] * stride + e]);
+            out[h] += (double)d * (double)d * (double)leaves[l].weight;
+        }
+    }
+    return 0;
+}
+
+/* draw_normal: Box-Muller over two splitmix64 outputs; lib.rs:316-343 */
+double eo_draw_normal(uint64_t seed, uint32_t index, uint32_t metric) {
+    const uint64_t prime = 1000003ull;
+    uint64_t base = (seed * prime + (uint64_t)index) * prime;
+    uint64_t combined = base + (uint64_t)metric;
+    uint64_t first = eo_mix64(combined), second = eo_mix64(combined ^ 0xd2b74407b1ce6e93ull);
+    const double inv = 1.0 / 9007199254740992.0;
+    double raw = (double)(first >> 11) * inv;
+    double u1 = raw < 1.0e-12 ? 1.0e-12 : (raw > 1.0 - 1.0e-12 ? 1.0 - 1.0e-12 : raw);
+    double u2 = (double)(second >> 11) * inv;
+    return sqrt(-2.0 * log(u1)) * cos(6.283185307179586 * u2);
+}

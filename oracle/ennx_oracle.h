@@ -57,6 +57,15 @@ int32_t eo_dense_linear_f32(const float* input, size_t columns, const float* wei
                             const float* bias, eo_view weight_view, eo_view bias_view,
                             const eo_term* terms, size_t nt, float* out);
 uint32_t eo_trial_hash(uint32_t seed_low, uint32_t seed_high, uint32_t element);
+/* resident BF16 search */
+typedef struct { uint64_t key; uint64_t offset; uint64_t length; float scale; float weight; } eo_bf16_leaf;
+uint16_t eo_bf16_seed(uint16_t v, uint64_t key, uint64_t element, uint64_t seed, float scale, float coef);
+int32_t eo_search_candidate(const uint16_t* base, size_t len, const eo_bf16_leaf* leaves, size_t nl,
+                            uint64_t seed, float coef, uint16_t* out);
+int32_t eo_search_distances(const uint16_t* rows, size_t stride, size_t base_slot, const uint32_t* history_slots,
+                            size_t history, const eo_bf16_leaf* leaves, size_t nl, size_t len, uint64_t seed,
+                            float coef, double* out);
+double eo_draw_normal(uint64_t seed, uint32_t index, uint32_t metric);
 uint32_t eo_perturb_code(uint32_t code, uint32_t seed_low, uint32_t seed_high, uint32_t element,
                          uint32_t bits, uint32_t whole, uint32_t threshold);
 

@@ -19,10 +19,11 @@
 //     differences: |c|^2 + |h|^2 - 2 c.h on tensor cores would cancel
 //     catastrophically, since candidates and history rows all lie within a
 //     trust region around the same base.
-//   * search_score_pick_kernel: per region, sums the tile partials in a fixed
-//     order, runs the k-nearest-neighbour acquisition (bit-exact float order
-//     of acquisition_score, bf16.rs:224-275) and picks the best candidate
-//     (lower index on ties, lib.rs:1660-1744) -- score and pick in one launch.
+//   * search_score_pick_kernel: per candidate, sums the tile partials in a
+//     fixed tree order with the whole CTA, runs the k-nearest-neighbour
+//     acquisition (the float order of acquisition_score, bf16.rs:224-275);
+//     the region's last CTA to finish picks its best candidate (lower index
+//     on ties, lib.rs:1660-1744) -- score and pick in one launch.
 //   * search_write_kernel: materialises the selected candidates (bf16_seed).
 //   * search_tell_plan_kernel + search_tell_copy_kernel: the sequential
 //     bookkeeping of tell_bf16 on one thread, then the row copies it decides
@@ -43,7 +44,8 @@ constexpr int kThreads = 256;
 constexpr int kTileElems = kThreads * 8;  // one 16-byte vector per thread
 constexpr int kMaxHistory = 128;          // MAX_HISTORY, cuda/kernels/src/lib.rs:18
 constexpr int kMaxPending = 32;           // BF16_MAX_PENDING, bf16_search.rs:7
-constexpr int kChunk = 8;                 // candidates per distance pass
+constexpr int kChunk = 8;                 // candidates per register pass
+constexpr int kGroup = 32;                // candidates sharing one pass over the history
 
 struct SearchLeaf {  // Bf16Leaf with mix64(key ^ K) precomputed
   uint64_t key_mix;
@@ -99,6 +101,7 @@ struct AskArgs {
   uint16_t* rows_out;
   uint16_t* batch;
   uint32_t* region_status;         // [regions]
+  uint32_t* region_done;           // [regions] tickets of the score kernel
 };
 
 // trial_hash, cuda/kernels/src/lib.rs:150-158
@@ -131,9 +134,20 @@ __device__ __forceinline__ uint32_t history_rows(const AskArgs& a) {
 // bf16_seed (cuda/kernels/src/bf16.rs:160-176): v + scale*coef*sign rounded
 // to BF16, or one ulp toward the step if that leaves v unchanged.  The
 // products and the sum round separately, as in the reference.
+// Bit 0 of mix64(x), the sign of dense_sign (lib.rs:345-353): the last
+// xor-shift makes it bit0 ^ bit31 of the last product, whose low 32 bits only
+// need the low 32 bits of its operands -- one 32-bit multiply instead of a
+// 64-bit one.
+__device__ __forceinline__ uint32_t mix64_bit0(uint64_t x) {
+  uint64_t v = x + 0x9e3779b97f4a7c15ull;
+  v = (v ^ (v >> 30)) * 0xbf58476d1ce4e5b9ull;
+  const uint32_t lo = (uint32_t)(v ^ (v >> 27)) * 0x133111ebu;  // low word of 0x94d049bb133111eb
+  return (lo ^ (lo >> 31)) & 1u;
+}
+
 __device__ __forceinline__ uint16_t bf16_seed(uint16_t v, uint64_t key_mix, uint64_t emix, float scale,
                                               uint64_t seed, float coef) {
-  float dir = (mix64(seed ^ key_mix ^ emix) & 1ull) ? 1.0f : -1.0f;
+  float dir = mix64_bit0(seed ^ key_mix ^ emix) ? 1.0f : -1.0f;
   float x = __fadd_rn(bf16_to_f32(v), __fmul_rn(__fmul_rn(scale, coef), dir));
   uint16_t cand = f32_to_bf16_rne(x);
   if (coef == 0.0f || cand == v) return bf16_next(v, (coef > 0.0f) == (dir > 0.0f));
@@ -218,20 +232,31 @@ __device__ __forceinline__ float xpose_reduce16(float (&v)[16], int lane) {
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads) search_distance_kernel(const __grid_constant__ AskArgs a) {
   __shared__ float red[2][kThreads / 32][16];
-  __shared__ float part_sum[kChunk][kMaxHistory];
+  __shared__ float part_sum[kGroup][kMaxHistory];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const uint32_t H = history_rows(a);
   const float coef = step_coefficient(a);
   const uint64_t tiles = (a.len + kTileElems - 1) / kTileElems;
   int rbuf = 0;
-  for (uint32_t c0 = 0; c0 < a.candidates; c0 += kChunk) {
-    for (int i = tid; i < kChunk * kMaxHistory; i += kThreads) part_sum[i / kMaxHistory][i % kMaxHistory] = 0.0f;
-    uint64_t seed[kChunk];
+  // Candidates in groups of kGroup: per tile, every chunk of the group reads
+  // the same history tiles, so HBM sees each history row once per group.
+  for (uint32_t g0 = 0; g0 < a.candidates; g0 += kGroup) {
+    for (int i = tid; i < kGroup * kMaxHistory; i += kThreads) part_sum[i / kMaxHistory][i % kMaxHistory] = 0.0f;
+    __syncthreads();
+    for (uint64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x)
+    for (uint32_t c0 = g0; c0 < g0 + kGroup && c0 < a.candidates; c0 += kChunk) {
+      uint64_t seed[kChunk];
 #pragma unroll
-    for (int c = 0; c < kChunk; ++c) seed[c] = c0 + c < a.candidates ? candidate_seed(a, c0 + c) : 0;
-    for (uint64_t tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+      for (int c = 0; c < kChunk; ++c) seed[c] = c0 + c < a.candidates ? candidate_seed(a, c0 + c) : 0;
       const uint64_t e0 = tile * kTileElems + (uint64_t)tid * 8;
       const bool active = e0 < a.len;
+      // history rows 0 and 1 in flight while the candidates are generated
+      uint4 nxt[2];
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+        nxt[hh] = active && (uint32_t)hh < H
+                      ? ld_row16(a.rows + (uint64_t)__ldg(&a.history_slots[hh]) * a.stride + e0)
+                      : make_uint4(0, 0, 0, 0);
       // candidate values of this chunk for the thread's vector, packed bf16 pairs
       uint32_t cand[kChunk][4];
       uint64_t w2[4];
@@ -283,12 +308,13 @@ __global__ void __launch_bounds__(kThreads) search_distance_kernel(const __grid_
 #pragma unroll
         for (int c = 0; c < kChunk; ++c) { acc[c][0] = 0; acc[c][1] = 0; }
         if (active) {
-          uint4 hv[2];
+          const uint4 hv[2] = {nxt[0], nxt[1]};
+          // next pair in flight during this pair's arithmetic
 #pragma unroll
           for (int hh = 0; hh < 2; ++hh) {
-            const uint32_t h = h0 + hh;
-            hv[hh] = h < H ? ld_row16(a.rows + (uint64_t)__ldg(&a.history_slots[h]) * a.stride + e0)
-                           : make_uint4(0, 0, 0, 0);
+            const uint32_t h = h0 + 2 + hh;
+            nxt[hh] = h < H ? ld_row16(a.rows + (uint64_t)__ldg(&a.history_slots[h]) * a.stride + e0)
+                            : make_uint4(0, 0, 0, 0);
           }
 #pragma unroll
           for (int p = 0; p < 4; ++p) {
@@ -326,14 +352,14 @@ __global__ void __launch_bounds__(kThreads) search_distance_kernel(const __grid_
 #pragma unroll
           for (int w = 0; w < kThreads / 32; ++w) t += red[rbuf][w][tid];
           const uint32_t h = h0 + (tid & 1);
-          if (h < H) part_sum[tid >> 1][h] += t;
+          if (h < H) part_sum[c0 - g0 + (tid >> 1)][h] += t;
         }
         rbuf ^= 1;
       }
     }
     __syncthreads();
-    for (int i = tid; i < kChunk * kMaxHistory; i += kThreads) {
-      const uint32_t c = c0 + i / kMaxHistory, h = i % kMaxHistory;
+    for (int i = tid; i < kGroup * kMaxHistory; i += kThreads) {
+      const uint32_t c = g0 + i / kMaxHistory, h = i % kMaxHistory;
       if (c < a.candidates && h < H)
         a.partials[((uint64_t)blockIdx.x * a.candidates + c) * a.hstride + h] = part_sum[i / kMaxHistory][h];
     }
@@ -393,44 +419,79 @@ __device__ __forceinline__ bool better(float s, uint32_t i, float bs, uint32_t b
   return s > bs || (s == bs && i < bi);
 }
 
+// One CTA per candidate: the tile partials are summed by all threads in a
+// fixed tree order (deterministic for a given history length), thread 0
+// scores, and the last CTA of each region to finish -- found with an atomic
+// ticket, nothing waits -- picks the region's best (pick_trial order: higher
+// score, then lower index).
 __global__ void __launch_bounds__(kThreads) search_score_pick_kernel(const __grid_constant__ AskArgs a) {
-  __shared__ float dist[kThreads / 32][kMaxHistory];
-  __shared__ float nd[kThreads / 32][kMaxHistory];
-  __shared__ uint32_t ni[kThreads / 32][kMaxHistory];
-  __shared__ float best_s[kThreads / 32];
-  __shared__ uint32_t best_i[kThreads / 32];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const uint32_t region = blockIdx.x;
+  __shared__ float red[kThreads];
+  __shared__ float dist[kMaxHistory];
+  __shared__ float nd[kMaxHistory];
+  __shared__ uint32_t ni[kMaxHistory];
+  __shared__ uint32_t last;
+  const int tid = threadIdx.x;
+  const uint32_t c = blockIdx.x;
+  const uint32_t region = c / a.cpr;
   const uint32_t H = history_rows(a);
   const uint32_t K = min(a.neighbors, H);
+  uint32_t hp = 1;
+  while (hp < H) hp <<= 1;                  // history lanes (power of two <= 128)
+  const uint32_t slices = kThreads / hp;    // >= 2
+  const uint32_t h = tid % hp, sl = tid / hp;
+  float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+  if (h < H) {
+    const float* p = a.partials + (uint64_t)c * a.hstride + h;
+    const uint64_t step = (uint64_t)a.candidates * a.hstride;
+    uint32_t t = sl;
+    for (; t + 3 * slices < a.parts; t += 4 * slices) {
+      s0 += __ldcg(p + (uint64_t)t * step);
+      s1 += __ldcg(p + (uint64_t)(t + slices) * step);
+      s2 += __ldcg(p + (uint64_t)(t + 2 * slices) * step);
+      s3 += __ldcg(p + (uint64_t)(t + 3 * slices) * step);
+    }
+    for (; t < a.parts; t += slices) s0 += __ldcg(p + (uint64_t)t * step);
+  }
+  red[tid] = (s0 + s1) + (s2 + s3);
+  __syncthreads();
+  for (uint32_t half = slices / 2; half > 0; half >>= 1) {
+    if (sl < half) red[tid] += red[tid + half * hp];
+    __syncthreads();
+  }
+  if (tid < (int)H) {
+    dist[tid] = red[tid];
+    a.distances[(uint64_t)c * kMaxHistory + tid] = red[tid];
+  }
+  __syncthreads();
+  if (tid == 0) {
+    const float sc = (a.invalid[c] || !isfinite(dist[0])) ? -INFINITY : acquisition(a, dist, H, K, c, nd, ni);
+    a.scores[c] = sc;
+    __threadfence();
+    const uint32_t ticket = atomicAdd(&a.region_done[region], 1u);
+    last = ticket == a.cpr - 1;
+  }
+  __syncthreads();
+  if (!last || tid >= 32) return;
+  __threadfence();
   const uint32_t first = region * a.cpr, end = first + a.cpr;
   float bs = -INFINITY;
   uint32_t bi = 0xffffffffu;
-  for (uint32_t c = first + warp; c < end; c += kThreads / 32) {
-    for (uint32_t h = lane; h < H; h += 32) {
-      float d = 0.0f;
-      for (uint32_t t = 0; t < a.parts; ++t) d += a.partials[((uint64_t)t * a.candidates + c) * a.hstride + h];
-      dist[warp][h] = d;
-      a.distances[(uint64_t)c * kMaxHistory + h] = d;
-    }
-    __syncwarp();
-    if (lane == 0) {
-      float s = (a.invalid[c] || !isfinite(dist[warp][0])) ? -INFINITY
-                                                          : acquisition(a, dist[warp], H, K, c, nd[warp], ni[warp]);
-      a.scores[c] = s;
-      if (better(s, c, bs, bi)) { bs = s; bi = c; }
-    }
-    __syncwarp();
+  for (uint32_t q = first + tid; q < end; q += 32) {
+    const float sq = __ldcg(&a.scores[q]);
+    if (better(sq, q, bs, bi)) { bs = sq; bi = q; }
   }
-  if (lane == 0) { best_s[warp] = bs; best_i[warp] = bi; }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    for (int w = 1; w < kThreads / 32; ++w)
-      if (better(best_s[w], best_i[w], bs, bi)) { bs = best_s[w]; bi = best_i[w]; }
-    // A region whose candidates all scored NaN keeps index 0xffffffff;
-    // the host check (or the write kernel) treats it as invalid.
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) {
+    const float os = __shfl_xor_sync(0xffffffffu, bs, off);
+    const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, off);
+    if (better(os, oi, bs, bi)) { bs = os; bi = oi; }
+  }
+  if (tid == 0) {
+    // all-NaN regions keep index 0xffffffff: the host check or the write
+    // kernel treats it as invalid
     a.selection[region].index = bi;
     a.selection[region].score = bs;
+    a.region_done[region] = 0;
   }
 }
 
@@ -786,7 +847,8 @@ int32_t run_ask(ennx_b200_bf16_search* h, size_t base_slot, size_t history, cons
   ENNX_CUDA(cudaMemcpyAsync(h->trial_slots, trial_slots, regions * sizeof(uint32_t), cudaMemcpyHostToDevice, s),
             "trial slots");
   ENNX_CUDA(cudaMemsetAsync(h->invalid, 0, candidates * sizeof(uint32_t), s), "flags");
-  ENNX_CUDA(cudaMemsetAsync(h->region_status, 0, kMaxPending * sizeof(uint32_t), s), "status");
+  // region status words and the score kernel's tickets
+  ENNX_CUDA(cudaMemsetAsync(h->region_status, 0, 2 * kMaxPending * sizeof(uint32_t), s), "status");
 
   AskArgs a;
   memset(&a, 0, sizeof(a));
@@ -826,11 +888,12 @@ int32_t run_ask(ennx_b200_bf16_search* h, size_t base_slot, size_t history, cons
   a.rows_out = h->rows;
   a.batch = h->batch;
   a.region_status = h->region_status;
+  a.region_done = h->region_status + kMaxPending;
 
   if (h->profiling) ENNX_CUDA(cudaEventRecord(h->ev[0], s), "event");
   search_distance_kernel<<<parts, kThreads, 0, s>>>(a);
   ENNX_LAUNCH_CHECK("search_distance launch");
-  search_score_pick_kernel<<<(unsigned)regions, kThreads, 0, s>>>(a);
+  search_score_pick_kernel<<<(unsigned)candidates, kThreads, 0, s>>>(a);
   ENNX_LAUNCH_CHECK("search_score_pick launch");
   if (h->profiling) ENNX_CUDA(cudaEventRecord(h->ev[1], s), "event");
   dim3 wgrid((unsigned)((h->len + kTileElems - 1) / kTileElems), (unsigned)regions);
@@ -921,12 +984,12 @@ int32_t ennx_b200_bf16_search_create(const uint16_t* base, size_t len, const enn
     if ((st = dev_alloc((void**)&h->accepted, kMaxPending * sizeof(uint32_t), "accepted"))) break;
     if ((st = dev_alloc((void**)&h->tell_values, kMaxPending * sizeof(float), "tell values"))) break;
     if ((st = dev_alloc((void**)&h->tell_variances, kMaxPending * sizeof(float), "tell variances"))) break;
-    if ((st = dev_alloc((void**)&h->region_status, kMaxPending * sizeof(uint32_t), "status"))) break;
+    if ((st = dev_alloc((void**)&h->region_status, 2 * kMaxPending * sizeof(uint32_t), "status"))) break;
     if ((st = dev_alloc((void**)&h->plan, sizeof(CopyPlan), "plan"))) break;
     if ((st = dev_alloc((void**)&h->selection, kMaxPending * sizeof(ennx_b200_selection), "selection"))) break;
     if ((st = dev_alloc((void**)&h->trial_slots, kMaxPending * sizeof(uint32_t), "trial slots"))) break;
     e = cudaMemsetAsync(h->state, 0, sizeof(SearchStateDev), h->stream);
-    if (e == cudaSuccess) e = cudaMemsetAsync(h->region_status, 0, kMaxPending * sizeof(uint32_t), h->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(h->region_status, 0, 2 * kMaxPending * sizeof(uint32_t), h->stream);
     if (e == cudaSuccess) e = cudaMemsetAsync(h->plan, 0, sizeof(CopyPlan), h->stream);
     if (e == cudaSuccess)
       e = cudaMemcpyAsync(h->rows, base, len * sizeof(uint16_t), cudaMemcpyDeviceToDevice, h->stream);

@@ -82,6 +82,20 @@ class PackedLinear(ctypes.Structure):
                 ("perturb_threshold", ctypes.c_uint32)]
 
 
+class KdaDecoderLayer(ctypes.Structure):
+    """ennx_b200_kda_decoder_layer: the packed linears of one decoder layer."""
+    _fields_ = [(n, PackedLinear) for n in ("qkv", "control", "output", "qkv_conv", "forget_b", "gate_b", "decay",
+                                            "time_bias", "output_norm", "attention_norm", "moe_norm", "router")] + \
+               [("expert_gate", ctypes.c_void_p), ("expert_up", ctypes.c_void_p), ("expert_down", ctypes.c_void_p)]
+
+
+class KdaDecoderConfig(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_uint32) for n in ("num_layers", "hidden", "heads", "head_width", "gate_rank",
+                                               "num_experts", "top_k", "expert_width")] + \
+               [("residual_scale", ctypes.c_float), ("rms_epsilon", ctypes.c_float),
+                ("embedding_scale", ctypes.c_float)]
+
+
 class PerturbSeed(ctypes.Structure):
     _fields_ = [("low", ctypes.c_uint32), ("high", ctypes.c_uint32), ("enabled", ctypes.c_uint32)]
 
@@ -124,6 +138,13 @@ SIGNATURES = {
     "ennx_b200_check_bf16": (_I32, [_P, _SZ, _P, _P]),
     "ennx_b200_dense_dist2": (_I32, [_P, _SZ, _P, _SZ, _P, _SZ, _P]),
     "ennx_b200_bf16_search_create": (_I32, [_P, _SZ, _P, _SZ, _SZ, _P, _P]),
+    "ennx_b200_kda_decoder_create": (_I32, [_P, _SZ, _P, _SZ, _P, _SZ, _P, _P, _P, _P, _P, _P]),
+    "ennx_b200_kda_decoder_destroy": (_I32, [_P]),
+    "ennx_b200_kda_decoder_reset": (_I32, [_P]),
+    "ennx_b200_kda_decoder_prepare": (_I32, [_P, _U64]),
+    "ennx_b200_kda_decoder_decode_token": (_I32, [_P, _U32, _U64, _P]),
+    "ennx_b200_kda_decoder_generate": (_I32, [_P, _P, _SZ, _SZ, _U64, _P]),
+    "ennx_b200_kda_decoder_logits": (_I32, [_P, _P, _SZ]),
     "ennx_b200_bf16_search_destroy": (_I32, [_P]),
     "ennx_b200_bf16_search_init": (_I32, [_P, _F32, _F32, _SZ, ctypes.c_double, ctypes.c_double, ctypes.c_double]),
     "ennx_b200_bf16_search_copy_row": (_I32, [_P, _SZ, _SZ]),

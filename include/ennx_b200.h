@@ -477,6 +477,62 @@ ENNX_B200_API int32_t ennx_b200_bf16_search_set_profiling(ennx_b200_bf16_search*
 ENNX_B200_API int32_t ennx_b200_bf16_search_last_profile(ennx_b200_bf16_search* search, float* out,
                                                          int32_t* available);
 
+/* ---- resident single-token KDA-MoE decoder on packed weights (replaces
+ *      NativeKdaModel / KdaMoeMetalModel, rust/crates/ennx-py/src/
+ *      py_experimental.rs:163-315, rust/crates/ennx/src/forward_metal.rs:
+ *      614-810, 1140-1394; Metal-only there) ---------------------------- */
+
+/* The packed linears of one layer, named as the reference's model package
+ * names them: layers.{i}.attention.{qkv, control, output, qkv_conv,
+ * forget_b, gate_b, decay, time_bias, output_norm},
+ * layers.{i}.{attention_norm, moe_norm}, layers.{i}.moe.router and
+ * layers.{i}.moe.experts.{e}.{gate, up, down} (host arrays of num_experts). */
+typedef struct {
+    ennx_b200_packed_linear qkv, control, output, qkv_conv, forget_b, gate_b;
+    ennx_b200_packed_linear decay, time_bias, output_norm, attention_norm, moe_norm, router;
+    const ennx_b200_packed_linear* expert_gate;
+    const ennx_b200_packed_linear* expert_up;
+    const ennx_b200_packed_linear* expert_down;
+} ennx_b200_kda_decoder_layer;
+
+typedef struct {
+    uint32_t num_layers, hidden, heads, head_width, gate_rank, num_experts, top_k, expert_width;
+    float residual_scale, rms_epsilon, embedding_scale;
+} ennx_b200_kda_decoder_config;
+
+typedef struct ennx_b200_kda_decoder ennx_b200_kda_decoder;
+
+/* Copy the host arenas (packed u8 codes, f32 scales and biases) to the
+ * device, validate every linear's shape and arena bounds, reset the decode
+ * state and prepare candidate 0 (the reference constructor's order).
+ * `embedding` is tied: token lookup and LM head.  hidden = heads x
+ * head_width, head_width <= 128, top_k <= 8.  The decoder runs on its own
+ * stream; every call below synchronises before returning. */
+ENNX_B200_API int32_t ennx_b200_kda_decoder_create(const uint8_t* packed, size_t packed_bytes, const float* scales,
+                                                   size_t num_scales, const float* biases, size_t num_biases,
+                                                   const ennx_b200_kda_decoder_config* config,
+                                                   const ennx_b200_kda_decoder_layer* layers,
+                                                   const ennx_b200_packed_linear* embedding,
+                                                   const ennx_b200_packed_linear* final_norm, void* stream,
+                                                   ennx_b200_kda_decoder** out);
+ENNX_B200_API int32_t ennx_b200_kda_decoder_destroy(ennx_b200_kda_decoder* decoder);
+/* Zero the recurrent state and the convolution history of every layer. */
+ENNX_B200_API int32_t ennx_b200_kda_decoder_reset(ennx_b200_kda_decoder* decoder);
+/* Dequantise the norm / decay / time-bias vectors under `seed`
+ * (prepare_candidate, forward_metal.rs:1262-1283). */
+ENNX_B200_API int32_t ennx_b200_kda_decoder_prepare(ennx_b200_kda_decoder* decoder, uint64_t seed);
+/* One greedy step: embed `token`, run every layer, LM head, argmax. */
+ENNX_B200_API int32_t ennx_b200_kda_decoder_decode_token(ennx_b200_kda_decoder* decoder, uint32_t token,
+                                                         uint64_t seed, uint32_t* next_token);
+/* out[0..prompt_len) = prompt, then max_new_tokens greedy tokens; the token
+ * step is one CUDA graph replayed per token with the token fed back on the
+ * device. */
+ENNX_B200_API int32_t ennx_b200_kda_decoder_generate(ennx_b200_kda_decoder* decoder, const uint32_t* prompt,
+                                                     size_t prompt_len, size_t max_new_tokens, uint64_t seed,
+                                                     uint32_t* out);
+/* fp32 logits of the last step (host, vocab entries). */
+ENNX_B200_API int32_t ennx_b200_kda_decoder_logits(ennx_b200_kda_decoder* decoder, float* out, size_t vocab);
+
 /* ---- measurement (CUDA-event timing per kernel class, the counterpart of
  *      the reference's AskProfile / ENNX_CUDA_PROFILE, cuda/src/lib.rs:165-171,
  *      977-1005) --------------------------------------------------------- */

@@ -34,7 +34,7 @@ namespace {
 
 constexpr int kMaxKeyWidth = 128;   // kda_decode_step: min(key_width, 128)
 constexpr int kMaxTopK = 8;         // moe_router_topk_simd
-constexpr int kMaxExperts = 1024;   // router scores in shared memory
+constexpr int kMaxExperts = 1 << 16;  // router scores buffer
 
 struct LayerDev {  // device copies of one layer's descriptors
   PackedDesc qkv, control, output, conv, forget_b, gate_b, router;
@@ -57,8 +57,70 @@ struct Arena {
   const float* bi;
 };
 
-// Packed dot product of one weight row with x (fp32), lanes over 8-column
-// runs; the warp sum is returned in every lane.
+// perturb_code (kda_moe.metal:73-90) on one code
+__device__ __forceinline__ uint32_t perturb_one(uint32_t code, const PackedDesc& d, ennx_b200_perturb_seed s,
+                                                uint32_t element, uint32_t max_code) {
+  const uint32_t random = packed_hash(s.low, s.high, element);
+  const uint32_t amount = d.whole + (uint32_t)((random >> 1) < (d.threshold >> 1));
+  if (amount == 0u) return code;
+  if ((random & 1u) == 0u) return code >= amount ? code - amount : min(code + amount, max_code);
+  return code + amount <= max_code ? code + amount : code >= amount ? code - amount : 0u;
+}
+
+// Codes of one 64-column chunk as 32-bit words (int4: 8 words, int8: 16),
+// all loads issued before any is used; byte assembly where the arena offset
+// leaves the chunk unaligned.
+template <int kWords>
+__device__ __forceinline__ void load_chunk(const uint8_t* p, uint32_t (&cw)[kWords]) {
+  if (((uintptr_t)p & 3u) == 0) {
+#pragma unroll
+    for (int w = 0; w < kWords; ++w) cw[w] = __ldg(reinterpret_cast<const uint32_t*>(p) + w);
+  } else {
+#pragma unroll
+    for (int w = 0; w < kWords; ++w)
+      cw[w] = (uint32_t)__ldg(p + 4 * w) | ((uint32_t)__ldg(p + 4 * w + 1) << 8) |
+              ((uint32_t)__ldg(p + 4 * w + 2) << 16) | ((uint32_t)__ldg(p + 4 * w + 3) << 24);
+  }
+}
+
+// One 64-column chunk of a row: 8 runs of 8 columns, one scale/bias per run.
+template <bool kInt4>
+__device__ __forceinline__ float chunk_dot(const uint8_t* wrow, const float* srow, const float* brow,
+                                           const PackedDesc& d, ennx_b200_perturb_seed s, uint32_t elem_row,
+                                           uint32_t base, const float* __restrict__ x, float acc) {
+  constexpr int kWords = kInt4 ? 8 : 16;
+  constexpr uint32_t kMax = kInt4 ? 15u : 255u;
+  uint32_t cw[kWords];
+  load_chunk<kWords>(wrow + (kInt4 ? base / 2 : base), cw);
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    const uint32_t c0 = base + 8 * r;
+    const uint32_t g = min(c0 / d.group_size, (uint32_t)d.groups - 1u);
+    const float sc = __ldg(srow + g), bi = __ldg(brow + g);
+    float xv[8];
+    if (((uintptr_t)(x + c0) & 15u) == 0) {
+      const float4 a = __ldg(reinterpret_cast<const float4*>(x + c0));
+      const float4 b = __ldg(reinterpret_cast<const float4*>(x + c0 + 4));
+      xv[0] = a.x; xv[1] = a.y; xv[2] = a.z; xv[3] = a.w; xv[4] = b.x; xv[5] = b.y; xv[6] = b.z; xv[7] = b.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) xv[j] = __ldg(x + c0 + j);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      uint32_t code = kInt4 ? (cw[r] >> (4 * j)) & 15u : (cw[2 * r + (j >> 2)] >> (8 * (j & 3))) & 255u;
+      if (s.enabled) code = perturb_one(code, d, s, elem_row + c0 + j, kMax);
+      acc = fmaf(xv[j], __fmaf_rn((float)code, sc, bi), acc);
+    }
+  }
+  return acc;
+}
+
+// Packed dot product of one weight row with x (fp32); the warp sum is
+// returned in every lane.  Each lane takes contiguous 64-column chunks
+// (stride 2048 columns per warp) so that many independent code loads are in
+// flight per lane; chunks that leave the row or straddle a scale group of a
+// size that is not a multiple of 8 take the per-element path.
 __device__ __forceinline__ float warp_row_dot(const Arena& A, const PackedDesc& d, ennx_b200_perturb_seed seed,
                                               uint64_t row, const float* __restrict__ x, int lane) {
   // the reference enables perturbation for every seed; a descriptor with
@@ -66,12 +128,19 @@ __device__ __forceinline__ float warp_row_dot(const Arena& A, const PackedDesc& 
   ennx_b200_perturb_seed s = seed;
   if (d.whole == 0 && (d.threshold >> 1) == 0) s.enabled = 0;
   float acc = 0.0f;
-  const uint64_t n = d.input_width;
-  for (uint64_t c0 = (uint64_t)lane * 8; c0 < n; c0 += 256) {
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const uint64_t c = c0 + j;
-      if (c < n) acc = fmaf(__ldg(x + c), packed_weight(A.w, A.sc, A.bi, d, s, row, c), acc);
+  const uint32_t n = (uint32_t)d.input_width;
+  const bool fast = (d.group_size & 7u) == 0;
+  const uint8_t* wrow = A.w + d.byte_offset + row * d.row_bytes;
+  const float* srow = A.sc + d.scale_offset + row * d.groups;
+  const float* brow = A.bi + d.bias_offset + row * d.groups;
+  const uint32_t elem_row = (uint32_t)d.element_offset + (uint32_t)row * n;  // 32-bit, as the reference
+  for (uint32_t base = (uint32_t)lane * 64; base < n; base += 32 * 64) {
+    if (fast && base + 64 <= n) {
+      acc = d.bits == 4 ? chunk_dot<true>(wrow, srow, brow, d, s, elem_row, base, x, acc)
+                        : chunk_dot<false>(wrow, srow, brow, d, s, elem_row, base, x, acc);
+    } else {
+      for (uint32_t c = base; c < n && c < base + 64; ++c)
+        acc = fmaf(__ldg(x + c), packed_weight(A.w, A.sc, A.bi, d, s, row, c), acc);
     }
   }
 #pragma unroll
@@ -100,26 +169,31 @@ struct GemvArgs {
 };
 
 // decoder_project_packed_simd / moe_gate_up_simd / moe_down_simd: one warp
-// per output row.  kResidual and kDown add residual_scale * result to y
-// (decoder_residual fused into the projection that produces the update).
+// per output row, one instantiation per mode.  kResidual and kDown add
+// residual_scale * result to y (decoder_residual fused into the projection
+// that produces the update).
+template <int kMode>
 __global__ void __launch_bounds__(256) dec_gemv_kernel(const __grid_constant__ GemvArgs g) {
   const int lane = threadIdx.x & 31;
   const uint32_t row = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (row >= g.rows) return;  // whole warps leave together
-  if (g.mode == kPlain || g.mode == kResidual) {
-    const float v = warp_row_dot(g.A, g.d, g.seed, row, g.x, lane);
-    if (lane == 0) g.y[row] = g.mode == kPlain ? v : g.y[row] + g.residual_scale * v;
-  } else if (g.mode == kGateUp) {
+  if constexpr (kMode == kPlain || kMode == kResidual) {
+    const PackedDesc d = g.d;
+    const float v = warp_row_dot(g.A, d, g.seed, row, g.x, lane);
+    if (lane == 0) g.y[row] = kMode == kPlain ? v : g.y[row] + g.residual_scale * v;
+  } else if constexpr (kMode == kGateUp) {
     const uint32_t rank = row / g.expert_width, feature = row % g.expert_width;
     const uint32_t e = g.route_idx[rank];
-    const float gv = warp_row_dot(g.A, g.gate[e], g.seed, feature, g.x, lane);
-    const float uv = warp_row_dot(g.A, g.up[e], g.seed, feature, g.x, lane);
+    const PackedDesc dg = g.gate[e];
+    const float gv = warp_row_dot(g.A, dg, g.seed, feature, g.x, lane);
+    const PackedDesc du = g.up[e];
+    const float uv = warp_row_dot(g.A, du, g.seed, feature, g.x, lane);
     if (lane == 0) g.y[row] = gv / (1.0f + expf(-gv)) * uv;
   } else {  // kDown: y[row] += rs * sum_rank w_rank * down_e(act_rank)[row]
     float sum = 0.0f;
     for (uint32_t r = 0; r < g.top_k; ++r) {
-      const uint32_t e = g.route_idx[r];
-      sum += g.route_w[r] * warp_row_dot(g.A, g.down[e], g.seed, row, g.x + (uint64_t)r * g.expert_width, lane);
+      const PackedDesc dd = g.down[g.route_idx[r]];
+      sum += g.route_w[r] * warp_row_dot(g.A, dd, g.seed, row, g.x + (uint64_t)r * g.expert_width, lane);
     }
     if (lane == 0) g.y[row] = g.y[row] + g.residual_scale * sum;
   }
@@ -209,40 +283,73 @@ __global__ void __launch_bounds__(256) dec_gate_beta_kernel(const float* __restr
   if (i % hw == 0) beta[h] = 1.0f / (1.0f + expf(-control[2 * rank + h]));
 }
 
-// kda_decode_step: one CTA per head, one thread per value column; the
-// column of the state stays in registers for the step.
-__global__ void __launch_bounds__(kMaxKeyWidth) dec_kda_step_kernel(const float* __restrict__ qkv,
-                                                                    const float* __restrict__ gate,
-                                                                    const float* __restrict__ beta,
-                                                                    float* __restrict__ state,
-                                                                    float* __restrict__ out, uint32_t heads,
-                                                                    uint32_t hw) {
-  __shared__ float sq[kMaxKeyWidth], sk[kMaxKeyWidth], sdecay[kMaxKeyWidth];
-  const uint32_t h = blockIdx.x, col = threadIdx.x;
+// kda_decode_step: CTA per (head, block of 32 value columns); its 8 warps
+// split the key rows (16 each at d_k = 128) and keep their part of each
+// column in registers across the two passes (read-out k.S of the decayed
+// state, then the delta-rule update and q.S), with fixed-order shared-memory
+// sums across the warps.
+constexpr int kStepWarps = 8;
+constexpr int kStepRows = kMaxKeyWidth / kStepWarps;  // rows per warp at most
+
+__global__ void __launch_bounds__(kStepWarps * 32) dec_kda_step_kernel(const float* __restrict__ qkv,
+                                                                       const float* __restrict__ gate,
+                                                                       const float* __restrict__ beta,
+                                                                       float* __restrict__ state,
+                                                                       float* __restrict__ out, uint32_t heads,
+                                                                       uint32_t hw) {
+  __shared__ float red[kStepWarps][32];
+  __shared__ float upd_s[32];
+  const uint32_t h = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const uint32_t col = blockIdx.y * 32 + lane;
   const uint32_t width = heads * hw;
   const uint32_t kw = hw < (uint32_t)kMaxKeyWidth ? hw : (uint32_t)kMaxKeyWidth;
-  if (col < kw) {
-    sq[col] = qkv[h * hw + col];
-    sk[col] = qkv[width + h * hw + col];
-    sdecay[col] = expf(gate[h * hw + col]);
+  const uint32_t per = (kw + kStepWarps - 1) / kStepWarps;
+  const uint32_t r0 = warp * per;
+  const bool live = col < hw;
+  float* S = state + (uint64_t)h * hw * hw + col;
+  const float* q = qkv + h * hw;
+  const float* k = qkv + width + h * hw;
+  const float* g = gate + h * hw;
+  float sv[kStepRows];
+  float part = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kStepRows; ++j) {
+    const uint32_t i = r0 + j;
+    sv[j] = 0.0f;
+    if ((uint32_t)j < per && i < kw && live) {
+      sv[j] = S[(uint64_t)i * hw] * expf(g[i]);
+      part = fmaf(k[i], sv[j], part);
+    }
+  }
+  red[warp][lane] = part;
+  __syncthreads();
+  if (warp == 0) {
+    float read = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kStepWarps; ++w) read += red[w][lane];
+    upd_s[lane] = live ? beta[h] * (qkv[2 * width + h * hw + col] - read) : 0.0f;
   }
   __syncthreads();
-  if (col >= hw) return;
-  // Two passes over the column (coalesced across the CTA's threads): the
-  // decayed state's read-out k.S, then the delta-rule update and q.S.  The
-  // second pass re-reads the column (an L1 hit) instead of holding 128 values
-  // in registers.
-  float* S = state + (uint64_t)h * hw * hw + col;
-  float read = 0.0f;
-  for (uint32_t i = 0; i < kw; ++i) read = fmaf(sk[i], S[(uint64_t)i * hw] * sdecay[i], read);
-  const float upd = beta[h] * (qkv[2 * width + h * hw + col] - read);
-  float res = 0.0f;
-  for (uint32_t i = 0; i < kw; ++i) {
-    const float si = fmaf(sk[i], upd, S[(uint64_t)i * hw] * sdecay[i]);
-    res = fmaf(sq[i], si, res);
-    S[(uint64_t)i * hw] = si;
+  const float upd = upd_s[lane];
+  part = 0.0f;
+#pragma unroll
+  for (int j = 0; j < kStepRows; ++j) {
+    const uint32_t i = r0 + j;
+    if ((uint32_t)j < per && i < kw && live) {
+      sv[j] = fmaf(k[i], upd, sv[j]);
+      part = fmaf(q[i], sv[j], part);
+      S[(uint64_t)i * hw] = sv[j];
+    }
   }
-  out[h * hw + col] = res * rsqrtf((float)kw);
+  __syncthreads();  // every warp has read red[] for the first sum
+  red[warp][lane] = part;
+  __syncthreads();
+  if (warp == 0 && live) {
+    float res = 0.0f;
+#pragma unroll
+    for (int w = 0; w < kStepWarps; ++w) res += red[w][lane];
+    out[h * hw + col] = res * rsqrtf((float)kw);
+  }
 }
 
 // kda_postprocess_16k: per-head RMS norm x output_norm x sigmoid(output gate)
@@ -272,38 +379,47 @@ __global__ void __launch_bounds__(256) dec_post_kernel(const float* __restrict__
   }
 }
 
-// moe_router_topk_simd: warps score the experts (packed dot), one thread
-// keeps the top k (strict '>', lower expert first on ties) and writes the
-// softmax over them.
-__global__ void __launch_bounds__(512) dec_router_kernel(Arena A, PackedDesc d, ennx_b200_perturb_seed seed,
-                                                         const float* __restrict__ x, uint32_t experts,
-                                                         uint32_t top_k, uint32_t* __restrict__ idx,
-                                                         float* __restrict__ wts) {
-  __shared__ float scores[kMaxExperts];
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (uint32_t e = warp; e < experts; e += blockDim.x >> 5) {
-    const float v = warp_row_dot(A, d, seed, e, x, lane);
-    if (lane == 0) scores[e] = v;
+// moe_router_topk_simd, second half: the expert scores come from the packed
+// GEMV (warp per expert, all SMs); one warp then takes k rounds of "highest
+// score, lowest expert index" -- the selection of the reference's insertion
+// with strict '>' -- and writes the softmax over the chosen scores.
+__global__ void __launch_bounds__(32) dec_topk_kernel(const float* __restrict__ scores, uint32_t experts,
+                                                      uint32_t top_k, uint32_t* __restrict__ idx,
+                                                      float* __restrict__ wts) {
+  __shared__ float val[kMaxTopK];
+  __shared__ uint32_t ind[kMaxTopK];
+  const uint32_t lane = threadIdx.x;
+  uint32_t taken_last = 0xffffffffu;
+  for (uint32_t r = 0; r < top_k; ++r) {
+    float best = -INFINITY;
+    uint32_t bi = 0xffffffffu;
+    for (uint32_t e = lane; e < experts; e += 32) {
+      bool taken = false;
+      for (uint32_t q = 0; q < r; ++q) taken |= ind[q] == e;
+      const float v = scores[e];
+      if (!taken && (v > best || (v == best && e < bi) || bi == 0xffffffffu)) { best = v; bi = e; }
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+      const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (oi != 0xffffffffu && (bi == 0xffffffffu || ob > best || (ob == best && oi < bi))) { best = ob; bi = oi; }
+    }
+    if (lane == 0) { val[r] = best; ind[r] = bi; }
+    __syncwarp();
+    taken_last = bi;
   }
-  __syncthreads();
-  if (threadIdx.x != 0) return;
-  float val[kMaxTopK];
-  uint32_t ind[kMaxTopK];
-  for (uint32_t r = 0; r < top_k; ++r) { val[r] = -INFINITY; ind[r] = 0; }
-  for (uint32_t e = 0; e < experts; ++e) {
-    const float sc = scores[e];
-    for (uint32_t r = 0; r < top_k; ++r)
-      if (sc > val[r]) {
-        for (uint32_t m = top_k - 1; m > r; --m) { val[m] = val[m - 1]; ind[m] = ind[m - 1]; }
-        val[r] = sc;
-        ind[r] = e;
-        break;
-      }
+  (void)taken_last;
+  if (lane == 0) {
+    const float mx = val[0];
+    float ex[kMaxTopK], den = 0.0f;
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r)
+      if ((uint32_t)r < top_k) { ex[r] = expf(val[r] - mx); den += ex[r]; }
+#pragma unroll
+    for (int r = 0; r < kMaxTopK; ++r)
+      if ((uint32_t)r < top_k) { idx[r] = ind[r]; wts[r] = ex[r] / den; }
   }
-  const float mx = val[0];
-  float den = 0.0f;
-  for (uint32_t r = 0; r < top_k; ++r) { val[r] = expf(val[r] - mx); den += val[r]; }
-  for (uint32_t r = 0; r < top_k; ++r) { idx[r] = ind[r]; wts[r] = val[r] / den; }
 }
 
 // decoder_argmax: 256 lanes scan strided logits (strict '>'), then a tree
@@ -337,6 +453,55 @@ __global__ void __launch_bounds__(256) dec_argmax_kernel(const float* __restrict
   }
 }
 
+// The perturbed codes of one candidate (seed), written once into a shadow
+// arena: integer-code perturbation depends on (seed, element) only, not on
+// the token, so every token of that candidate then reads ready codes and no
+// GEMV hashes.  One thread per byte (one int8 code or two int4 codes); the
+// job of a byte is found by binary search over the cumulative byte starts.
+struct ArenaJob {
+  PackedDesc d;
+  uint64_t first;  // first byte of this linear in the concatenated job range
+};
+
+__global__ void __launch_bounds__(256) dec_perturb_arena_kernel(const uint8_t* __restrict__ src,
+                                                                uint8_t* __restrict__ dst,
+                                                                const ArenaJob* __restrict__ jobs, uint32_t njobs,
+                                                                uint64_t total, ennx_b200_perturb_seed seed) {
+  constexpr uint64_t kChunkBytes = 64;  // one job search per chunk
+  for (uint64_t c0 = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) * kChunkBytes; c0 < total;
+       c0 += (uint64_t)gridDim.x * blockDim.x * kChunkBytes) {
+    uint32_t lo = 0, hi = njobs - 1;
+    while (lo < hi) {
+      const uint32_t mid = (lo + hi + 1) >> 1;
+      if (jobs[mid].first <= c0) lo = mid; else hi = mid - 1;
+    }
+    uint32_t j = lo;
+    uint64_t next = j + 1 < njobs ? jobs[j + 1].first : total;
+    for (uint64_t i = c0; i < c0 + kChunkBytes && i < total; ++i) {
+      while (i >= next) {
+        ++j;
+        next = j + 1 < njobs ? jobs[j + 1].first : total;
+      }
+      const PackedDesc& d = jobs[j].d;
+      const uint64_t b = i - jobs[j].first;
+      uint32_t v = src[d.byte_offset + b];
+      if (d.whole != 0 || (d.threshold >> 1) != 0) {
+        const uint64_t row = b / d.row_bytes, cb = b % d.row_bytes;
+        const uint32_t er = (uint32_t)d.element_offset + (uint32_t)row * (uint32_t)d.input_width;  // 32-bit
+        if (d.bits == 8) {
+          v = perturb_one(v, d, seed, er + (uint32_t)cb, 255u);
+        } else {
+          const uint32_t c = 2u * (uint32_t)cb;
+          const uint32_t a = perturb_one(v & 15u, d, seed, er + c, 15u);
+          const uint32_t z = c + 1 < d.input_width ? perturb_one(v >> 4, d, seed, er + c + 1, 15u) : (v >> 4);
+          v = a | (z << 4);
+        }
+      }
+      dst[d.byte_offset + b] = (uint8_t)v;
+    }
+  }
+}
+
 }  // namespace
 }  // namespace ennx
 
@@ -359,14 +524,21 @@ struct ennx_b200_kda_decoder {
   float* final_norm_v;
   // activations
   float *hidden, *normed, *qkv, *control, *raw_gate, *ogate, *gate, *beta, *post, *gated, *act, *logits, *route_w;
+  float* scores;  // router scores [experts]
   uint32_t *route_idx, *token, *next, *out_tokens, *out_count;
   size_t out_cap;
   // graph of one token step
   cudaGraphExec_t graph;
-  uint64_t graph_seed;
   int have_graph;
   int has_logits;
   int own_stream;
+  // per-candidate perturbed codes
+  uint8_t* shadow;
+  ArenaJob* jobs;
+  uint32_t njobs;
+  uint64_t job_bytes;
+  uint64_t shadow_seed;
+  int have_shadow;
 };
 
 namespace {
@@ -387,7 +559,8 @@ void destroy_decoder(ennx_b200_kda_decoder* h) {
   void* ptrs[] = {h->packed,   h->scales,  h->biases,   h->expert_descs, h->final_norm_v, h->hidden,
                   h->normed,   h->qkv,     h->control,  h->raw_gate,     h->ogate,        h->gate,
                   h->beta,     h->post,    h->gated,    h->act,          h->logits,       h->route_w,
-                  h->route_idx, h->token,  h->next,     h->out_tokens,   h->out_count};
+                  h->route_idx, h->token,  h->next,     h->out_tokens,   h->out_count, h->scores,
+                  h->shadow,   h->jobs};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (h->layers) {
@@ -431,7 +604,12 @@ ennx_b200_perturb_seed seed_of(uint64_t s) {
 
 int32_t gemv(ennx_b200_kda_decoder* h, const GemvArgs& g) {
   const unsigned blocks = (g.rows + 7) / 8;
-  dec_gemv_kernel<<<blocks, 256, 0, h->stream>>>(g);
+  switch (g.mode) {
+    case kPlain: dec_gemv_kernel<kPlain><<<blocks, 256, 0, h->stream>>>(g); break;
+    case kResidual: dec_gemv_kernel<kResidual><<<blocks, 256, 0, h->stream>>>(g); break;
+    case kGateUp: dec_gemv_kernel<kGateUp><<<blocks, 256, 0, h->stream>>>(g); break;
+    default: dec_gemv_kernel<kDown><<<blocks, 256, 0, h->stream>>>(g); break;
+  }
   ENNX_LAUNCH_CHECK("decoder gemv");
   return ENNX_B200_OK;
 }
@@ -440,7 +618,7 @@ GemvArgs plain(ennx_b200_kda_decoder* h, const PackedDesc& d, const float* x, fl
                int mode) {
   GemvArgs g;
   memset(&g, 0, sizeof(g));
-  g.A = Arena{h->packed, h->scales, h->biases};
+  g.A = Arena{h->shadow, h->scales, h->biases};
   g.x = x;
   g.y = y;
   g.d = d;
@@ -456,8 +634,10 @@ GemvArgs plain(ennx_b200_kda_decoder* h, const PackedDesc& d, const float* x, fl
 int32_t enqueue_step(ennx_b200_kda_decoder* h, uint64_t seed64) {
   const ennx_b200_kda_decoder_config& c = h->cfg;
   cudaStream_t s = h->stream;
-  const ennx_b200_perturb_seed seed = seed_of(seed64);
-  const Arena A{h->packed, h->scales, h->biases};
+  // the codes in the shadow arena are already perturbed for this seed
+  ennx_b200_perturb_seed seed = seed_of(seed64);
+  seed.enabled = 0;
+  const Arena A{h->shadow, h->scales, h->biases};
   const uint32_t W = c.heads * c.head_width;
   PackedDesc emb, fin;
   ENNX_TRY(make_desc(&h->embedding, &emb));
@@ -479,16 +659,16 @@ int32_t enqueue_step(ennx_b200_kda_decoder* h, uint64_t seed64) {
     dec_gate_beta_kernel<<<(W + 255) / 256, 256, 0, s>>>(h->raw_gate, h->control, L.decay, L.time_bias, h->gate,
                                                          h->beta, c.heads, c.head_width, c.gate_rank);
     ENNX_LAUNCH_CHECK("decoder gate/beta");
-    dec_kda_step_kernel<<<c.heads, kMaxKeyWidth, 0, s>>>(h->qkv, h->gate, h->beta, L.state, h->post, c.heads,
-                                                         c.head_width);
+    dec_kda_step_kernel<<<dim3(c.heads, (c.head_width + 31) / 32), kStepWarps * 32, 0, s>>>(
+        h->qkv, h->gate, h->beta, L.state, h->post, c.heads, c.head_width);
     ENNX_LAUNCH_CHECK("decoder kda step");
     dec_post_kernel<<<c.heads, 256, 0, s>>>(h->post, h->ogate, L.out_norm, h->gated, c.head_width, c.rms_epsilon);
     ENNX_LAUNCH_CHECK("decoder post");
     ENNX_TRY(gemv(h, plain(h, L.output, h->gated, h->hidden, seed, kResidual)));
     dec_rmsnorm_kernel<<<1, 1024, 0, s>>>(h->hidden, L.moe_norm, h->normed, c.hidden, c.rms_epsilon);
     ENNX_LAUNCH_CHECK("decoder rmsnorm");
-    dec_router_kernel<<<1, 512, 0, s>>>(A, L.router, seed, h->normed, c.num_experts, c.top_k, h->route_idx,
-                                        h->route_w);
+    ENNX_TRY(gemv(h, plain(h, L.router, h->normed, h->scores, seed, kPlain)));
+    dec_topk_kernel<<<1, 32, 0, s>>>(h->scores, c.num_experts, c.top_k, h->route_idx, h->route_w);
     ENNX_LAUNCH_CHECK("decoder router");
     GemvArgs gu = plain(h, L.router, h->normed, h->act, seed, kGateUp);
     gu.gate = L.gate;
@@ -517,8 +697,22 @@ int32_t enqueue_step(ennx_b200_kda_decoder* h, uint64_t seed64) {
 
 // The step for `seed`, captured once and replayed (the seed is a kernel
 // argument, so a new seed recaptures).
+int32_t build_shadow(ennx_b200_kda_decoder* h, uint64_t seed) {
+  if (h->have_shadow && h->shadow_seed == seed) return ENNX_B200_OK;
+  uint64_t blocks = (h->job_bytes / 64 + 255) / 256 + 1;
+  const uint64_t cap = (uint64_t)sm_count() * 16;
+  if (blocks > cap) blocks = cap;
+  dec_perturb_arena_kernel<<<(unsigned)blocks, 256, 0, h->stream>>>(h->packed, h->shadow, h->jobs, h->njobs,
+                                                                    h->job_bytes, seed_of(seed));
+  ENNX_LAUNCH_CHECK("decoder perturbed arena");
+  h->have_shadow = 1;
+  h->shadow_seed = seed;
+  return ENNX_B200_OK;
+}
+
 int32_t run_step(ennx_b200_kda_decoder* h, uint64_t seed) {
-  if (!h->have_graph || h->graph_seed != seed) {
+  ENNX_TRY(build_shadow(h, seed));
+  if (!h->have_graph) {
     if (h->have_graph) {
       cudaGraphExecDestroy(h->graph);
       h->have_graph = 0;
@@ -536,7 +730,6 @@ int32_t run_step(ennx_b200_kda_decoder* h, uint64_t seed) {
     cudaGraphDestroy(g);
     ENNX_CUDA(e, "decoder graph instantiate");
     h->have_graph = 1;
-    h->graph_seed = seed;
   }
   ENNX_CUDA(cudaGraphLaunch(h->graph, h->stream), "decoder graph launch");
   note_launch(0);
@@ -682,6 +875,44 @@ int32_t ennx_b200_kda_decoder_create(const uint8_t* packed, size_t packed_bytes,
       D.time_bias = (float*)dalloc(W * sizeof(float), &st);
       D.out_norm = (float*)dalloc(c.head_width * sizeof(float), &st);
     }
+    // jobs of the per-candidate perturbation pass: every linear of the model
+    {
+      const size_t nj = (size_t)L * (12 + 3 * (size_t)E) + 2;
+      ArenaJob* jobs = (ArenaJob*)calloc(nj, sizeof(ArenaJob));
+      if (!jobs) { st = set_error(ENNX_B200_CUDA_ERROR, "out of host memory"); break; }
+      size_t n = 0;
+      uint64_t first = 0;
+      auto add = [&](const ennx_b200_packed_linear* l) {
+        PackedDesc d;
+        make_desc(l, &d);
+        jobs[n].d = d;
+        jobs[n].first = first;
+        first += d.row_bytes * d.output_width;
+        ++n;
+      };
+      add(embedding);
+      add(final_norm);
+      for (uint32_t l = 0; l < L; ++l) {
+        const ennx_b200_kda_decoder_layer& y = h->host_layers[l];
+        const ennx_b200_packed_linear* v[] = {&y.qkv,   &y.control,   &y.output,      &y.qkv_conv,
+                                              &y.forget_b, &y.gate_b, &y.decay,       &y.time_bias,
+                                              &y.output_norm, &y.attention_norm, &y.moe_norm, &y.router};
+        for (const ennx_b200_packed_linear* x : v) add(x);
+        const ennx_b200_packed_linear* he = h->host_experts + ((size_t)l * 3) * E;
+        for (uint32_t e = 0; e < 3 * E; ++e) add(&he[e]);
+      }
+      h->njobs = (uint32_t)n;
+      h->job_bytes = first;
+      h->jobs = (ArenaJob*)dalloc(n * sizeof(ArenaJob), &st);
+      h->shadow = (uint8_t*)dalloc(packed_bytes, &st);
+      if (!st) {
+        cudaError_t e = cudaMemcpyAsync(h->jobs, jobs, n * sizeof(ArenaJob), cudaMemcpyHostToDevice, h->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(h->stream);
+        if (e != cudaSuccess) st = check_cuda(e, "decoder jobs");
+      }
+      free(jobs);
+      if (st) break;
+    }
     h->final_norm_v = (float*)dalloc(c.hidden * sizeof(float), &st);
     h->hidden = (float*)dalloc(c.hidden * sizeof(float), &st);
     h->normed = (float*)dalloc(c.hidden * sizeof(float), &st);
@@ -696,6 +927,7 @@ int32_t ennx_b200_kda_decoder_create(const uint8_t* packed, size_t packed_bytes,
     h->act = (float*)dalloc((size_t)c.top_k * c.expert_width * sizeof(float), &st);
     h->logits = (float*)dalloc(embedding->output_width * sizeof(float), &st);
     h->route_w = (float*)dalloc(kMaxTopK * sizeof(float), &st);
+    h->scores = (float*)dalloc(c.num_experts * sizeof(float), &st);
     h->route_idx = (uint32_t*)dalloc(kMaxTopK * sizeof(uint32_t), &st);
     h->token = (uint32_t*)dalloc(sizeof(uint32_t), &st);
     h->next = (uint32_t*)dalloc(sizeof(uint32_t), &st);

@@ -407,14 +407,19 @@ def dense_linear(input, weight, weight_view, terms, bias=None, bias_view=None, d
 
 
 # The resident search classes live in ennx_b200.search (which imports this
-# module's ParamBlock and DLPack import); they resolve here on first use, as
-# the reference's experimental namespace resolves its names lazily.
+# module's ParamBlock and DLPack import) and the packed model classes in
+# ennx_b200.native; they resolve here on first use, as the reference's
+# experimental namespace resolves its names lazily.
 _SEARCH_NAMES = ("Proposals", "SearchState", "turbo_enn")
-__all__ += list(_SEARCH_NAMES)
+_NATIVE_NAMES = ("ModelPackage", "NativeKdaModel")
+__all__ += list(_SEARCH_NAMES) + list(_NATIVE_NAMES)
 
 
 def __getattr__(name: str):
     if name in _SEARCH_NAMES:
         from . import search
         return getattr(search, name)
+    if name in _NATIVE_NAMES:
+        from . import native
+        return getattr(native, name)
     raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

@@ -134,3 +134,20 @@ def test_host_rules_of_the_search_mirror():
         check(4, 0.0, 0.0, [B(1, 3)], 8, 1)
     with pytest.raises(ValueError, match="BF16 blocks cover 3 weights, expected 4"):
         check(4, 0.0, 0.0, [B(0, 3)], 8, 1)
+
+
+def test_oracle_full_history_reuses_the_oldest_slot():
+    """tell_history (cuda/kernels/src/lib.rs:446-472): at capacity the oldest
+    history slot is evicted and receives the new trial row."""
+    n = 128
+    o = S.SearchOracle(np.full(n, 0x3F80, np.uint16), [(4, 0, n, 0.05, 1.0)], 0.0, 3)
+    slots = []
+    for r in range(4):
+        p = o.ask_round(1, 2, 1, r)
+        trial = o.rows[p[0][1]].copy()
+        o.tell_round(p, [float(r + 1)])
+        assert o.sync() == [True]
+        slots.append(list(o.hist_slots))
+        assert np.array_equal(o.rows[o.hist_slots[-1]], trial) and np.array_equal(o.rows[0], trial)
+    assert slots == [[1, 2], [1, 2, 3], [2, 3, 1], [3, 1, 2]]
+    assert o.outcomes == [2.0, 3.0, 4.0]

@@ -7,7 +7,7 @@
 // Metal kernels it encodes (kda_moe.metal): decoder_rms_norm (:536-554),
 // decoder_project_packed_simd (:424-449), kda_short_conv_decode (:481-508),
 // kda_split_qkv_16k (:137-153), kda_normalize_qk (:510-534),
-// kda_split_control_16k (:847-867), kda_make_gate_beta_16k (:875-896),
+// kda_split_control_16k (:847-867), kda_make_gate_beta_16k (:875-896, fused into the step),
 // kda_decode_step (:283-338), kda_postprocess_16k (:898-921),
 // decoder_residual (:556-565), moe_router_topk_simd (:625-689),
 // moe_gate_up_simd / moe_down_simd (:759-834), packed_embedding_lookup
@@ -169,9 +169,10 @@ struct GemvArgs {
 };
 
 // decoder_project_packed_simd / moe_gate_up_simd / moe_down_simd: one warp
-// per output row, one instantiation per mode.  kResidual and kDown add
+// per output dot, one instantiation per mode.  kResidual adds
 // residual_scale * result to y (decoder_residual fused into the projection
-// that produces the update).
+// that produces the update); the expert modes give every (rank, row) dot its
+// own warp and leave SwiGLU and the rank sum to two short kernels.
 template <int kMode>
 __global__ void __launch_bounds__(256) dec_gemv_kernel(const __grid_constant__ GemvArgs g) {
   const int lane = threadIdx.x & 31;
@@ -182,21 +183,43 @@ __global__ void __launch_bounds__(256) dec_gemv_kernel(const __grid_constant__ G
     const float v = warp_row_dot(g.A, d, g.seed, row, g.x, lane);
     if (lane == 0) g.y[row] = kMode == kPlain ? v : g.y[row] + g.residual_scale * v;
   } else if constexpr (kMode == kGateUp) {
-    const uint32_t rank = row / g.expert_width, feature = row % g.expert_width;
+    // rows [0, k*I): gate dots, [k*I, 2*k*I): up dots, one warp each
+    const uint32_t half = g.top_k * g.expert_width;
+    const bool up = row >= half;
+    const uint32_t rr = up ? row - half : row;
+    const uint32_t rank = rr / g.expert_width, feature = rr % g.expert_width;
     const uint32_t e = g.route_idx[rank];
-    const PackedDesc dg = g.gate[e];
-    const float gv = warp_row_dot(g.A, dg, g.seed, feature, g.x, lane);
-    const PackedDesc du = g.up[e];
-    const float uv = warp_row_dot(g.A, du, g.seed, feature, g.x, lane);
-    if (lane == 0) g.y[row] = gv / (1.0f + expf(-gv)) * uv;
-  } else {  // kDown: y[row] += rs * sum_rank w_rank * down_e(act_rank)[row]
-    float sum = 0.0f;
-    for (uint32_t r = 0; r < g.top_k; ++r) {
-      const PackedDesc dd = g.down[g.route_idx[r]];
-      sum += g.route_w[r] * warp_row_dot(g.A, dd, g.seed, row, g.x + (uint64_t)r * g.expert_width, lane);
-    }
-    if (lane == 0) g.y[row] = g.y[row] + g.residual_scale * sum;
+    const PackedDesc d = up ? g.up[e] : g.gate[e];
+    const float v = warp_row_dot(g.A, d, g.seed, feature, g.x, lane);
+    if (lane == 0) g.y[row] = v;
+  } else {  // kDown: rows [r*H, (r+1)*H): w_r * down_e(act_r)[row], summed by dec_down_sum_kernel
+    const uint32_t hidden = g.rows / g.top_k;
+    const uint32_t r = row / hidden, f = row % hidden;
+    const PackedDesc dd = g.down[g.route_idx[r]];
+    const float v = warp_row_dot(g.A, dd, g.seed, f, g.x + (uint64_t)r * g.expert_width, lane);
+    if (lane == 0) g.y[row] = g.route_w[r] * v;
   }
+}
+
+// SwiGLU of the selected experts: act = silu(gate) * up
+__global__ void __launch_bounds__(256) dec_swiglu_kernel(const float* __restrict__ gu, float* __restrict__ act,
+                                                         uint32_t n) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float gv = gu[i];
+  act[i] = gv / (1.0f + expf(-gv)) * gu[n + i];
+}
+
+// hidden += residual_scale * sum over ranks (in rank order) of the weighted
+// expert outputs (moe_down_simd's sum + decoder_residual)
+__global__ void __launch_bounds__(256) dec_down_sum_kernel(const float* __restrict__ part,
+                                                           float* __restrict__ hidden, uint32_t top_k,
+                                                           uint32_t n, float rs) {
+  const uint32_t f = blockIdx.x * blockDim.x + threadIdx.x;
+  if (f >= n) return;
+  float sum = 0.0f;
+  for (uint32_t r = 0; r < top_k; ++r) sum += part[(uint64_t)r * n + f];
+  hidden[f] = hidden[f] + rs * sum;
 }
 
 // decoder_rms_norm: y = x * rsqrt(mean(x^2) + eps) * w; one CTA.
@@ -268,21 +291,6 @@ __global__ void __launch_bounds__(256) dec_l2norm_kernel(float* __restrict__ qkv
 
 __device__ __forceinline__ float softplus_stable(float x) { return fmaxf(x, 0.0f) + log1pf(expf(-fabsf(x))); }
 
-// kda_make_gate_beta_16k: g = max(-exp(decay_h) * softplus(raw + tb), -5),
-// beta = sigmoid(raw_beta) (raw_beta = control[2r + h])
-__global__ void __launch_bounds__(256) dec_gate_beta_kernel(const float* __restrict__ raw_gate,
-                                                            const float* __restrict__ control,
-                                                            const float* __restrict__ decay,
-                                                            const float* __restrict__ tb, float* __restrict__ gate,
-                                                            float* __restrict__ beta, uint32_t heads, uint32_t hw,
-                                                            uint32_t rank) {
-  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= heads * hw) return;
-  const uint32_t h = i / hw;
-  gate[i] = fmaxf(-expf(decay[h]) * softplus_stable(raw_gate[i] + tb[i]), -5.0f);
-  if (i % hw == 0) beta[h] = 1.0f / (1.0f + expf(-control[2 * rank + h]));
-}
-
 // kda_decode_step: CTA per (head, block of 32 value columns); its 8 warps
 // split the key rows (16 each at d_k = 128) and keep their part of each
 // column in registers across the two passes (read-out k.S of the decayed
@@ -291,12 +299,17 @@ __global__ void __launch_bounds__(256) dec_gate_beta_kernel(const float* __restr
 constexpr int kStepWarps = 8;
 constexpr int kStepRows = kMaxKeyWidth / kStepWarps;  // rows per warp at most
 
+// The gates of the step are formed here (kda_make_gate_beta_16k,
+// kda_moe.metal:869-896): g = max(-exp(decay_h) * softplus(raw + tb), -5) per
+// key row, beta = sigmoid(control[2r + h]).
 __global__ void __launch_bounds__(kStepWarps * 32) dec_kda_step_kernel(const float* __restrict__ qkv,
-                                                                       const float* __restrict__ gate,
-                                                                       const float* __restrict__ beta,
+                                                                       const float* __restrict__ raw_gate,
+                                                                       const float* __restrict__ control,
+                                                                       const float* __restrict__ decay,
+                                                                       const float* __restrict__ time_bias,
                                                                        float* __restrict__ state,
                                                                        float* __restrict__ out, uint32_t heads,
-                                                                       uint32_t hw) {
+                                                                       uint32_t hw, uint32_t rank) {
   __shared__ float red[kStepWarps][32];
   __shared__ float upd_s[32];
   const uint32_t h = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -309,7 +322,9 @@ __global__ void __launch_bounds__(kStepWarps * 32) dec_kda_step_kernel(const flo
   float* S = state + (uint64_t)h * hw * hw + col;
   const float* q = qkv + h * hw;
   const float* k = qkv + width + h * hw;
-  const float* g = gate + h * hw;
+  const float* rg = raw_gate + h * hw;
+  const float* tb = time_bias + h * hw;
+  const float ed = expf(decay[h]);
   float sv[kStepRows];
   float part = 0.0f;
 #pragma unroll
@@ -317,7 +332,8 @@ __global__ void __launch_bounds__(kStepWarps * 32) dec_kda_step_kernel(const flo
     const uint32_t i = r0 + j;
     sv[j] = 0.0f;
     if ((uint32_t)j < per && i < kw && live) {
-      sv[j] = S[(uint64_t)i * hw] * expf(g[i]);
+      const float gi = fmaxf(-ed * softplus_stable(rg[i] + tb[i]), -5.0f);
+      sv[j] = S[(uint64_t)i * hw] * expf(gi);
       part = fmaf(k[i], sv[j], part);
     }
   }
@@ -327,7 +343,8 @@ __global__ void __launch_bounds__(kStepWarps * 32) dec_kda_step_kernel(const flo
     float read = 0.0f;
 #pragma unroll
     for (int w = 0; w < kStepWarps; ++w) read += red[w][lane];
-    upd_s[lane] = live ? beta[h] * (qkv[2 * width + h * hw + col] - read) : 0.0f;
+    const float beta = 1.0f / (1.0f + expf(-control[2 * rank + h]));
+    upd_s[lane] = live ? beta * (qkv[2 * width + h * hw + col] - read) : 0.0f;
   }
   __syncthreads();
   const float upd = upd_s[lane];
@@ -389,7 +406,6 @@ __global__ void __launch_bounds__(32) dec_topk_kernel(const float* __restrict__ 
   __shared__ float val[kMaxTopK];
   __shared__ uint32_t ind[kMaxTopK];
   const uint32_t lane = threadIdx.x;
-  uint32_t taken_last = 0xffffffffu;
   for (uint32_t r = 0; r < top_k; ++r) {
     float best = -INFINITY;
     uint32_t bi = 0xffffffffu;
@@ -407,9 +423,7 @@ __global__ void __launch_bounds__(32) dec_topk_kernel(const float* __restrict__ 
     }
     if (lane == 0) { val[r] = best; ind[r] = bi; }
     __syncwarp();
-    taken_last = bi;
   }
-  (void)taken_last;
   if (lane == 0) {
     const float mx = val[0];
     float ex[kMaxTopK], den = 0.0f;
@@ -525,6 +539,8 @@ struct ennx_b200_kda_decoder {
   // activations
   float *hidden, *normed, *qkv, *control, *raw_gate, *ogate, *gate, *beta, *post, *gated, *act, *logits, *route_w;
   float* scores;  // router scores [experts]
+  float* gu;      // expert gate | up dots [2][top_k][expert_width]
+  float* part;    // weighted expert outputs [top_k][hidden]
   uint32_t *route_idx, *token, *next, *out_tokens, *out_count;
   size_t out_cap;
   // graph of one token step
@@ -560,7 +576,7 @@ void destroy_decoder(ennx_b200_kda_decoder* h) {
                   h->normed,   h->qkv,     h->control,  h->raw_gate,     h->ogate,        h->gate,
                   h->beta,     h->post,    h->gated,    h->act,          h->logits,       h->route_w,
                   h->route_idx, h->token,  h->next,     h->out_tokens,   h->out_count, h->scores,
-                  h->shadow,   h->jobs};
+                  h->shadow,   h->jobs,    h->gu,       h->part};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   if (h->layers) {
@@ -656,11 +672,9 @@ int32_t enqueue_step(ennx_b200_kda_decoder* h, uint64_t seed64) {
     ENNX_TRY(gemv(h, plain(h, L.control, h->normed, h->control, seed, kPlain)));
     ENNX_TRY(gemv(h, plain(h, L.forget_b, h->control, h->raw_gate, seed, kPlain)));
     ENNX_TRY(gemv(h, plain(h, L.gate_b, h->control + c.gate_rank, h->ogate, seed, kPlain)));
-    dec_gate_beta_kernel<<<(W + 255) / 256, 256, 0, s>>>(h->raw_gate, h->control, L.decay, L.time_bias, h->gate,
-                                                         h->beta, c.heads, c.head_width, c.gate_rank);
-    ENNX_LAUNCH_CHECK("decoder gate/beta");
     dec_kda_step_kernel<<<dim3(c.heads, (c.head_width + 31) / 32), kStepWarps * 32, 0, s>>>(
-        h->qkv, h->gate, h->beta, L.state, h->post, c.heads, c.head_width);
+        h->qkv, h->raw_gate, h->control, L.decay, L.time_bias, L.state, h->post, c.heads, c.head_width,
+        c.gate_rank);
     ENNX_LAUNCH_CHECK("decoder kda step");
     dec_post_kernel<<<c.heads, 256, 0, s>>>(h->post, h->ogate, L.out_norm, h->gated, c.head_width, c.rms_epsilon);
     ENNX_LAUNCH_CHECK("decoder post");
@@ -670,21 +684,28 @@ int32_t enqueue_step(ennx_b200_kda_decoder* h, uint64_t seed64) {
     ENNX_TRY(gemv(h, plain(h, L.router, h->normed, h->scores, seed, kPlain)));
     dec_topk_kernel<<<1, 32, 0, s>>>(h->scores, c.num_experts, c.top_k, h->route_idx, h->route_w);
     ENNX_LAUNCH_CHECK("decoder router");
-    GemvArgs gu = plain(h, L.router, h->normed, h->act, seed, kGateUp);
+    GemvArgs gu = plain(h, L.router, h->normed, h->gu, seed, kGateUp);
     gu.gate = L.gate;
     gu.up = L.up;
     gu.route_idx = h->route_idx;
-    gu.rows = c.top_k * c.expert_width;
+    gu.rows = 2 * c.top_k * c.expert_width;
+    gu.top_k = c.top_k;
     gu.expert_width = c.expert_width;
     ENNX_TRY(gemv(h, gu));
-    GemvArgs dn = plain(h, L.router, h->act, h->hidden, seed, kDown);
+    const uint32_t nact = c.top_k * c.expert_width;
+    dec_swiglu_kernel<<<(nact + 255) / 256, 256, 0, s>>>(h->gu, h->act, nact);
+    ENNX_LAUNCH_CHECK("decoder swiglu");
+    GemvArgs dn = plain(h, L.router, h->act, h->part, seed, kDown);
     dn.down = L.down;
     dn.route_idx = h->route_idx;
     dn.route_w = h->route_w;
-    dn.rows = c.hidden;
+    dn.rows = c.top_k * c.hidden;
     dn.top_k = c.top_k;
     dn.expert_width = c.expert_width;
     ENNX_TRY(gemv(h, dn));
+    dec_down_sum_kernel<<<(c.hidden + 255) / 256, 256, 0, s>>>(h->part, h->hidden, c.top_k, c.hidden,
+                                                               c.residual_scale);
+    ENNX_LAUNCH_CHECK("decoder expert sum");
   }
   dec_rmsnorm_kernel<<<1, 1024, 0, s>>>(h->hidden, h->final_norm_v, h->normed, c.hidden, c.rms_epsilon);
   ENNX_LAUNCH_CHECK("decoder final norm");
@@ -925,6 +946,8 @@ int32_t ennx_b200_kda_decoder_create(const uint8_t* packed, size_t packed_bytes,
     h->post = (float*)dalloc(W * sizeof(float), &st);
     h->gated = (float*)dalloc(W * sizeof(float), &st);
     h->act = (float*)dalloc((size_t)c.top_k * c.expert_width * sizeof(float), &st);
+    h->gu = (float*)dalloc(2ull * c.top_k * c.expert_width * sizeof(float), &st);
+    h->part = (float*)dalloc((size_t)c.top_k * c.hidden * sizeof(float), &st);
     h->logits = (float*)dalloc(embedding->output_width * sizeof(float), &st);
     h->route_w = (float*)dalloc(kMaxTopK * sizeof(float), &st);
     h->scores = (float*)dalloc(c.num_experts * sizeof(float), &st);

@@ -412,7 +412,8 @@ def dense_linear(input, weight, weight_view, terms, bias=None, bias_view=None, d
 # experimental namespace resolves its names lazily.
 _SEARCH_NAMES = ("Proposals", "SearchState", "turbo_enn")
 _NATIVE_NAMES = ("ModelPackage", "NativeKdaModel")
-__all__ += list(_SEARCH_NAMES) + list(_NATIVE_NAMES)
+_QUANT_NAMES = ("quantize_int4", "quantize_fp4_e2m1")
+__all__ += list(_SEARCH_NAMES) + list(_NATIVE_NAMES) + list(_QUANT_NAMES)
 
 
 def __getattr__(name: str):
@@ -422,4 +423,7 @@ def __getattr__(name: str):
     if name in _NATIVE_NAMES:
         from . import native
         return getattr(native, name)
+    if name in _QUANT_NAMES:
+        from . import quantization
+        return getattr(quantization, name)
     raise AttributeError(f"module {__name__!r} has no attribute {name!r}")

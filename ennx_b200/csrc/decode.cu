@@ -537,7 +537,7 @@ struct ennx_b200_kda_decoder {
   PackedDesc* expert_descs;                    // device [layers][3][experts]
   float* final_norm_v;
   // activations
-  float *hidden, *normed, *qkv, *control, *raw_gate, *ogate, *gate, *beta, *post, *gated, *act, *logits, *route_w;
+  float *hidden, *normed, *qkv, *control, *raw_gate, *ogate, *post, *gated, *act, *logits, *route_w;
   float* scores;  // router scores [experts]
   float* gu;      // expert gate | up dots [2][top_k][expert_width]
   float* part;    // weighted expert outputs [top_k][hidden]
@@ -573,8 +573,8 @@ void destroy_decoder(ennx_b200_kda_decoder* h) {
   if (!h) return;
   if (h->have_graph) cudaGraphExecDestroy(h->graph);
   void* ptrs[] = {h->packed,   h->scales,  h->biases,   h->expert_descs, h->final_norm_v, h->hidden,
-                  h->normed,   h->qkv,     h->control,  h->raw_gate,     h->ogate,        h->gate,
-                  h->beta,     h->post,    h->gated,    h->act,          h->logits,       h->route_w,
+                  h->normed,   h->qkv,     h->control,  h->raw_gate,     h->ogate,
+                  h->post,     h->gated,   h->act,      h->logits,       h->route_w,
                   h->route_idx, h->token,  h->next,     h->out_tokens,   h->out_count, h->scores,
                   h->shadow,   h->jobs,    h->gu,       h->part};
   for (void* p : ptrs)
@@ -941,8 +941,6 @@ int32_t ennx_b200_kda_decoder_create(const uint8_t* packed, size_t packed_bytes,
     h->control = (float*)dalloc((2ull * c.gate_rank + c.heads) * sizeof(float), &st);
     h->raw_gate = (float*)dalloc(W * sizeof(float), &st);
     h->ogate = (float*)dalloc(W * sizeof(float), &st);
-    h->gate = (float*)dalloc(W * sizeof(float), &st);
-    h->beta = (float*)dalloc(c.heads * sizeof(float), &st);
     h->post = (float*)dalloc(W * sizeof(float), &st);
     h->gated = (float*)dalloc(W * sizeof(float), &st);
     h->act = (float*)dalloc((size_t)c.top_k * c.expert_width * sizeof(float), &st);

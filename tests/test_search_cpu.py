@@ -151,3 +151,51 @@ def test_oracle_full_history_reuses_the_oldest_slot():
         assert np.array_equal(o.rows[o.hist_slots[-1]], trial) and np.array_equal(o.rows[0], trial)
     assert slots == [[1, 2], [1, 2, 3], [2, 3, 1], [3, 1, 2]]
     assert o.outcomes == [2.0, 3.0, 4.0]
+
+
+def _host_only_search(capacity=3, pending=2):
+    """A SearchState with its host bookkeeping only (no device handle): the
+    rules of bf16_search.rs:470-540 that run before any device call."""
+    s = object.__new__(P.SearchState)
+    s._capacity, s._pending_capacity, s._slots = capacity, pending, capacity + pending + 1
+    s._pending, s._exports, s._next_id, s._device_index = [], 0, 0, 0
+    return s
+
+
+def test_search_host_rules_without_a_device():
+    s = _host_only_search()
+    assert s._free_slots(2) == [4, 5]
+    s._pending = [(0, 4)]
+    assert s._free_slots(1) == [5]
+    with pytest.raises(ValueError, match="not enough free BF16 model slots"):
+        s._free_slots(2)
+    with pytest.raises(ValueError, match="duplicate trial"):
+        s._check_trials([(0, 4), (0, 4)])
+    with pytest.raises(ValueError, match="does not match an outstanding ask"):
+        s._check_trials([(1, 5)])
+    s._exports = 1
+    with pytest.raises(ValueError, match="release live JAX proposals"):
+        s._ensure_idle()
+    with pytest.raises(ValueError, match="release live JAX proposals"):
+        s.ask(1, 2, 1, 0)
+    s._exports = 0
+    with pytest.raises(ValueError, match="unknown acquisition 'ei'"):
+        s.ask(1, 2, 1, 0, acquisition="ei")
+    with pytest.raises(ValueError, match="tell must finish the outstanding BF16 round"):
+        s.ask(1, 2, 1, 0)
+    s._pending = []
+    with pytest.raises(ValueError, match="BF16 round shape exceeds pending capacity"):
+        s.ask(3, 2, 1, 0)
+    p = P.Proposals(s, [(0, 4)])
+    assert p.arms == 1
+    with pytest.raises(BufferError, match="does not export copies"):
+        p.__dlpack__(copy=True)
+    with pytest.raises(BufferError, match="cannot export to another device"):
+        p.__dlpack__(dl_device=(1, 0))
+    for bad in (0, -3):
+        with pytest.raises(ValueError, match="invalid DLPack CUDA stream"):
+            p.__dlpack__(stream=bad)
+    with pytest.raises(ValueError, match="equal non-zero length"):
+        s.tell(p, [1.0, 2.0])
+    with pytest.raises(ValueError, match="values and variances must be finite"):
+        s.tell(p, [float("nan")])

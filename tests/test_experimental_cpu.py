@@ -149,3 +149,27 @@ def test_dlpack_lease_is_released_by_the_consumer(max_version):
     del cap
     gc.collect()
     assert _dlpack.live_exports() == before and released == [1, 1]
+
+
+def test_param_buffer_host_rules_without_a_device():
+    """The lease and DLPack argument rules of py_weights.rs:61-103, which run
+    before any device work."""
+    pb = object.__new__(X.ParamBuffer)
+    pb._exported = True
+    with pytest.raises(ValueError, match="cannot materialize while a JAX candidate is alive"):
+        pb.materialize([(1, 1.0)])
+    pb._exported = False
+    with pytest.raises(ValueError, match="BF16 pytree terms cancel to zero"):
+        pb.materialize([(1, 1.0), (1, -1.0)])
+    with pytest.raises(ValueError, match="dense coefficient must be finite"):
+        pb.materialize([(1, float("inf"))])
+    with pytest.raises(BufferError, match="does not export copies"):
+        pb.__dlpack__(copy=True)
+    pb._device = torch.device("cuda", 0)
+    with pytest.raises(BufferError, match="cannot export to another device"):
+        pb.__dlpack__(dl_device=(1, 0))
+    with pytest.raises(ValueError, match="invalid DLPack CUDA stream"):
+        pb.__dlpack__(stream=0)
+    pb._exported = True
+    with pytest.raises(ValueError, match="already exported"):
+        pb.__dlpack__(stream=1)

@@ -199,6 +199,8 @@ def run_reference(args):
 
 
 def run_ours(args):
+    import ctypes
+
     import torch
     import torch.distributed as dist
 
@@ -255,9 +257,17 @@ def run_ours(args):
             dist.barrier()
         torch.cuda.synchronize()
 
+    def device_ok(where: str):
+        # every bounded device wait that gave up records a status; a run in
+        # which a kernel returned early must not report a number
+        st = _abi.lib().ennx_b200_device_status(ctypes.c_void_p(stream.cuda_stream))
+        if st != _abi.OK:
+            raise SystemExit(f"device status {st} after {where}: {_abi.lib().ennx_b200_last_error().decode()}")
+
     for i in range(args.warmup):
         step(i, False)
     barrier()
+    device_ok("warm-up")
     fit0 = fit_all.cpu()
     if not torch.isfinite(fit0).all():
         raise SystemExit(f"non-finite fitness {fit0}")
@@ -277,8 +287,6 @@ def run_ours(args):
         launches = _abi.lib().ennx_b200_launch_count() - n0
         prof = None
         if profile:
-            import ctypes
-
             class Entry(ctypes.Structure):
                 _fields_ = [("name", ctypes.c_char * 32), ("launches", ctypes.c_int64), ("total_ms", ctypes.c_double),
                             ("flops", ctypes.c_double), ("bytes", ctypes.c_double)]
@@ -296,8 +304,11 @@ def run_ours(args):
     clocks.start()
     ms, launches, _ = timed(False)
     clk = clocks.stop()
+    device_ok("the timed pass")
     ms_e2e, _, _ = timed(True)
+    device_ok("the end-to-end pass")
     _, _, prof = timed(False, profile=True)  # per-kernel CUDA-event breakdown (separate pass)
+    device_ok("the profiled pass")
 
     tokens_per_step = POP * BATCH * SEQ
     value = tokens_per_step * args.steps / (ms / 1000.0)

@@ -38,6 +38,9 @@ int32_t check_cuda(cudaError_t e, const char* what);
 // Device-side error word shared by every kernel of one process and device.
 // Kernels write a nonzero code (ENNX_B200_TIMEOUT, ...) instead of trapping.
 int* device_error_word();
+// an additional per-device status word (static device memory) that
+// consume_device_error also reads and clears
+void register_status_word(int dev, int* word);
 int32_t consume_device_error(cudaStream_t stream);  // synchronises `stream`
 
 // Number of SMs of the current device (cached per device).

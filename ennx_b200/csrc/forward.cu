@@ -427,9 +427,12 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
 // The noise stream perturbs job j+1 into layer slot (j+1)%2 while the compute
 // stream runs job j; a pair's embedding (= LM head) and final norm are
 // perturbed with its layer 0 into embedding slot i%2.
+// hidden_out (nullable): run only the first `stop_layers` layers of each pair
+// and copy the residual stream [2][batch*seq][hidden] there instead of the
+// LM head (per-layer parity checks).
 int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_weights& W, uint64_t seed, float sigma,
                        int first_pair, int num_pairs, int batch, int seq, Work& w, float* fitness,
-                       cudaStream_t caller) {
+                       cudaStream_t caller, int stop_layers = -1, uint16_t* hidden_out = nullptr) {
   PipeStreams* ps = nullptr;
   ENNX_TRY(pipe_streams(&ps));
   cudaStream_t cs = ps->compute, ns = ps->noise;
@@ -444,7 +447,7 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
   cudaEvent_t ready[2] = {ps->ev[2], ps->ev[3]}, freed[2] = {ps->ev[4], ps->ev[5]};
   cudaEvent_t emb_freed[2] = {ps->ev[6], ps->ev[7]};
   const long long Tc = (long long)batch * seq, T = 2 * Tc, H = c.hidden, V = c.vocab;
-  const int L = c.layers;
+  const int L = hidden_out ? stop_layers : c.layers;
   const int jobs = num_pairs * L;
 
   ENNX_CUDA(cudaEventRecord(ev_start, caller), "fork");
@@ -502,7 +505,13 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
     ENNX_TRY(compute_layer(c, l, layer_ptrs(c, l, w, slot), batch, seq, w, cs));
     ENNX_CUDA(cudaEventRecord(freed[slot], cs), "freed");
     freed_recorded[slot] = true;
-    if (l == L - 1) {
+    if (l == L - 1 && hidden_out) {
+      ENNX_CUDA(cudaMemcpyAsync(hidden_out + (size_t)i * T * H, w.hidden, sizeof(uint16_t) * (size_t)T * H,
+                                cudaMemcpyDeviceToDevice, cs),
+                "copy hidden state");
+      ENNX_CUDA(cudaEventRecord(emb_freed[es], cs), "emb freed");
+      emb_freed_recorded[es] = true;
+    } else if (l == L - 1) {
       uint16_t* fn = w.fnorm_scr[es];
       ENNX_TRY(launch_rmsnorm(w.hidden, H, fn, fn + H, Tc, w.xn, H, T, (int)H, c.rms_eps, cs));
       ennx_b200_gemm_params p;
@@ -634,6 +643,74 @@ int32_t ennx_b200_population_forward(const ennx_b200_model_config* cfg, const en
   ENNX_TRY(run_population(*cfg, *weights, seed, sigma, first_pair, num_pairs, batch, seq, w, fitness,
                           (cudaStream_t)stream));
   return ENNX_B200_OK;
+}
+
+int32_t ennx_b200_population_hidden(const ennx_b200_model_config* cfg, const ennx_b200_model_weights* weights,
+                                    uint64_t seed, float sigma, int32_t pair, int32_t layers, const int32_t* tokens,
+                                    int32_t batch, int32_t seq, uint16_t* hidden, void* workspace,
+                                    size_t workspace_bytes, void* stream) {
+  ENNX_TRY(validate_config(cfg, batch, seq));
+  if (!weights || !weights->embedding || !weights->final_norm || !weights->layers || !tokens || !hidden)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "population_hidden: null argument");
+  if (pair < 0 || layers < 1 || layers > cfg->layers)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "population_hidden: layers must be in [1, %d]", cfg->layers);
+  if (!isfinite(sigma) || sigma < 0.0f) return set_error(ENNX_B200_INVALID_ARGUMENT, "sigma must be finite and >= 0");
+  Work w;
+  carve_work(*cfg, batch, seq, nullptr, w);
+  if (!workspace || workspace_bytes < w.bytes)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "population_hidden: workspace of %zu bytes required", w.bytes);
+  carve_work(*cfg, batch, seq, (uint8_t*)workspace, w);
+  w.tokens = tokens;
+  return run_population(*cfg, *weights, seed, sigma, pair, 1, batch, seq, w, nullptr, (cudaStream_t)stream, layers,
+                        hidden);
+}
+
+int32_t ennx_b200_l2norm_heads_bf16(uint16_t* x, int64_t rows, int32_t heads, int64_t ld, void* stream) {
+  if (!x || rows <= 0 || heads <= 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "l2norm_heads: empty input");
+  if (ld < (int64_t)heads * HD || ld % 4 || ((uintptr_t)x & 7u))
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "l2norm_heads: 8-byte aligned rows with ld >= heads*128 required");
+  return launch_l2norm_heads(x, ld, heads, rows, (cudaStream_t)stream);
+}
+
+int32_t ennx_b200_kda_gate_beta(const uint16_t* raw_gate, int64_t ld_gate, const uint16_t* raw_beta, int64_t ld_beta,
+                                const uint16_t* decay, const uint16_t* time_bias, int64_t tokens, int32_t heads,
+                                float* gate, float* beta, void* stream) {
+  if (!raw_gate || !raw_beta || !decay || !time_bias || !gate || !beta || tokens <= 0 || heads <= 0)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "kda_gate_beta: null or empty argument");
+  if (ld_gate < (int64_t)heads * HD || ld_beta < heads)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "kda_gate_beta: row strides too small");
+  return launch_kda_gate(raw_gate, ld_gate, raw_beta, ld_beta, decay, nullptr, time_bias, nullptr, tokens, tokens,
+                         heads, HD, gate, beta, (cudaStream_t)stream);
+}
+
+int32_t ennx_b200_kda_postprocess(const uint16_t* o, const uint16_t* gate, int64_t ld_gate, const uint16_t* norm,
+                                  int64_t tokens, int32_t heads, float eps, uint16_t* out, void* stream) {
+  if (!o || !gate || !norm || !out || tokens <= 0 || heads <= 0)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "kda_postprocess: null or empty argument");
+  if (ld_gate < (int64_t)heads * HD || ld_gate % 4 || (((uintptr_t)o | (uintptr_t)gate | (uintptr_t)out) & 7u))
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "kda_postprocess: 8-byte aligned rows with ld >= heads*128 required");
+  return launch_kda_post(o, gate, ld_gate, norm, nullptr, tokens, heads, tokens, eps, out, (cudaStream_t)stream);
+}
+
+int32_t ennx_b200_kda_gated(const uint16_t* qkv, int64_t ld_qkv, const uint16_t* raw_gate, int64_t ld_gate,
+                            const uint16_t* raw_beta, int64_t ld_beta, const uint16_t* decay, const uint16_t* time_bias,
+                            float* state, uint16_t* o, int32_t batch, int32_t seq, int32_t heads, void* workspace,
+                            size_t workspace_bytes, void* stream) {
+  if (!qkv || !raw_gate || !raw_beta || !decay || !time_bias || !o)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "kda_gated: null argument");
+  const long long hw = (long long)heads * HD;
+  if (ld_qkv < 3 * hw || ld_gate < hw || ld_beta < heads || ld_gate % 8)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "kda_gated: row strides too small or unaligned");
+  KdaRawGate rg;
+  memset(&rg, 0, sizeof(rg));
+  rg.f = raw_gate; rg.ldf = ld_gate;
+  rg.rbeta = raw_beta; rg.ldb = ld_beta;
+  rg.decay0 = rg.decay1 = decay;
+  rg.tb0 = rg.tb1 = time_bias;
+  rg.split_seq = batch;
+  rg.active = 1;
+  return launch_kda_chunked(qkv, qkv + hw, qkv + 2 * hw, ld_qkv, nullptr, nullptr, state, o, hw, batch, seq, heads,
+                            workspace, workspace_bytes, (cudaStream_t)stream, &rg);
 }
 
 }  // extern "C"

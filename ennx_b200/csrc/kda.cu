@@ -738,7 +738,8 @@ size_t kda_workspace_bytes(int batch, int seq, int heads) {
 
 int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, long long ld_qkv, const float* g,
                            const float* beta, float* state, uint16_t* o, long long ldo, int batch, int seq, int heads,
-                           void* workspace, size_t workspace_bytes, cudaStream_t s, const KdaRawGate* raw) {
+                           void* workspace, size_t workspace_bytes, cudaStream_t s, const KdaRawGate* raw,
+                           int* err_word) {
   if (batch <= 0 || seq <= 0 || heads <= 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "kda: empty input");
   if (ld_qkv % 8 || ldo % 2 || (((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) & 15u))
     return set_error(ENNX_B200_INVALID_ARGUMENT, "kda: q/k/v must be 16-byte aligned with ld %% 8 == 0");
@@ -760,7 +761,9 @@ int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t*
   ENNX_TRY(make_tmap_2d_bf16(&tb, big, DK, R * 192, DK, 64, 64, true));
   ENNX_TRY(make_tmap_2d_bf16(&ts, small, C, R * 128, C, 64, 64, true));
   ENNX_TRY(make_tmap_2d_bf16(&tv, v, (uint64_t)heads * DK, (uint64_t)rows, (uint64_t)ld_qkv, DK, C, false));
-  int* err = device_error_word();
+  // A caller-supplied status word (the allocation-free entry point's static
+  // one) replaces the lazily allocated per-device word.
+  int* err = err_word ? err_word : device_error_word();
   if (!err) return set_error(ENNX_B200_CUDA_ERROR, "kda: no device error word");
   int dev = 0;
   cudaGetDevice(&dev);

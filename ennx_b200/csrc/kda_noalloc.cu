@@ -29,14 +29,22 @@ constexpr size_t kNoAllocScratchBytes = 32ull << 20;
 // comes from cudaGetSymbolAddress below.
 static __device__ __align__(256) uint8_t g_kda_scratch[kNoAllocScratchBytes];
 
+// This path's own status word: a bounded device wait that gives up writes
+// ENNX_B200_TIMEOUT here (the regular entry points use a word that is
+// allocated on first use, which this path must not do).  Zero-initialised at
+// module load; ennx_b200_device_status reads and clears it.
+static __device__ int g_kda_noalloc_status;
+
 constexpr int kMaxDevices = 64;
 void* g_scratch_ptr[kMaxDevices];
+int* g_status_ptr[kMaxDevices];
 std::mutex g_scratch_mu;
 
-// Resolve the device address of the scratch array once per device, with that
-// device current.  The first call on a device therefore runs this set-up and
-// should happen before any stream capture begins.
-int32_t scratch_address(void** out) {
+// Resolve the device addresses of the scratch array and of the status word
+// once per device, with that device current.  The first call on a device
+// therefore runs this set-up and should happen before any stream capture
+// begins.
+int32_t scratch_address(void** out, int** status) {
   int dev = 0;
   ENNX_CUDA(cudaGetDevice(&dev), "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return set_error(ENNX_B200_UNSUPPORTED, "device index %d out of range", dev);
@@ -45,9 +53,15 @@ int32_t scratch_address(void** out) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_kda_scratch);
     if (e != cudaSuccess || !p) return check_cuda(e, "cudaGetSymbolAddress(kda scratch)");
+    void* w = nullptr;
+    e = cudaGetSymbolAddress(&w, g_kda_noalloc_status);
+    if (e != cudaSuccess || !w) return check_cuda(e, "cudaGetSymbolAddress(kda status word)");
     g_scratch_ptr[dev] = p;
+    g_status_ptr[dev] = (int*)w;
+    register_status_word(dev, (int*)w);
   }
   *out = g_scratch_ptr[dev];
+  *status = g_status_ptr[dev];
   return ENNX_B200_OK;
 }
 
@@ -67,7 +81,8 @@ extern "C" int32_t ennx_b200_kda_chunked_noalloc(const uint16_t* q, const uint16
                      "holds %zu; use ennx_b200_kda_chunked with a caller workspace",
                      need, kNoAllocScratchBytes);
   void* scratch = nullptr;
-  ENNX_TRY(scratch_address(&scratch));
+  int* status = nullptr;
+  ENNX_TRY(scratch_address(&scratch, &status));
   return launch_kda_chunked(q, k, v, (long long)heads * 128, g, beta, state, o, (long long)heads * 128, batch, seq,
-                            heads, scratch, kNoAllocScratchBytes, (cudaStream_t)stream);
+                            heads, scratch, kNoAllocScratchBytes, (cudaStream_t)stream, nullptr, status);
 }

@@ -65,7 +65,7 @@ struct KdaRawGate {
 int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, long long ld_qkv,
                            const float* g, const float* beta, float* state, uint16_t* o, long long ldo, int batch,
                            int seq, int heads, void* workspace, size_t workspace_bytes, cudaStream_t s,
-                           const KdaRawGate* raw = nullptr);
+                           const KdaRawGate* raw = nullptr, int* err_word = nullptr);
 
 // dense.cu: W +/- sigma*eps; cols > 0 writes the [n/cols, cols] result as a
 // block of a matrix with row stride dld (noise indexed by the source element)

@@ -52,18 +52,39 @@ int* device_error_word() {
   return g_err_word[d];
 }
 
+static int* g_extra_word[kMaxDevices];
+
+void register_status_word(int dev, int* word) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (dev >= 0 && dev < kMaxDevices) g_extra_word[dev] = word;
+}
+
+// Reads and clears every status word of the current device: the shared word
+// of the regular entry points (only if it exists already: a word that was
+// never allocated was never written, so checking allocates nothing) and the
+// static word of the allocation-free entry point.
 int32_t consume_device_error(cudaStream_t stream) {
-  int* w = device_error_word();
-  if (!w) return set_error(ENNX_B200_CUDA_ERROR, "could not allocate the device error word");
-  ENNX_CUDA(cudaStreamSynchronize(stream), "stream synchronize");
-  int host = 0;
-  ENNX_CUDA(cudaMemcpy(&host, w, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
-  if (host != 0) {
-    cudaMemset(w, 0, sizeof(int));
-    if (host == ENNX_B200_TIMEOUT)
-      return set_error(ENNX_B200_TIMEOUT, "a device wait exceeded its bound; the kernel returned early");
-    return set_error(host, "device kernel reported status %d", host);
+  int d = current_device();
+  int* words[2];
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    words[0] = g_err_word[d];
+    words[1] = g_extra_word[d];
   }
+  ENNX_CUDA(cudaStreamSynchronize(stream), "stream synchronize");
+  int worst = 0;
+  for (int* w : words) {
+    if (!w) continue;
+    int host = 0;
+    ENNX_CUDA(cudaMemcpy(&host, w, sizeof(int), cudaMemcpyDeviceToHost), "read device error word");
+    if (host != 0) {
+      ENNX_CUDA(cudaMemset(w, 0, sizeof(int)), "clear device error word");
+      if (!worst) worst = host;
+    }
+  }
+  if (worst == ENNX_B200_TIMEOUT)
+    return set_error(ENNX_B200_TIMEOUT, "a device wait exceeded its bound; the kernel returned early");
+  if (worst) return set_error(worst, "device kernel reported status %d", worst);
   return ENNX_B200_OK;
 }
 

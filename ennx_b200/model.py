@@ -154,3 +154,16 @@ class PopulationEvaluator:
                   ctypes.c_void_p(fit.data_ptr()), ctypes.c_void_p(self.workspace.data_ptr()),
                   self.workspace.numel(), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         return fit
+
+    def hidden(self, tokens: torch.Tensor, seed: int, sigma: float, pair: int, layers: int) -> torch.Tensor:
+        """Residual stream after the first `layers` layers of antithetic pair
+        `pair`: bf16 [2, batch*seq, hidden] (sign + first) -- a per-layer
+        parity probe of the same device path as ``__call__``."""
+        if tokens.dtype != torch.int32 or tuple(tokens.shape) != (self.batch, self.seq + 1) or not tokens.is_cuda:
+            raise ValueError(f"tokens must be a CUDA int32 tensor of shape {(self.batch, self.seq + 1)}")
+        out = torch.empty(2, self.batch * self.seq, self.cfg.hidden, device=tokens.device, dtype=torch.bfloat16)
+        _abi.call("ennx_b200_population_hidden", ctypes.byref(self._ccfg), ctypes.byref(self._cw), seed, sigma, pair,
+                  layers, ctypes.c_void_p(tokens.data_ptr()), self.batch, self.seq, ctypes.c_void_p(out.data_ptr()),
+                  ctypes.c_void_p(self.workspace.data_ptr()), self.workspace.numel(),
+                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        return out

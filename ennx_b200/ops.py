@@ -162,3 +162,49 @@ def kda_chunked(q, k, v, g, beta, state: torch.Tensor | None = None) -> torch.Te
     _abi.call("ennx_b200_kda_chunked", _ptr(q), _ptr(k), _ptr(v), _ptr(g), _ptr(beta), _ptr(state), _ptr(o), B, T, H,
               _ptr(ws), nbytes, _stream())
     return o
+
+
+def l2norm_heads(x: torch.Tensor) -> torch.Tensor:
+    """In-place per-head L2 normalisation of bf16 [rows, heads*128] (returns x)."""
+    _check_dev(x)
+    rows, width = x.shape
+    _abi.call("ennx_b200_l2norm_heads_bf16", _ptr(x), rows, width // 128, x.stride(0), _stream())
+    return x
+
+
+def kda_gate_beta(raw_gate: torch.Tensor, raw_beta: torch.Tensor, decay: torch.Tensor, time_bias: torch.Tensor):
+    """(g f32 [T, heads*128], beta f32 [T, heads]) from bf16 raw projections."""
+    _check_dev(raw_gate, raw_beta, decay, time_bias)
+    T, width = raw_gate.shape
+    heads = width // 128
+    g = torch.empty(T, width, dtype=torch.float32, device=raw_gate.device)
+    b = torch.empty(T, heads, dtype=torch.float32, device=raw_gate.device)
+    _abi.call("ennx_b200_kda_gate_beta", _ptr(raw_gate), raw_gate.stride(0), _ptr(raw_beta), raw_beta.stride(0),
+              _ptr(decay), _ptr(time_bias), T, heads, _ptr(g), _ptr(b), _stream())
+    return g, b
+
+
+def kda_postprocess(o: torch.Tensor, gate: torch.Tensor, norm: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """Per-head RMSNorm x norm x sigmoid(gate); o, gate bf16 [T, heads*128], norm bf16 [128]."""
+    _check_dev(o, gate, norm)
+    T, width = o.shape
+    out = torch.empty_like(o)
+    _abi.call("ennx_b200_kda_postprocess", _ptr(o), _ptr(gate), gate.stride(0), _ptr(norm), T, width // 128, eps,
+              _ptr(out), _stream())
+    return out
+
+
+def kda_gated(qkv: torch.Tensor, raw_gate: torch.Tensor, raw_beta: torch.Tensor, decay: torch.Tensor,
+              time_bias: torch.Tensor, batch: int, seq: int, state: torch.Tensor | None = None) -> torch.Tensor:
+    """The forward's fused KDA: qkv bf16 [batch*seq, >= 3*heads*128] (q, k not
+    normalised), raw_gate bf16 [batch*seq, heads*128], raw_beta bf16
+    [batch*seq, >= heads]; returns o bf16 [batch*seq, heads*128]."""
+    _check_dev(qkv, raw_gate, raw_beta, decay, time_bias, state)
+    heads = raw_gate.shape[1] // 128
+    o = torch.empty(batch * seq, heads * 128, dtype=torch.bfloat16, device=qkv.device)
+    nbytes = _abi.lib().ennx_b200_kda_workspace_size(batch, seq, heads)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=qkv.device)
+    _abi.call("ennx_b200_kda_gated", _ptr(qkv), qkv.stride(0), _ptr(raw_gate), raw_gate.stride(0), _ptr(raw_beta),
+              raw_beta.stride(0), _ptr(decay), _ptr(time_bias), _ptr(state), _ptr(o), batch, seq, heads, _ptr(ws),
+              nbytes, _stream())
+    return o

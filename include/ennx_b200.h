@@ -235,10 +235,15 @@ ENNX_B200_API int32_t ennx_b200_kda_chunked(const uint16_t* q, const uint16_t* k
  * exit, so batch * heads * ceil(seq / 64) must stay <= 508 (66 048 bytes per
  * chunk record); larger problems are rejected with ENNX_B200_INVALID_ARGUMENT.
  * Calls allocate nothing (no cudaMalloc/cudaFree, no allocating library
- * call).  The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress) with that device current; make that first call
+ * call, and no lazily allocated status word either: a device wait that
+ * gives up writes ENNX_B200_TIMEOUT to a static status word of this path).
+ * The first call on a device looks up the addresses of the array and of that
+ * word (cudaGetSymbolAddress) with that device current; make that first call
  * before any stream capture.  Every call shares the one array: calls that
- * overlap on the GPU (different streams, or threads) race on it. */
+ * overlap on the GPU (different streams, or threads) race on it.  A call
+ * that returned early leaves a partial o/state; ennx_b200_device_status(stream)
+ * (outside any capture: it synchronises the stream) reports it and clears
+ * the word, and itself allocates nothing when no regular entry point ran. */
 ENNX_B200_API int32_t ennx_b200_kda_chunked_noalloc(const uint16_t* q, const uint16_t* k, const uint16_t* v,
                                                     const float* g, const float* beta, float* state,
                                                     uint16_t* o, int32_t batch, int32_t seq, int32_t heads,
@@ -300,6 +305,51 @@ ENNX_B200_API int32_t ennx_b200_population_forward(const ennx_b200_model_config*
                                                    const int32_t* tokens, int32_t batch, int32_t seq,
                                                    float* fitness, void* workspace, size_t workspace_bytes,
                                                    void* stream);
+
+/* Per-layer parity probe of the population forward: runs antithetic pair
+ * `pair` through the first `layers` decoder layers only and copies the
+ * residual stream after them to hidden (device bf16 [2][batch*seq][hidden],
+ * sign + first), instead of the LM head.  Same arguments and workspace as
+ * ennx_b200_population_forward.  No counterpart in the reference (its
+ * Metal executor exposes per-layer outputs only through its own buffers,
+ * forward_metal.rs:614-810). */
+ENNX_B200_API int32_t ennx_b200_population_hidden(const ennx_b200_model_config* cfg,
+                                                  const ennx_b200_model_weights* weights, uint64_t seed,
+                                                  float sigma, int32_t pair, int32_t layers,
+                                                  const int32_t* tokens, int32_t batch, int32_t seq,
+                                                  uint16_t* hidden, void* workspace, size_t workspace_bytes,
+                                                  void* stream);
+
+/* ---- KDA element-wise stages (the 16k-prefill kernels of kda_moe.metal) --- */
+
+/* In-place per-head L2 normalisation of bf16 rows (x[r, h*128 .. +127] /=
+ * max(|x|, 1e-6)), kda_normalize_qk (kda_moe.metal:510-534). */
+ENNX_B200_API int32_t ennx_b200_l2norm_heads_bf16(uint16_t* x, int64_t rows, int32_t heads, int64_t ld,
+                                                  void* stream);
+/* gate[t, j] = max(-exp(decay[j/128]) * softplus(raw_gate[t, j] + time_bias[j]), -5),
+ * beta[t, h] = sigmoid(raw_beta[t, h]); f32 outputs [tokens, heads*128] and
+ * [tokens, heads]; kda_make_gate_beta_16k + softplus_stable
+ * (kda_moe.metal:869-895). */
+ENNX_B200_API int32_t ennx_b200_kda_gate_beta(const uint16_t* raw_gate, int64_t ld_gate, const uint16_t* raw_beta,
+                                              int64_t ld_beta, const uint16_t* decay, const uint16_t* time_bias,
+                                              int64_t tokens, int32_t heads, float* gate, float* beta,
+                                              void* stream);
+/* out[t, h, :] = o[t, h, :] * rsqrt(mean(o[t, h, :]^2) + eps) * norm * sigmoid(gate[t, h*128 + :]),
+ * kda_postprocess_16k (kda_moe.metal:898-921). */
+ENNX_B200_API int32_t ennx_b200_kda_postprocess(const uint16_t* o, const uint16_t* gate, int64_t ld_gate,
+                                                const uint16_t* norm, int64_t tokens, int32_t heads, float eps,
+                                                uint16_t* out, void* stream);
+/* The forward's fused KDA: q, k, v are columns [0, hw), [hw, 2hw), [2hw, 3hw)
+ * of qkv rows (hw = heads*128, q and k NOT yet normalised); the chunk
+ * preparation applies the per-head L2 norm of q and k (rounded to bf16) and
+ * forms g and beta from the raw projections exactly as
+ * ennx_b200_l2norm_heads_bf16 / ennx_b200_kda_gate_beta define them, then
+ * runs the chunked recurrence of ennx_b200_kda_chunked. */
+ENNX_B200_API int32_t ennx_b200_kda_gated(const uint16_t* qkv, int64_t ld_qkv, const uint16_t* raw_gate,
+                                          int64_t ld_gate, const uint16_t* raw_beta, int64_t ld_beta,
+                                          const uint16_t* decay, const uint16_t* time_bias, float* state,
+                                          uint16_t* o, int32_t batch, int32_t seq, int32_t heads,
+                                          void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---- packed int4/int8 linear (KdaPackedLinear) ------------------------- */
 

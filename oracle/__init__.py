@@ -81,6 +81,7 @@ def lib():
             "eo_philox4x32_10": (None, [P, P, P]),
             "eo_noise8": (None, [u64, u32, u32, u64, P]),
             "eo_perturb_bf16": (None, [P, sz, u64, u32, u32, f32, ctypes.c_int, P]),
+            "eo_perturb_bf16_at": (None, [P, sz, sz, u64, u32, u32, f32, ctypes.c_int, P]),
             "eo_rmsnorm": (None, [P, P, sz, sz, f32, P]),
             "eo_router_logits": (None, [P, P, sz, sz, sz, P]),
             "eo_router_topk": (None, [P, sz, sz, sz, P, P]),
@@ -240,9 +241,23 @@ def noise(seed: int, pair: int, tensor: int, n: int, start: int = 0) -> np.ndarr
 
 
 def perturb_bf16(w_bits, seed, pair, tensor, sigma, sign):
+    """bf16 bits of W + sign*sigma*eps.  Tensors above 4 M elements are split
+    over host threads (the C function releases the GIL under ctypes)."""
     w = _c(w_bits, np.uint16).reshape(-1)
     out = np.zeros_like(w)
-    lib().eo_perturb_bf16(_p(w), w.size, seed, pair, tensor, sigma, int(sign), _p(out))
+    n = w.size
+    chunk = 1 << 22
+    if n <= chunk:
+        lib().eo_perturb_bf16(_p(w), n, seed, pair, tensor, sigma, int(sign), _p(out))
+        return out.reshape(np.shape(w_bits))
+    import concurrent.futures as cf
+
+    def run(s0):
+        m = min(chunk, n - s0)
+        lib().eo_perturb_bf16_at(w[s0:].ctypes.data_as(ctypes.c_void_p), m, s0, seed, pair, tensor, sigma, int(sign),
+                                 out[s0:].ctypes.data_as(ctypes.c_void_p))
+    with cf.ThreadPoolExecutor(os.cpu_count() or 1) as ex:
+        list(ex.map(run, range(0, n, chunk)))
     return out.reshape(np.shape(w_bits))
 
 

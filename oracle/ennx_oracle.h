@@ -84,6 +84,8 @@ void eo_packed_dequantize(const uint8_t* weights, const float* scales, const flo
 /* ---- population noise (builder-defined; no reference counterpart) ---- */
 void eo_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]);
 void eo_noise8(uint64_t seed, uint32_t pair, uint32_t tensor, uint64_t block, float out[8]);
+void eo_perturb_bf16_at(const uint16_t* w, size_t n, size_t start, uint64_t seed, uint32_t pair, uint32_t tensor,
+                        float sigma, int sign, uint16_t* out);
 void eo_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor,
                      float sigma, int sign, uint16_t* out);
 

@@ -37,9 +37,11 @@ def perturbed(bits: np.ndarray, seed: int, pair: int, tensor: int, sigma, sign: 
 
 
 def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pair: int, sign: int,
-                   return_rows: bool = False):
+                   return_rows: bool = False, hidden_at: dict | None = None):
     """Mean CE of one candidate.  W: {'embedding': bits, 'final_norm': bits,
-    'layers': [ {field: bits} ]} (bf16 bit patterns as uint16 arrays)."""
+    'layers': [ {field: bits} ]} (bf16 bit patterns as uint16 arrays).
+    hidden_at: {n: None} -> filled with the residual stream [T, H] after the
+    first n layers (float32 values of the bf16 activations)."""
     B, S1 = tokens.shape
     S = S1 - 1
     T = B * S
@@ -98,6 +100,8 @@ def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pa
             out = round_bf16((gemm(act, P["w_down"][e]) * (rs * gate[rows, ranks])[:, None]).astype(np.float32))
             np.add.at(y, rows, out.astype(np.float64))
         h = round_bf16(y.astype(np.float32))
+        if hidden_at is not None and (l + 1) in hidden_at:
+            hidden_at[l + 1] = h.copy()
     fnorm = perturbed(W["final_norm"], seed, pair, 1, sigma, sign)
     x = round_bf16(rmsnorm(h, fnorm, cfg.rms_eps))
     logits = gemm(x, emb)

@@ -1,0 +1,127 @@
+"""Parity at the benchmark's own shapes (configs[1..4]) against the CPU oracle.
+
+The device runs each operator at its full benchmark size; the CPU oracle
+(serial, float64 where it accumulates) checks slices of the result that it
+can finish in seconds: whole sequences of selected (batch, head) pairs, a
+sample of tokens, or one antithetic pair of the full model at a short
+sequence.  Tolerance: |x - ref| <= 1e-2 + 2e-2 |ref| for bf16 outputs (the
+BASELINE bound), routing indices bit-exact.
+"""
+import numpy as np
+import pytest
+
+import oracle as O
+from oracle import forward as OF
+
+pytestmark = [pytest.mark.gpu, pytest.mark.slow]
+torch = pytest.importorskip("torch")
+
+from ennx_b200 import ops  # noqa: E402
+from ennx_b200.model import HybridConfig, PopulationEvaluator, gate_up_interleave, init_weights  # noqa: E402
+
+RTOL, ATOL = 2e-2, 1e-2
+
+
+def close(got, ref, rtol=RTOL, atol=ATOL, what=""):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    err = np.abs(got - ref) - (atol + rtol * np.abs(ref))
+    assert err.max() <= 0, f"{what}: max excess {err.max():.3e} at {np.unravel_index(err.argmax(), err.shape)}"
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean():
+    yield
+    ops.device_status()  # a kernel that gave up on a bounded wait fails the test
+
+
+def _randn(shape, seed, std=1.0):
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device="cuda") * std).to(torch.bfloat16)
+
+
+def test_attention_configs1_full_size():
+    """B=8, S=2048, Hq=16, Hkv=4, RoPE 1e6; two (batch, q-head) slices, all 2048 queries."""
+    B, S, Hq, Hkv = 8, 2048, 16, 4
+    q, k, v = _randn((B, S, Hq, 128), 1), _randn((B, S, Hkv, 128), 2), _randn((B, S, Hkv, 128), 3)
+    q_host, k_host, v_host = q.float().cpu().numpy(), k.float().cpu().numpy(), v.float().cpu().numpy()
+    o = ops.gqa_attention(q, k, v, 1e6).float().cpu().numpy()
+    for b, h in ((0, 0), (5, 13)):
+        kv = h // (Hq // Hkv)
+        rq = O.round_bf16(O.rope(q_host[b:b + 1, :, h:h + 1], 1e6))
+        rk = O.round_bf16(O.rope(k_host[b:b + 1, :, kv:kv + 1], 1e6))
+        ref = O.gqa_attention(rq, rk, v_host[b:b + 1, :, kv:kv + 1])
+        close(o[b:b + 1, :, h:h + 1], ref, what=f"attention (b={b}, h={h})")
+
+
+@pytest.mark.parametrize("gscale", [64.0, 1.0])
+def test_kda_configs3_full_size(gscale):
+    """B=8, T=4096, H=16, chunk 64; two (batch, head) sequences over all
+    4096 steps and their final states against the serial recurrence.  gscale 1
+    decays by up to e^-5 per step (the clamp), gscale 64 by up to e^-5/64."""
+    B, T, H = 8, 4096, 16
+    g = torch.Generator(device="cuda").manual_seed(7)
+    q = torch.nn.functional.normalize(torch.randn(B, T, H, 128, generator=g, device="cuda"), dim=-1).bfloat16()
+    k = torch.nn.functional.normalize(torch.randn(B, T, H, 128, generator=g, device="cuda"), dim=-1).bfloat16()
+    v = torch.randn(B, T, H, 128, generator=g, device="cuda").bfloat16()
+    gl = -5.0 * torch.rand(B, T, H, 128, generator=g, device="cuda") / gscale
+    beta = torch.sigmoid(torch.randn(B, T, H, generator=g, device="cuda"))
+    state = torch.zeros(B, H, 128, 128, device="cuda")
+    o = ops.kda_chunked(q, k, v, gl, beta, state)
+    torch.cuda.synchronize()
+    for b, h in ((0, 0), (6, 11)):
+        sl = (slice(b, b + 1), slice(None), slice(h, h + 1))
+        ref, ref_state = O.kda_recurrence(q[sl].float().cpu().numpy(), k[sl].float().cpu().numpy(),
+                                          v[sl].float().cpu().numpy(), gl[sl].cpu().numpy(),
+                                          beta[b:b + 1, :, h:h + 1].cpu().numpy())
+        close(o[sl].float().cpu().numpy(), ref, what=f"kda output (b={b}, h={h})")
+        close(state[b:b + 1, h:h + 1].cpu().numpy(), ref_state, rtol=2e-2, atol=2e-2, what=f"kda state (b={b}, h={h})")
+
+
+def test_moe_configs2_full_size():
+    """16384 tokens, hidden 2048, 64 experts top-8, width 768; routing
+    indices of every token bit-exact, expert outputs of 512 sampled tokens."""
+    T, Hd, E, topk, I = 16384, 2048, 64, 8, 768
+    x = _randn((T, Hd), 11)
+    wr = _randn((E, Hd), 12, 0.02)
+    wg, wu = _randn((E, I, Hd), 13, 0.02), _randn((E, I, Hd), 14, 0.02)
+    wd = _randn((E, Hd, I), 15, 0.02)
+    y, idx, gate = ops.moe_layer(x, wr, gate_up_interleave(wg, wu), wd, topk, return_routing=True)
+    xb = x.cpu().view(torch.int16).numpy().view(np.uint16)
+    ridx, rgate = O.router_topk(O.router_logits(xb, wr.cpu().view(torch.int16).numpy().view(np.uint16)), topk)
+    assert np.array_equal(idx.cpu().numpy(), ridx)
+    sample = np.random.default_rng(0).choice(T, 512, replace=False)
+    ref = O.moe_experts(O.from_bf16_bits(xb[sample]), ridx[sample], rgate[sample], wg.float().cpu().numpy(),
+                        wu.float().cpu().numpy(), wd.float().cpu().numpy())
+    close(y.float().cpu().numpy()[sample], ref, what="moe expert outputs")
+
+
+def _bits(t):
+    return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def test_forward_configs4_full_model_one_pair():
+    """configs[4] model (24 layers, hidden 2048, 16/4 heads, 64 experts top-8,
+    vocab 151 936, gate rank 128) on one antithetic pair at batch 1 x seq 64:
+    the residual stream after layer 1 (KDA) and layer 4 (GQA), both signs,
+    within the bf16 bound, and both fitness values within 2e-3."""
+    cfg = HybridConfig()
+    w = init_weights(cfg, seed=1234)
+    B, S = 1, 64
+    tok = torch.randint(0, cfg.vocab, (B, S + 1), generator=torch.Generator().manual_seed(9), dtype=torch.int32)
+    ev = PopulationEvaluator(cfg, w, B, S)
+    seed, sigma, pair = 1001, 1e-3, 5
+    fit = ev(tok.cuda(), seed, sigma, pair, 1).cpu().numpy()
+    hid = {n: ev.hidden(tok.cuda(), seed, sigma, pair, n).float().cpu().numpy() for n in (1, 4)}
+    wb = {"embedding": _bits(w["embedding"]), "final_norm": _bits(w["final_norm"]),
+          "layers": [{k: _bits(v) for k, v in L.items()} for L in w["layers"]]}
+    del w
+    torch.cuda.empty_cache()
+    for s, sign in enumerate((+1, -1)):
+        at = {1: None, 4: None}
+        ref = OF.candidate_loss(cfg, wb, tok.numpy(), seed, sigma, pair, sign, hidden_at=at)
+        for n in (1, 4):
+            close(hid[n][s], at[n], what=f"hidden after {n} layers, sign {sign:+d}")
+        np.testing.assert_allclose(fit[s], ref, rtol=2e-3, atol=2e-3)
+    assert fit[0] != fit[1]
+

@@ -118,3 +118,68 @@ def test_kda_state_carries_across_calls():
         parts = [d[:, sl].contiguous() for d in dev]
         halves.append(ops.kda_chunked(*parts, state=state).float().cpu().numpy())
     close(np.concatenate(halves, 1), ref)
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean():
+    yield
+    ops.device_status()  # a kernel that gave up on a bounded wait fails the test
+
+
+def test_l2norm_heads_per_element():
+    """kda_normalize_qk (kda_moe.metal:510-534): every element within bf16 rounding."""
+    x = rnd((1000, 16 * 128), 30, 3.0)
+    x[7, 256:384] = 0  # an all-zero head: max(|x|, 1e-6) keeps it zero
+    y = ops.l2norm_heads(x.clone().cuda()).float().cpu().numpy()
+    ref = O.l2norm_heads(x.float().numpy().reshape(1000, 16, 128)).reshape(1000, -1)
+    close(y, ref, rtol=4e-3, atol=1e-6)
+    assert np.all(y[7, 256:384] == 0)
+
+
+def test_kda_gate_beta_per_element():
+    """kda_make_gate_beta_16k (kda_moe.metal:869-895): g including the -5 clamp, beta."""
+    T, heads = 777, 16
+    raw = rnd((T, heads * 128), 31, 4.0)
+    rbeta = rnd((T, heads), 32, 2.0)
+    decay = rnd((heads,), 33, 0.7)
+    tb = rnd((heads * 128,), 34, 0.5)
+    g, b = ops.kda_gate_beta(raw.cuda(), rbeta.cuda(), decay.cuda(), tb.cuda())
+    rg, rb = O.kda_gate_beta(raw.float().numpy(), rbeta.float().numpy(), decay.float().numpy(), tb.float().numpy(),
+                             heads, 128)
+    g, b = g.cpu().numpy(), b.cpu().numpy()
+    close(g, rg, rtol=1e-4, atol=1e-6)
+    close(b, rb, rtol=1e-5, atol=1e-6)
+    assert (rg == -5.0).any() and np.array_equal(g == -5.0, rg == -5.0)
+
+
+def test_kda_postprocess_per_element():
+    """kda_postprocess_16k (kda_moe.metal:898-921): per-head RMSNorm x norm x sigmoid(gate)."""
+    T, heads = 500, 16
+    o, gate, norm = rnd((T, heads * 128), 35), rnd((T, heads * 128), 36, 2.0), rnd((128,), 37)
+    y = ops.kda_postprocess(o.cuda(), gate.cuda(), norm.cuda(), 1e-6).float().cpu().numpy()
+    ref = O.kda_postprocess(o.float().numpy().reshape(T, heads, 128), gate.float().numpy(), norm.float().numpy(),
+                            1e-6).reshape(T, -1)
+    close(y, ref, rtol=5e-3, atol=1e-5)
+
+
+@pytest.mark.parametrize("B,T,heads", [(2, 200, 2), (1, 1000, 4)])
+def test_kda_gated_matches_oracle(B, T, heads):
+    """The forward's fused KDA (q/k L2 norm and gate/beta formed inside the
+    chunk preparation) against l2norm_heads + kda_gate_beta + the serial
+    recurrence of the oracle."""
+    hw = heads * 128
+    rows = B * T
+    qkv = rnd((rows, 3 * hw + 64), 40)
+    raw = rnd((rows, hw), 41, 1.5)
+    rbeta = rnd((rows, 8), 42)
+    decay, tb = rnd((heads,), 43, 0.5), rnd((hw,), 44, 0.5)
+    o = ops.kda_gated(qkv.cuda(), raw.cuda(), rbeta.cuda(), decay.cuda(), tb.cuda(), B, T).float().cpu().numpy()
+    qf = qkv.float().numpy()
+    q = O.round_bf16(O.l2norm_heads(qf[:, :hw].reshape(rows, heads, 128)))
+    k = O.round_bf16(O.l2norm_heads(qf[:, hw:2 * hw].reshape(rows, heads, 128)))
+    v = qf[:, 2 * hw:3 * hw]
+    g, beta = O.kda_gate_beta(raw.float().numpy(), rbeta.float().numpy()[:, :heads].copy(), decay.float().numpy(),
+                              tb.float().numpy(), heads, 128)
+    ref, _ = O.kda_recurrence(q.reshape(B, T, heads, 128), k.reshape(B, T, heads, 128), v.reshape(B, T, heads, 128),
+                              g.reshape(B, T, heads, 128), beta.reshape(B, T, heads))
+    close(o, ref.reshape(rows, hw))

@@ -1,16 +1,27 @@
-"""The allocation-free KDA entry point against the regular one.
+"""The allocation-free KDA entry point.
 
 ennx_b200_kda_chunked_noalloc serves callers that cannot allocate device
-memory (inside a CUDA graph capture, under a host that owns all device memory,
-in latency-critical loops): it takes its scratch from a static 32 MiB device
-array instead of a caller workspace.  This file is collected last so that a
-run stopping at the first failure has already run every other test; it also
-passes on its own in a fresh process.
+memory (code inside a CUDA graph that is being captured, hosts that own every
+byte of device memory through their own pool, latency-critical loops where an
+allocation is an unbounded stall): it takes its scratch from a static 32 MiB
+device array and reports device-side timeouts through a static status word.
+
+Checked here: the result against the regular entry point on two calls in a
+row, against the serial CPU recurrence, and -- in a fresh process whose FIRST
+library call is this entry point -- that free device memory does not change
+across that call.  This file is collected last so that a run stopping at the
+first failure has already run every other test; it also passes on its own.
 """
 import ctypes
+import os
+import subprocess
+import sys
+import textwrap
 
 import numpy as np
 import pytest
+
+import oracle as O
 
 pytestmark = pytest.mark.gpu
 torch = pytest.importorskip("torch")
@@ -18,6 +29,7 @@ torch = pytest.importorskip("torch")
 from ennx_b200 import _abi  # noqa: E402
 
 RTOL, ATOL = 2e-2, 1e-2  # the chunked-KDA tolerance used by the other KDA tests
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
 def _inputs(B, T, H, seed):
@@ -64,7 +76,7 @@ def test_noalloc_matches_regular_on_two_calls_in_a_row():
         s_new = s_ref.clone()
         ref = _regular(q, k, v, gl, beta, s_ref)
         got = _noalloc(q, k, v, gl, beta, s_new)
-        torch.cuda.synchronize()
+        _abi.check(_abi.lib().ennx_b200_device_status(_stream()), "device_status")
         a, b = got.float().cpu().numpy(), ref.float().cpu().numpy()
         assert np.all(np.abs(a - b) <= ATOL + RTOL * np.abs(b)), f"call {call}: outputs differ"
         sa, sb = s_new.cpu().numpy(), s_ref.cpu().numpy()
@@ -79,3 +91,77 @@ def test_noalloc_rejects_problems_beyond_the_static_scratch():
                                                   _stream())
     assert st == _abi.INVALID_ARGUMENT
     assert b"static scratch" in _abi.lib().ennx_b200_last_error()
+
+
+# A fresh process (no torch: plain cudart through ctypes) whose first library
+# call is the allocation-free entry point.  Modules load eagerly at context
+# creation, so the static array exists before the measurement; free device
+# memory is then read before and after the first and a second call, and the
+# output is compared with the serial CPU recurrence.
+_FRESH = textwrap.dedent(r"""
+    import ctypes, sys
+    import numpy as np
+    sys.path.insert(0, sys.argv[1])
+    import oracle as O
+    from ennx_b200 import _abi
+    lib = _abi.lib()
+    rt = None
+    for line in open("/proc/self/maps"):
+        if "libcudart.so" in line:
+            rt = ctypes.CDLL(line.split()[-1])
+            break
+    assert rt is not None, "libcudart is not loaded by the library"
+    def ok(e, what):
+        assert e == 0, f"{what}: cuda error {e}"
+    ok(rt.cudaSetDevice(0), "cudaSetDevice")
+    ok(rt.cudaFree(None), "cudaFree(0)")
+    B, T, H = 1, 200, 2
+    rng = np.random.default_rng(7)
+    q = O.round_bf16(O.l2norm_heads(rng.standard_normal((B, T, H, 128)).astype(np.float32)))
+    k = O.round_bf16(O.l2norm_heads(rng.standard_normal((B, T, H, 128)).astype(np.float32)))
+    v = O.round_bf16(rng.standard_normal((B, T, H, 128)).astype(np.float32))
+    g = (rng.uniform(-5.0, 0.0, (B, T, H, 128)) / 64.0).astype(np.float32)
+    beta = (1.0 / (1.0 + np.exp(-rng.standard_normal((B, T, H))))).astype(np.float32)
+    host = {"q": O.to_bf16_bits(q), "k": O.to_bf16_bits(k), "v": O.to_bf16_bits(v), "g": g, "beta": beta,
+            "o": np.zeros((B, T, H, 128), np.uint16), "state": np.zeros((B, H, 128, 128), np.float32)}
+    dev = {}
+    for name, a in host.items():
+        p = ctypes.c_void_p()
+        ok(rt.cudaMalloc(ctypes.byref(p), ctypes.c_size_t(a.nbytes)), "cudaMalloc (test inputs)")
+        ok(rt.cudaMemcpy(p, a.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(a.nbytes), 1), "h2d")
+        dev[name] = p
+    ok(rt.cudaDeviceSynchronize(), "sync")
+    def free_bytes():
+        f, t = ctypes.c_size_t(), ctypes.c_size_t()
+        ok(rt.cudaMemGetInfo(ctypes.byref(f), ctypes.byref(t)), "cudaMemGetInfo")
+        return f.value
+    outs = []
+    for call in range(2):
+        before = free_bytes()
+        st = lib.ennx_b200_kda_chunked_noalloc(dev["q"], dev["k"], dev["v"], dev["g"], dev["beta"], dev["state"],
+                                               dev["o"], B, T, H, None)
+        assert st == 0, lib.ennx_b200_last_error()
+        ok(rt.cudaDeviceSynchronize(), "sync")
+        after = free_bytes()
+        assert after == before, f"call {call}: free device memory changed by {before - after} bytes"
+        o = np.zeros((B, T, H, 128), np.uint16)
+        ok(rt.cudaMemcpy(o.ctypes.data_as(ctypes.c_void_p), dev["o"], ctypes.c_size_t(o.nbytes), 2), "d2h")
+        outs.append(O.from_bf16_bits(o))
+        if call == 0:  # second call: zero initial state again
+            z = np.zeros((B, H, 128, 128), np.float32)
+            ok(rt.cudaMemcpy(dev["state"], z.ctypes.data_as(ctypes.c_void_p), ctypes.c_size_t(z.nbytes), 1), "h2d")
+    st = lib.ennx_b200_device_status(None)
+    assert st == 0, lib.ennx_b200_last_error()
+    ref, _ = O.kda_recurrence(q, k, v, g, beta)
+    for call, got in enumerate(outs):
+        excess = np.abs(got - ref) - (%(atol)r + %(rtol)r * np.abs(ref))
+        assert excess.max() <= 0, f"call {call}: vs serial recurrence, max excess {excess.max()}"
+    print("fresh-process no-alloc ok")
+""") % {"atol": ATOL, "rtol": RTOL}
+
+
+def test_noalloc_first_call_in_a_fresh_process_allocates_nothing():
+    env = dict(os.environ, CUDA_MODULE_LOADING="EAGER")
+    r = subprocess.run([sys.executable, "-c", _FRESH, ROOT], capture_output=True, text=True, env=env, timeout=600)
+    assert r.returncode == 0, f"fresh process failed:\n{r.stdout}\n{r.stderr}"
+    assert "fresh-process no-alloc ok" in r.stdout

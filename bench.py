@@ -370,6 +370,41 @@ def run_op(args):
         c = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
         fn = lambda: ops.gemm(a, b, out=c)  # noqa: E731
         flops, nbytes, unit_name = 2.0 * M * N * K, 2.0 * (M * K + N * K + M * N), "gemm 2048^3"
+    elif args.op in ("gemm_pb", "gemm_pb_moe"):
+        # One antithetic pair's projection as the forward runs it: 2 x 4096
+        # rows against W + e and W - e (dense, N = K = 2048), or the expert
+        # gate/up GEMM (2 x 32768 routed rows over 64 experts, N = 1536,
+        # K = 2048).  --plain times the plain GEMM on stored W + e / W - e.
+        moe = args.op == "gemm_pb_moe"
+        K = 2048
+        if moe:
+            P, N = 64, 1536
+            rows = torch.multinomial(torch.ones(P), 2 * 4096 * 8, replacement=True, generator=torch.Generator()
+                                     .manual_seed(1))
+            counts = torch.cat([torch.bincount(rows[:32768], minlength=P), torch.bincount(rows[32768:], minlength=P)])
+            offs = torch.cat([torch.zeros(1, dtype=torch.int64), counts.cumsum(0)]).to(torch.int32).cuda()
+            M = int(offs[-1])
+        else:
+            P, N = 1, 2048
+            M = int(os.environ.get("ENNX_B200_BENCH_ROWS", "8192"))
+            K = int(os.environ.get("ENNX_B200_BENCH_K", "2048"))
+            offs = None
+        a = rn(M, K)
+        w, e = rn(P * N, K, std=0.02), rn(P * N, K, std=1e-3)
+        c = torch.empty(M, N // 2 if moe else N, device="cuda", dtype=torch.bfloat16)
+        epi = _abi.EPI_SWIGLU if moe else _abi.EPI_BF16
+        if args.plain:
+            wpm = torch.cat([(w.float() + e.float()).bfloat16(), (w.float() - e.float()).bfloat16()])
+            fn = lambda: ops.gemm(a, wpm, out=c, groups=2 * P, b_group_rows=N, n=N, group_offsets=offs,  # noqa: E731
+                                  epilogue=epi)
+        else:
+            fn = lambda: ops.gemm_perturbed(a, w, e, out=c, pairs=P, b_group_rows=N, n=N,  # noqa: E731
+                                            group_offsets=offs, epilogue=epi)
+        flops = 2.0 * M * N * K
+        nbytes = 2.0 * (M * K + 2 * P * N * K + M * c.shape[1])
+        unit_name = ("expert gate/up 65536 rows x 64 experts, N 1536, K 2048" if moe else
+                     "pair projection 2 x 4096 rows, N = K = 2048") + (" (plain, stored W+-e)" if args.plain else
+                                                                         " (perturbed operand path)")
     elif args.op == "attention":
         B, S, Hq, Hkv = 8, 2048, 16, 4
         q, k, v = rn(B, S, Hq, 128), rn(B, S, Hkv, 128), rn(B, S, Hkv, 128)
@@ -590,13 +625,15 @@ def run_decode(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["forward", "gemm", "attention", "moe", "kda", "search", "decode"],
+    ap.add_argument("--op", choices=["forward", "gemm", "gemm_pb", "gemm_pb_moe", "attention", "moe", "kda", "search",
+                                     "decode"],
                     default="forward")
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--plain", action="store_true", help="gemm_pb ops: time the plain GEMM on stored W +/- e")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)

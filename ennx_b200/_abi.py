@@ -162,6 +162,7 @@ SIGNATURES = {
     "ennx_b200_dense_linear_f32": (_I32, [_P, _SZ, _P, _SZ, _P, DenseView, DenseView, _P, _SZ, _P, _P]),
     "ennx_b200_perturb_bf16": (_I32, [_P, _SZ, _U64, _U32, _U32, _F32, _P, _P, _P]),
     "ennx_b200_gemm_bf16": (_I32, [_P, _P, _P, _P, _P]),
+    "ennx_b200_gemm_bf16_perturbed": (_I32, [_P, _P, _P, _P, _P, _P]),
     "ennx_b200_rmsnorm_bf16": (_I32, [_P, _P, ctypes.c_int64, _I32, _F32, _P, _P]),
     "ennx_b200_moe_route": (_I32, [_P, _P, ctypes.c_int64, _I32, _I32, _I32, _P, _P, _P, _P]),
     "ennx_b200_moe_workspace_size": (_SZ, [ctypes.c_int64, _I32, _I32, _I32, _I32]),
@@ -173,7 +174,7 @@ SIGNATURES = {
     "ennx_b200_kda_chunked_noalloc": (_I32, [_P, _P, _P, _P, _P, _P, _P, _I32, _I32, _I32, _P]),
     "ennx_b200_population_workspace_size": (_SZ, [_P, _I32, _I32]),
     "ennx_b200_population_forward": (_I32, [_P, _P, _U64, _F32, _I32, _I32, _P, _I32, _I32, _P, _P, _SZ, _P]),
-    "ennx_b200_population_hidden": (_I32, [_P, _P, _U64, _F32, _I32, _I32, _P, _I32, _I32, _P, _P, _SZ, _P]),
+    "ennx_b200_population_hidden": (_I32, [_P, _P, _U64, _F32, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
     "ennx_b200_l2norm_heads_bf16": (_I32, [_P, ctypes.c_int64, _I32, ctypes.c_int64, _P]),
     "ennx_b200_kda_gate_beta": (_I32, [_P, ctypes.c_int64, _P, ctypes.c_int64, _P, _P, ctypes.c_int64, _I32, _P, _P,
                                        _P]),

@@ -79,6 +79,26 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
+// bf16x2 arithmetic with one RNE rounding of the exact result, and a
+// streaming 16-byte global load that does not allocate in L1.
+__device__ __forceinline__ uint4 ldg_stream_v4(const uint16_t* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.b32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ uint32_t bf16x2_add(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("add.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+__device__ __forceinline__ uint32_t bf16x2_sub(uint32_t a, uint32_t b) {
+  uint32_t d;
+  asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+  return d;
+}
+
 // splitmix64 finaliser of the seeded sign (rust/crates/ennx/src/dense.rs:428-433).
 __host__ __device__ __forceinline__ uint64_t mix64(uint64_t x) {
   uint64_t v = x + 0x9e3779b97f4a7c15ull;
@@ -331,6 +351,12 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr) {
          ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
 }
 
+// K-major, 64-byte swizzle: rows of 64 B (32 bf16), 8-row groups 512 B apart.
+__device__ __forceinline__ uint64_t smem_desc_sw64(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(512u >> 4) << 32) |
+         ((uint64_t)1u << 46) | ((uint64_t)4u << 61);
+}
+
 // MN-major operand (rows of 64 MN-contiguous bf16 = 128 B, 128-byte swizzle):
 // SBO = 1024 B between groups of 8 K-rows, LBO = byte distance between
 // consecutive 64-wide MN blocks.
@@ -378,5 +404,8 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
 // ---------------------------------------------------------------------------
 int32_t make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                           uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer, bool swizzle128);
+// swizzle_bytes: 0 (none), 32, 64 or 128
+int32_t make_tmap_2d_bf16_sw(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                             uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer, int swizzle_bytes);
 
 }  // namespace ennx

@@ -170,8 +170,11 @@ __global__ void dense_linear_kernel(const float* __restrict__ x, const float* __
 }
 
 // Population noise: each thread owns 8 consecutive elements (one Philox
-// block) per step, 16-byte loads and stores; W +/- sigma*eps with two fp32
-// roundings, RNE.  Blocks of 128 threads cover a fixed 4096-element span and
+// block) per step, 16-byte loads and stores.  The noise step is
+// e = bf16(sigma * z) (RNE) and the perturbed weights are W +/- e, each
+// rounded once (RNE of the exact sum) -- the same values the perturbed GEMM
+// forms in its operand path from W and e.  With w == nullptr only e is
+// written (to `plus`): the noise operand of that GEMM.  Blocks of 128 threads cover a fixed 4096-element span and
 // retire quickly, so the block scheduler can interleave them with the compute
 // stream's kernels on the same SMs (this kernel runs on a low-priority
 // stream); the batched form covers every tensor of a layer in one launch.
@@ -193,7 +196,7 @@ __device__ __forceinline__ void perturb_block(const uint16_t* __restrict__ w, ui
 #pragma unroll
   for (int it = 0; it < kPerturbGroupsPerThread; ++it) {
     const uint64_t g = g0 + (uint64_t)it * kPerturbThreads;
-    raw[it] = g < full ? __ldcs(reinterpret_cast<const uint4*>(w) + g) : make_uint4(0, 0, 0, 0);
+    raw[it] = (w && g < full) ? __ldcs(reinterpret_cast<const uint4*>(w) + g) : make_uint4(0, 0, 0, 0);
   }
 #pragma unroll
   for (int it = 0; it < kPerturbGroupsPerThread; ++it) {
@@ -203,24 +206,32 @@ __device__ __forceinline__ void perturb_block(const uint16_t* __restrict__ w, ui
     float z[8];
     noise8(seed, pair, tensor, g, z);
     if (g < full) {
+      uint32_t ev[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) ev[j] = pack_bf16x2(__fmul_rn(sigma, z[2 * j]), __fmul_rn(sigma, z[2 * j + 1]));
+      const uint64_t d = cols ? (e0 / cols) * dld + e0 % cols : e0;
+      if (!w) {
+        __stcs(reinterpret_cast<uint4*>(plus + d), make_uint4(ev[0], ev[1], ev[2], ev[3]));
+        continue;
+      }
       const uint32_t in[4] = {raw[it].x, raw[it].y, raw[it].z, raw[it].w};
       uint32_t p[4], m[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float a = bf16_to_f32((uint16_t)(in[j] & 0xffffu));
-        const float b = bf16_to_f32((uint16_t)(in[j] >> 16));
-        const float sa = __fmul_rn(sigma, z[2 * j]), sb = __fmul_rn(sigma, z[2 * j + 1]);
-        p[j] = pack_bf16x2(__fadd_rn(a, sa), __fadd_rn(b, sb));
-        m[j] = pack_bf16x2(__fsub_rn(a, sa), __fsub_rn(b, sb));
+        p[j] = bf16x2_add(in[j], ev[j]);
+        m[j] = bf16x2_sub(in[j], ev[j]);
       }
-      const uint64_t d = cols ? (e0 / cols) * dld + e0 % cols : e0;
       __stcs(reinterpret_cast<uint4*>(plus + d), make_uint4(p[0], p[1], p[2], p[3]));
       if (minus) __stcs(reinterpret_cast<uint4*>(minus + d), make_uint4(m[0], m[1], m[2], m[3]));
     } else {
       for (uint64_t e = e0; e < n; ++e) {
-        const float a = bf16_to_f32(w[e]);
-        const float sg = __fmul_rn(sigma, z[e - e0]);
+        const uint16_t step = f32_to_bf16_rne(__fmul_rn(sigma, z[e - e0]));
         const uint64_t d = cols ? (e / cols) * dld + e % cols : e;
+        if (!w) {
+          plus[d] = step;
+          continue;
+        }
+        const float a = bf16_to_f32(w[e]), sg = bf16_to_f32(step);
         plus[d] = f32_to_bf16_rne(__fadd_rn(a, sg));
         if (minus) minus[d] = f32_to_bf16_rne(__fsub_rn(a, sg));
       }
@@ -322,7 +333,8 @@ using namespace ennx;
 namespace ennx {
 int32_t launch_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor, float sigma,
                             uint16_t* plus, uint16_t* minus, uint32_t cols, uint64_t dld, cudaStream_t s) {
-  if (!w || !plus || n == 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16 needs input and output");
+  if (!plus || n == 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16 needs an output");
+  if (!w && minus) return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16: the noise step has one output");
   if (((uintptr_t)w | (uintptr_t)plus | (uintptr_t)minus) & 15u)
     return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb_bf16 buffers must be 16-byte aligned");
   if (!isfinite(sigma)) return set_error(ENNX_B200_INVALID_ARGUMENT, "sigma must be finite");
@@ -347,7 +359,7 @@ int32_t launch_perturb_batch(const PerturbBatch& batch, cudaStream_t s) {
   uint64_t blocks = 0;
   for (int j = 0; j < b.count; ++j) {
     const PerturbJob& jb = b.job[j];
-    if (!jb.w || !jb.plus || jb.n == 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb batch: empty job %d", j);
+    if (!jb.plus || jb.n == 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb batch: empty job %d", j);
     if (((uintptr_t)jb.w | (uintptr_t)jb.plus | (uintptr_t)jb.minus) & 15u)
       return set_error(ENNX_B200_INVALID_ARGUMENT, "perturb batch: buffers must be 16-byte aligned");
     if (jb.cols && (jb.cols % 8 || jb.n % jb.cols || jb.dld % 8 || jb.dld < jb.cols))

@@ -12,10 +12,14 @@
 // generalised to prefill over whole sequences, GQA layers every
 // `attn_period` layers, and a fused LM-head cross-entropy at the end.
 //
-// Work is organised per antithetic pair: the pair's W+sigma*eps and
-// W-sigma*eps copies of one layer are generated into a scratch area (HBM
-// streaming kernel), then both candidates' tokens run through the layer as
-// one batch; every GEMM is a 2-group tcgen05 launch (MoE: 2*E groups).
+// Work is organised per antithetic pair: the pair's noise step e =
+// bf16(sigma*eps) of one layer's matrices is generated into a scratch area
+// (streaming kernel on a second stream), then both candidates' tokens run
+// through the layer as one batch; every GEMM is one perturbed tcgen05 launch
+// that forms W + e and W - e inside its operand path (MoE: E expert pairs),
+// so no perturbed weight matrix is ever stored.  Small per-layer vectors
+// (norm weights, decay, time bias) and the router matrix are written as
+// W +/- e copies.
 #include <string.h>
 
 #include <algorithm>
@@ -84,7 +88,8 @@ void carve_moe(Carver& c, long long tokens, int hidden, int experts, int top_k, 
 // expert block 0 of the weights, the rest block 1 (block stride = experts).
 int32_t run_moe(const uint16_t* x, const uint16_t* wr0, const uint16_t* wr1, const uint16_t* wgu, const uint16_t* wd,
                 long long tokens, long long split, int sets, int hidden, int experts, int top_k, int width,
-                const uint16_t* residual, uint16_t* out, MoeBuffers& m, cudaStream_t s, float residual_scale = 1.0f) {
+                const uint16_t* residual, uint16_t* out, MoeBuffers& m, cudaStream_t s, float residual_scale = 1.0f,
+                const uint16_t* gu_noise = nullptr, const uint16_t* down_noise = nullptr) {
   if (width % 128) return set_error(ENNX_B200_UNSUPPORTED, "moe: expert width %d must be a multiple of 128", width);
   long long rows = tokens * top_k;
   {
@@ -107,7 +112,9 @@ int32_t run_moe(const uint16_t* x, const uint16_t* wr0, const uint16_t* wr1, con
   {
     ProfScope ps("gemm", s, 2.0 * rows * 2 * width * hidden,
                  2.0 * (rows * hidden + (double)sets * experts * 2 * width * hidden + rows * width));
-    ENNX_TRY(gemm_bf16(&p, m.xperm, wgu, m.act, s));
+    // sets == 2 with noise: expert e of set 0 uses W + e, of set 1 W - e
+    if (gu_noise) ENNX_TRY(gemm_bf16_perturbed(&p, m.xperm, wgu, gu_noise, m.act, s));
+    else ENNX_TRY(gemm_bf16(&p, m.xperm, wgu, m.act, s));
   }
   memset(&p, 0, sizeof(p));
   p.m = (int)rows; p.n = hidden; p.k = width;
@@ -117,7 +124,8 @@ int32_t run_moe(const uint16_t* x, const uint16_t* wr0, const uint16_t* wr1, con
   {
     ProfScope ps("gemm", s, 2.0 * rows * hidden * width,
                  2.0 * (rows * width + (double)sets * experts * hidden * width + rows * hidden));
-    ENNX_TRY(gemm_bf16(&p, m.act, wd, m.yperm, s));
+    if (down_noise) ENNX_TRY(gemm_bf16_perturbed(&p, m.act, wd, down_noise, m.yperm, s));
+    else ENNX_TRY(gemm_bf16(&p, m.act, wd, m.yperm, s));
   }
   {
     ProfScope ps("moe_combine", s, 0, 2.0 * (rows * hidden + 2.0 * tokens * hidden));
@@ -181,15 +189,27 @@ long long field_elems(const Shapes& sh, int f) {
     default: return sh.rows[f] * sh.cols[f];
   }
 }
+// Matrices consumed by the perturbed GEMM: only their noise step e is
+// generated (one copy); the other fields get materialised W + e and W - e.
+bool gemm_field(int f) {
+  return f == F_QKV || f == F_CTL || f == F_FORGET || f == F_OGATE || f == F_WO || f == F_GATE_UP || f == F_DOWN;
+}
+int kda_ordinal(const ennx_b200_model_config& c, int l) {  // index of KDA layer l among the KDA layers
+  int n = 0;
+  for (int i = 0; i < l; ++i) n += is_gqa(c, i) ? 0 : 1;
+  return n;
+}
 // leading dimension of the fused QKV(+control) GEMM output
 long long qkv_ld(const Shapes& sh) { return (sh.rows[F_QKV] + sh.rows[F_CTL] + 7) / 8 * 8; }
 
 struct Work {
   const int* tokens;       // caller's [batch, seq + 1] token ids
-  uint16_t *emb_scr[2];    // two slots of [2][V*H] (plus, minus)
-  uint16_t *fnorm_scr[2];  // two slots of [2][H]
-  uint16_t *layer_scr[2];  // two slots of per-field [2][n] areas
-  size_t field_off[F_COUNT];  // element offsets into layer_scr (for the plus copy; minus follows)
+  uint16_t *emb_scr[2];    // two slots of the embedding's noise step [V*H]
+  uint16_t *fnorm_scr[2];  // two slots of [2][H] (final norm plus, minus)
+  uint16_t *layer_scr[2];  // two slots of per-field areas: [n] noise (GEMM fields) or [2][n] (plus, minus)
+  size_t field_off[F_COUNT];  // element offsets into layer_scr
+  uint16_t* base_fused;    // per KDA layer: [W_qkv; W_ctl] then [[W_f, 0], [0, W_o]] (base weights)
+  size_t base_stride;      // elements per KDA layer in base_fused
   uint16_t *hidden, *xn, *qkv, *fg, *o, *post;
   float *gate, *beta;
   int *inp, *tgt;
@@ -223,7 +243,7 @@ void carve_work(const ennx_b200_model_config& c, int batch, int seq, uint8_t* ba
   Carver cv{base, 0, 0, base == nullptr};
   const long long Tc = (long long)batch * seq, T = 2 * Tc, H = c.hidden;
   for (int k = 0; k < 2; ++k) {
-    w.emb_scr[k] = cv.take<uint16_t>(2 * align_elems((long long)c.vocab * H));
+    w.emb_scr[k] = cv.take<uint16_t>(align_elems((long long)c.vocab * H));
     w.fnorm_scr[k] = cv.take<uint16_t>(2 * align_elems(H));
   }
   size_t per_field_max[F_COUNT] = {0};
@@ -235,8 +255,15 @@ void carve_work(const ennx_b200_model_config& c, int batch, int seq, uint8_t* ba
     }
   }
   size_t off = 0;
-  for (int f = 0; f < F_COUNT; ++f) { w.field_off[f] = off; off += 2 * per_field_max[f]; }
+  for (int f = 0; f < F_COUNT; ++f) { w.field_off[f] = off; off += (gemm_field(f) ? 1 : 2) * per_field_max[f]; }
   for (int k = 0; k < 2; ++k) w.layer_scr[k] = cv.take<uint16_t>(off);
+  {
+    const Shapes sk = layer_shapes(c, false);
+    w.base_stride = align_elems(field_elems(sk, F_QKV)) + align_elems(field_elems(sk, F_FORGET));
+    long long kda_layers = 0;
+    for (int l = 0; l < c.layers; ++l) kda_layers += is_gqa(c, l) ? 0 : 1;
+    w.base_fused = cv.take<uint16_t>(w.base_stride * kda_layers);
+  }
   const long long qkv_cols = std::max(qkv_ld(layer_shapes(c, false)), qkv_ld(layer_shapes(c, true)));
   const long long heads_max = std::max(c.kda_heads, c.q_heads);
   w.hidden = cv.take<uint16_t>(T * H);
@@ -277,8 +304,11 @@ const uint16_t* field_ptr(const ennx_b200_layer_weights& L, int f) {
   }
 }
 
-int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* b, long long n, long long k, void* c, long long ldc,
-              long long rows, const uint16_t* residual, cudaStream_t s, double useful_flops = 0.0, float alpha = 1.0f) {
+// One antithetic pair's projection: rows [0, rows/2) against W + e, the rest
+// against W - e (W and e [n, k], row stride k), bf16 out (+ residual).
+int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* w, const uint16_t* e, long long n, long long k,
+              void* c, long long ldc, long long rows, const uint16_t* residual, cudaStream_t s,
+              double useful_flops = 0.0, float alpha = 1.0f) {
   ennx_b200_gemm_params p;
   memset(&p, 0, sizeof(p));
   p.m = (int)rows; p.n = (int)n; p.k = (int)k;
@@ -288,7 +318,7 @@ int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* b, long long n, 
   p.residual = residual; p.ldr = ldc;
   ProfScope ps("gemm", s, useful_flops > 0.0 ? useful_flops : 2.0 * rows * n * k,
                2.0 * (rows * k + 2.0 * n * k + rows * n * (residual ? 2 : 1)));
-  return gemm_bf16(&p, a, b, c, s);
+  return gemm_bf16_perturbed(&p, a, w, e, c, s);
 }
 
 // Per-device streams of the pipelined population forward: `compute` runs the
@@ -329,20 +359,13 @@ LayerPtrs layer_ptrs(const ennx_b200_model_config& c, int l, const Work& w, int 
     long long n = sh.rows[f] * sh.cols[f];
     lp.P[f] = lp.M[f] = nullptr;
     if (n == 0 || f == F_CTL || f == F_OGATE) continue;
-    lp.P[f] = w.layer_scr[slot] + w.field_off[f];
-    // minus copy directly after plus (GEMM operands: n % 64 == 0, so the
-    // B row-block stride between the two signs is exactly `rows`)
-    const long long fn = field_elems(sh, f);
-    lp.M[f] = lp.P[f] + (fn % 8 == 0 ? (size_t)fn : align_elems(fn));
+    lp.P[f] = w.layer_scr[slot] + w.field_off[f];  // GEMM fields: the noise step e
+    if (!gemm_field(f)) lp.M[f] = lp.P[f] + align_elems(field_elems(sh, f));  // minus copy after plus
   }
-  if (sh.rows[F_CTL]) {  // control rows follow the QKV rows of each sign
-    lp.P[F_CTL] = lp.P[F_QKV] + sh.rows[F_QKV] * sh.cols[F_QKV];
-    lp.M[F_CTL] = lp.M[F_QKV] + sh.rows[F_QKV] * sh.cols[F_QKV];
-  }
+  if (sh.rows[F_CTL]) lp.P[F_CTL] = lp.P[F_QKV] + sh.rows[F_QKV] * sh.cols[F_QKV];  // control rows follow QKV
   if (sh.rows[F_OGATE]) {  // output-gate block: rows [hw, 2hw), columns [r, 2r)
     const long long hw = sh.rows[F_FORGET], r = sh.cols[F_FORGET];
     lp.P[F_OGATE] = lp.P[F_FORGET] + hw * 2 * r + r;
-    lp.M[F_OGATE] = lp.M[F_FORGET] + hw * 2 * r + r;
   }
   return lp;
 }
@@ -363,7 +386,8 @@ int32_t add_layer_jobs(const ennx_b200_model_config& c, const ennx_b200_model_we
     // forget / output-gate weights land as blocks of the block-diagonal matrix
     const bool blk = f == F_FORGET || f == F_OGATE;
     PerturbJob& j = batch.job[batch.count++];
-    j.w = src; j.plus = lp.P[f]; j.minus = lp.M[f]; j.n = (uint64_t)n;
+    j.w = gemm_field(f) ? nullptr : src;  // GEMM fields: noise step only
+    j.plus = lp.P[f]; j.minus = lp.M[f]; j.n = (uint64_t)n;
     j.tensor = 16u + 16u * (uint32_t)l + (uint32_t)f;
     j.cols = blk ? (uint32_t)sh.cols[f] : 0u;
     j.dld = blk ? 2 * (uint64_t)sh.cols[f] : 0u;
@@ -371,9 +395,11 @@ int32_t add_layer_jobs(const ennx_b200_model_config& c, const ennx_b200_model_we
   return ENNX_B200_OK;
 }
 
-// compute stream: one decoder layer for both candidates of a pair (T rows)
-int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& lp, int batch, int seq, Work& w,
-                      cudaStream_t s) {
+// compute stream: one decoder layer for both candidates of a pair (T rows).
+// L: the caller's base weights of the layer; lp: the pair's noise steps and
+// small perturbed vectors.
+int32_t compute_layer(const ennx_b200_model_config& c, int l, const ennx_b200_layer_weights& L, const LayerPtrs& lp,
+                      int batch, int seq, Work& w, cudaStream_t s) {
   const long long Tc = (long long)batch * seq, T = 2 * Tc, H = c.hidden;
   const bool gqa = is_gqa(c, l);
   Shapes sh = layer_shapes(c, gqa);
@@ -382,7 +408,8 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
   ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_ATTN_NORM], M[F_ATTN_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
   // one GEMM: [q | k | v] (and on KDA layers the control projection after them)
   const long long qkv_cols = qkv_ld(sh);
-  ENNX_TRY(gemm2(w.xn, H, P[F_QKV], sh.rows[F_QKV] + sh.rows[F_CTL], H, w.qkv, qkv_cols, T, nullptr, s));
+  const uint16_t* base_qkv = gqa ? L.w_qkv : w.base_fused + (size_t)kda_ordinal(c, l) * w.base_stride;
+  ENNX_TRY(gemm2(w.xn, H, base_qkv, P[F_QKV], sh.rows[F_QKV] + sh.rows[F_CTL], H, w.qkv, qkv_cols, T, nullptr, s));
   if (gqa) {
     const long long kd = (long long)c.q_heads * HD, vd = kd + (long long)c.kv_heads * HD;
     ENNX_TRY(launch_rope(w.qkv, qkv_cols, c.q_heads, HD, T, seq, c.rope_theta, s));
@@ -393,12 +420,13 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
       ENNX_TRY(launch_gqa_attention(w.qkv, qkv_cols, w.qkv + kd, qkv_cols, w.qkv + vd, qkv_cols, w.o, kd, 2 * batch,
                                     seq, c.q_heads, c.kv_heads, s));
     }
-    ENNX_TRY(gemm2(w.o, kd, P[F_WO], H, kd, w.hidden, H, T, w.hidden, s, 0.0, c.residual_scale));
+    ENNX_TRY(gemm2(w.o, kd, L.w_o, P[F_WO], H, kd, w.hidden, H, T, w.hidden, s, 0.0, c.residual_scale));
   } else {
     const long long hw = (long long)c.kda_heads * HD, r = c.gate_rank;
     const uint16_t* ctl = w.qkv + sh.rows[F_QKV];  // [forget state | output state | beta], row stride qkv_cols
     // [f | og] = ctl[:, 0:2r] . [[W_f, 0], [0, W_o]]^T
-    ENNX_TRY(gemm2(ctl, qkv_cols, P[F_FORGET], 2 * hw, 2 * r, w.fg, 2 * hw, T, nullptr, s,
+    const uint16_t* base_fo = base_qkv + align_elems(field_elems(sh, F_QKV));
+    ENNX_TRY(gemm2(ctl, qkv_cols, base_fo, P[F_FORGET], 2 * hw, 2 * r, w.fg, 2 * hw, T, nullptr, s,
                    2.0 * 2.0 * T * hw * r));  // the zero blocks are not counted as work
     {
       KdaRawGate rg;
@@ -415,11 +443,11 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
     }
     ENNX_TRY(launch_kda_post(w.o, w.fg + hw, 2 * hw, P[F_OUT_NORM], M[F_OUT_NORM], Tc, c.kda_heads, T, c.rms_eps,
                              w.post, s));
-    ENNX_TRY(gemm2(w.post, hw, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s, 0.0, c.residual_scale));
+    ENNX_TRY(gemm2(w.post, hw, L.w_o, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s, 0.0, c.residual_scale));
   }
   ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_MOE_NORM], M[F_MOE_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
-  ENNX_TRY(run_moe(w.xn, P[F_ROUTER], M[F_ROUTER], P[F_GATE_UP], P[F_DOWN], T, Tc, 2, (int)H, c.experts, c.top_k,
-                   c.expert_width, w.hidden, w.hidden, w.moe, s, c.residual_scale));
+  ENNX_TRY(run_moe(w.xn, P[F_ROUTER], M[F_ROUTER], L.w_gate_up, L.w_down, T, Tc, 2, (int)H, c.experts, c.top_k,
+                   c.expert_width, w.hidden, w.hidden, w.moe, s, c.residual_scale, P[F_GATE_UP], P[F_DOWN]));
   return ENNX_B200_OK;
 }
 
@@ -432,7 +460,8 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const LayerPtrs& l
 // LM head (per-layer parity checks).
 int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_weights& W, uint64_t seed, float sigma,
                        int first_pair, int num_pairs, int batch, int seq, Work& w, float* fitness,
-                       cudaStream_t caller, int stop_layers = -1, uint16_t* hidden_out = nullptr) {
+                       cudaStream_t caller, int stop_layers = -1, uint16_t* hidden_out = nullptr,
+                       int* index_out = nullptr) {
   PipeStreams* ps = nullptr;
   ENNX_TRY(pipe_streams(&ps));
   cudaStream_t cs = ps->compute, ns = ps->noise;
@@ -453,12 +482,31 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
   ENNX_CUDA(cudaEventRecord(ev_start, caller), "fork");
   ENNX_CUDA(cudaStreamWaitEvent(cs, ev_start, 0), "fork compute");
   ENNX_CUDA(cudaStreamWaitEvent(ns, ev_start, 0), "fork noise");
-  {  // zero the block-diagonal forget/output-gate areas; perturbation fills only the diagonal blocks
+  {  // zero the block-diagonal forget/output-gate noise areas; the noise kernel fills only the diagonal blocks
     const long long blkdiag = field_elems(layer_shapes(c, false), F_FORGET);
     if (blkdiag > 0)
       for (int k = 0; k < 2; ++k)
-        ENNX_CUDA(cudaMemsetAsync(w.layer_scr[k] + w.field_off[F_FORGET], 0, 2 * (size_t)blkdiag * sizeof(uint16_t), ns),
+        ENNX_CUDA(cudaMemsetAsync(w.layer_scr[k] + w.field_off[F_FORGET], 0, (size_t)blkdiag * sizeof(uint16_t), ns),
                   "zero gate blocks");
+  }
+  // Base operands of the fused KDA projections, once per call: [W_qkv; W_ctl]
+  // (one GEMM computes both) and the block-diagonal [[W_f, 0], [0, W_o]].
+  for (int l = 0; l < L; ++l) {
+    if (is_gqa(c, l)) continue;
+    const ennx_b200_layer_weights& Lw = W.layers[l];
+    if (!Lw.w_qkv || !Lw.w_ctl || !Lw.w_forget || !Lw.w_ogate)
+      return set_error(ENNX_B200_INVALID_ARGUMENT, "missing KDA projection weights of layer %d", l);
+    const Shapes sk = layer_shapes(c, false);
+    uint16_t* bq = w.base_fused + (size_t)kda_ordinal(c, l) * w.base_stride;
+    uint16_t* bfo = bq + align_elems(field_elems(sk, F_QKV));
+    const size_t nq = (size_t)(sk.rows[F_QKV] * sk.cols[F_QKV]), nc = (size_t)(sk.rows[F_CTL] * sk.cols[F_CTL]);
+    const size_t hw = (size_t)sk.rows[F_FORGET], r = (size_t)sk.cols[F_FORGET];
+    ENNX_CUDA(cudaMemcpyAsync(bq, Lw.w_qkv, nq * 2, cudaMemcpyDeviceToDevice, cs), "base qkv");
+    ENNX_CUDA(cudaMemcpyAsync(bq + nq, Lw.w_ctl, nc * 2, cudaMemcpyDeviceToDevice, cs), "base ctl");
+    ENNX_CUDA(cudaMemsetAsync(bfo, 0, 4 * hw * r * 2, cs), "base gate blocks");
+    ENNX_CUDA(cudaMemcpy2DAsync(bfo, 4 * r, Lw.w_forget, 2 * r, 2 * r, hw, cudaMemcpyDeviceToDevice, cs), "base W_f");
+    ENNX_CUDA(cudaMemcpy2DAsync(bfo + hw * 2 * r + r, 4 * r, Lw.w_ogate, 2 * r, 2 * r, hw, cudaMemcpyDeviceToDevice, cs),
+              "base W_o gate");
   }
   targets_kernel<<<(unsigned)((Tc + 255) / 256), 256, 0, cs>>>(w.tokens, batch, seq, w.inp, w.tgt);
   ENNX_LAUNCH_CHECK("targets");
@@ -478,7 +526,7 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
     if (l == 0) {
       const int es = i % 2;
       PerturbJob& je = batch.job[batch.count++];
-      je.w = W.embedding; je.plus = w.emb_scr[es]; je.minus = w.emb_scr[es] + V * H; je.n = (uint64_t)(V * H);
+      je.w = nullptr; je.plus = w.emb_scr[es]; je.minus = nullptr; je.n = (uint64_t)(V * H);  // noise step only
       je.tensor = 0;
       PerturbJob& jn = batch.job[batch.count++];
       jn.w = W.final_norm; jn.plus = w.fnorm_scr[es]; jn.minus = w.fnorm_scr[es] + H; jn.n = (uint64_t)H;
@@ -489,7 +537,10 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
     {
       double elems = 0;
       for (int q = 0; q < batch.count; ++q) elems += (double)batch.job[q].n;
-      ProfScope pp("perturb", ns, 0, 6.0 * elems);
+      double bytes = 0;  // noise steps: 2 B written per element; W +/- e copies: 2 read + 4 written
+      for (int q = 0; q < batch.count; ++q) bytes += (batch.job[q].w ? 6.0 : 2.0) * (double)batch.job[q].n;
+      (void)elems;
+      ProfScope pp("noise", ns, 0, bytes);
       ENNX_TRY(launch_perturb_batch(batch, ns));
     }
     ENNX_CUDA(cudaEventRecord(ready[slot], ns), "ready");
@@ -501,14 +552,19 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
     if (j + 1 < jobs) ENNX_TRY(noise_job(j + 1));
     const int i = j / L, l = j % L, slot = j % 2, es = i % 2;
     ENNX_CUDA(cudaStreamWaitEvent(cs, ready[slot], 0), "wait ready");
-    if (l == 0) ENNX_TRY(launch_embed(w.inp, w.emb_scr[es], w.emb_scr[es] + V * H, Tc, T, (int)H, (int)V, w.hidden, cs));
-    ENNX_TRY(compute_layer(c, l, layer_ptrs(c, l, w, slot), batch, seq, w, cs));
+    if (l == 0)
+      ENNX_TRY(launch_embed(w.inp, W.embedding, nullptr, Tc, T, (int)H, (int)V, w.hidden, cs, w.emb_scr[es]));
+    ENNX_TRY(compute_layer(c, l, W.layers[l], layer_ptrs(c, l, w, slot), batch, seq, w, cs));
     ENNX_CUDA(cudaEventRecord(freed[slot], cs), "freed");
     freed_recorded[slot] = true;
     if (l == L - 1 && hidden_out) {
       ENNX_CUDA(cudaMemcpyAsync(hidden_out + (size_t)i * T * H, w.hidden, sizeof(uint16_t) * (size_t)T * H,
                                 cudaMemcpyDeviceToDevice, cs),
                 "copy hidden state");
+      if (index_out)
+        ENNX_CUDA(cudaMemcpyAsync(index_out, w.moe.idx, sizeof(int) * (size_t)T * c.top_k, cudaMemcpyDeviceToDevice,
+                                  cs),
+                  "copy routing");
       ENNX_CUDA(cudaEventRecord(emb_freed[es], cs), "emb freed");
       emb_freed_recorded[es] = true;
     } else if (l == L - 1) {
@@ -523,7 +579,7 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
       p.targets = w.tgt; p.lse_partial = w.lse; p.target_logit = w.tlogit;
       {
         ProfScope pf("gemm", cs, 2.0 * T * V * H, 2.0 * (T * H + 2.0 * V * H));
-        ENNX_TRY(gemm_bf16(&p, w.xn, w.emb_scr[es], nullptr, cs));
+        ENNX_TRY(gemm_bf16_perturbed(&p, w.xn, W.embedding, w.emb_scr[es], nullptr, cs));
       }
       ENNX_CUDA(cudaEventRecord(emb_freed[es], cs), "emb freed");
       emb_freed_recorded[es] = true;
@@ -647,7 +703,7 @@ int32_t ennx_b200_population_forward(const ennx_b200_model_config* cfg, const en
 
 int32_t ennx_b200_population_hidden(const ennx_b200_model_config* cfg, const ennx_b200_model_weights* weights,
                                     uint64_t seed, float sigma, int32_t pair, int32_t layers, const int32_t* tokens,
-                                    int32_t batch, int32_t seq, uint16_t* hidden, void* workspace,
+                                    int32_t batch, int32_t seq, uint16_t* hidden, int32_t* index, void* workspace,
                                     size_t workspace_bytes, void* stream) {
   ENNX_TRY(validate_config(cfg, batch, seq));
   if (!weights || !weights->embedding || !weights->final_norm || !weights->layers || !tokens || !hidden)
@@ -662,7 +718,7 @@ int32_t ennx_b200_population_hidden(const ennx_b200_model_config* cfg, const enn
   carve_work(*cfg, batch, seq, (uint8_t*)workspace, w);
   w.tokens = tokens;
   return run_population(*cfg, *weights, seed, sigma, pair, 1, batch, seq, w, nullptr, (cudaStream_t)stream, layers,
-                        hidden);
+                        hidden, index);
 }
 
 int32_t ennx_b200_l2norm_heads_bf16(uint16_t* x, int64_t rows, int32_t heads, int64_t ld, void* stream) {

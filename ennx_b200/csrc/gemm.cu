@@ -56,7 +56,6 @@ constexpr int EPI_BUF = 32 * 32 * 2;          // per-warp 32x32 bf16 staging til
 constexpr int TMEM_COLS = 512;
 constexpr int MAX_GROUPS = 256;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + EPI_WARPS * EPI_BUF + 1024 /*align*/ + 4096 /*barriers, tables*/;
-constexpr uint32_t IDESC = idesc_bf16_f32(BM, BN);
 
 struct Args {
   int M, N, K;
@@ -111,6 +110,161 @@ __device__ __forceinline__ TileInfo decode_tile(const Smem& s, const Args& a, in
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
+// Epilogue of one 128-row x 256-column accumulator tile (this CTA's rows of
+// tile t): warp quarter q reads TMEM lanes 32q..32q+31, warpgroup `half` owns
+// columns [128*half, 128*half + 128).  Full tiles leave through the per-warp
+// 32x32 staging tile `stg` and TMA stores; group-tail tiles use masked direct
+// stores.  tbase = TMEM address of the accumulator at this warp's lane quarter.
+template <int TM>
+__device__ __forceinline__ void epi_tile(const Args& a, const CUtensorMap* tmC, const TileInfo& t, int rank,
+                                         uint32_t tbase, uint8_t* stg, int lane, int q, int half) {
+  const uint32_t stg_addr = smem_u32(stg);
+  const int cta_row = t.mt * TM + rank * BM;  // first row of this CTA's 128 rows, within the group
+  const int mrow = cta_row + q * 32 + lane;
+  const bool row_ok = mrow < t.rows;
+  const long long grow = (long long)t.row0 + mrow;
+  const int warp_row0 = t.row0 + cta_row + q * 32;
+  const bool use_tma = a.has_tmc && (cta_row + BM <= t.rows || t.row0 + t.rows == a.M);
+  uint32_t v[32];
+
+  // 32 packed bf16 pairs (16 words) of this lane's row -> C[row, col0 .. col0+31]
+  auto store_bf16 = [&](const uint32_t (&pk)[16], int col0, int ncols) {
+    if (use_tma) {
+      if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+      __syncwarp();
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int jj = (j + (lane >> 1)) & 3;  // rotate the 16-byte chunks: fewer bank conflicts
+        uint32_t c0, c1, c2, c3;  // constant-index selects keep pk in registers
+        c0 = jj == 0 ? pk[0] : jj == 1 ? pk[4] : jj == 2 ? pk[8] : pk[12];
+        c1 = jj == 0 ? pk[1] : jj == 1 ? pk[5] : jj == 2 ? pk[9] : pk[13];
+        c2 = jj == 0 ? pk[2] : jj == 1 ? pk[6] : jj == 2 ? pk[10] : pk[14];
+        c3 = jj == 0 ? pk[3] : jj == 1 ? pk[7] : jj == 2 ? pk[11] : pk[15];
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(stg_addr + lane * 64 + jj * 16),
+                     "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+                     : "memory");
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) {
+        asm volatile(
+            "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)tmC),
+            "r"(stg_addr), "r"(col0), "r"(warp_row0)
+            : "memory");
+        asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+      }
+    } else if (row_ok && col0 < ncols) {
+      uint16_t* dst = (uint16_t*)a.C + grow * a.ldc + col0;
+      if (col0 + 32 <= ncols) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) st_global_v4(dst + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < ncols) dst[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
+      }
+    }
+  };
+
+  if (a.epi == ENNX_B200_EPI_SWIGLU) {
+    for (int c = half * 64; c < half * 64 + 64; c += 32) {
+      uint32_t u[32];
+      tmem_ld32(tbase + c, v);
+      tmem_ld32(tbase + c + BN / 2, u);
+      tmem_ld_wait();
+      uint32_t pk[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) {
+        float g0 = __uint_as_float(v[2 * j]) * a.alpha, g1 = __uint_as_float(v[2 * j + 1]) * a.alpha;
+        float u0 = __uint_as_float(u[2 * j]) * a.alpha, u1 = __uint_as_float(u[2 * j + 1]) * a.alpha;
+        pk[j] = pack_bf16x2(silu(g0) * u0, silu(g1) * u1);
+      }
+      store_bf16(pk, t.nt * (BN / 2) + c, a.N / 2);
+    }
+  } else if (a.epi == ENNX_B200_EPI_LSE) {
+    float m = -INFINITY, ssum = 0.0f, tl = 0.0f;
+    int tgt = row_ok ? a.targets[grow] : -1;
+    bool have_t = false;
+    for (int c = half * 128; c < half * 128 + 128; c += 32) {
+      tmem_ld32(tbase + c, v);
+      tmem_ld_wait();
+      int col0 = t.nt * BN + c;
+      float cm = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        float x = __uint_as_float(v[j]) * a.alpha;
+        if (col0 + j < a.N) cm = fmaxf(cm, x);
+        if (col0 + j == tgt) { tl = x; have_t = true; }
+      }
+      if (cm > -INFINITY) {
+        float nm = fmaxf(m, cm);
+        float acc_s = ssum * __expf(m - nm);
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (col0 + j < a.N) acc_s += __expf(__uint_as_float(v[j]) * a.alpha - nm);
+        ssum = acc_s;
+        m = nm;
+      }
+    }
+    if (row_ok) {
+      a.lse[grow * a.n_parts + t.nt * 2 + half] = make_float2(m, ssum);
+      if (have_t) a.tlogit[grow] = tl;
+    }
+  } else {
+    const float rs = (a.epi == ENNX_B200_EPI_ROWSCALE && row_ok) ? a.row_scale[grow] : a.alpha;
+    for (int c = half * 128; c < half * 128 + 128; c += 32) {
+      tmem_ld32(tbase + c, v);
+      tmem_ld_wait();
+      int col0 = t.nt * BN + c;
+      bool full = col0 + 32 <= a.N;
+      if (a.epi == ENNX_B200_EPI_F32) {
+        if (!row_ok || col0 >= a.N) continue;
+        float* dst = (float*)a.C + grow * a.ldc + col0;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            float x0 = __uint_as_float(v[4 * j]) * rs, x1 = __uint_as_float(v[4 * j + 1]) * rs;
+            float x2 = __uint_as_float(v[4 * j + 2]) * rs, x3 = __uint_as_float(v[4 * j + 3]) * rs;
+            st_global_v4(dst + 4 * j, __float_as_uint(x0), __float_as_uint(x1), __float_as_uint(x2),
+                         __float_as_uint(x3));
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < a.N) dst[j] = __uint_as_float(v[j]) * rs;
+        }
+        continue;
+      }
+      if (use_tma && col0 >= a.N) continue;  // warp-uniform: whole chunk outside C
+      float x[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(v[j]) * rs;
+      if (a.R && row_ok && col0 < a.N) {
+        const uint16_t* rp = a.R + grow * a.ldr + col0;
+        if (full) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            uint4 rv = *reinterpret_cast<const uint4*>(rp + 8 * j);
+            uint32_t w4[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+              x[8 * j + 2 * h] += bf16_to_f32((uint16_t)(w4[h] & 0xffffu));
+              x[8 * j + 2 * h + 1] += bf16_to_f32((uint16_t)(w4[h] >> 16));
+            }
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (col0 + j < a.N) x[j] += bf16_to_f32(rp[j]);
+        }
+      }
+      uint32_t pk[16];
+#pragma unroll
+      for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(x[2 * j], x[2 * j + 1]);
+      store_bf16(pk, col0, a.N);
+    }
+  }
+}
 template <bool PAIR>
 __global__ void __launch_bounds__(THREADS, 2)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -232,9 +386,7 @@ __global__ void __launch_bounds__(THREADS, 2)
     const int ew = warp - 2;
     const int q = warp & 3;
     const int half = ew >> 2;
-    const int r_in_tile = q * 32 + lane;
     uint8_t* stg = epi_smem + ew * EPI_BUF;
-    const uint32_t stg_addr = smem_u32(stg);
     int it = 0;
     for (int tile = unit0; tile < total; tile += units, ++it) {
       int acc = it & 1;
@@ -242,152 +394,8 @@ __global__ void __launch_bounds__(THREADS, 2)
       if (!mbar_wait(&s.tfull[acc], acc_phase, a.err)) { s.abort_flag = 1; break; }
       tc_fence_after();
       TileInfo t = decode_tile<G::TM>(s, a, tile);
-      const int cta_row = t.mt * G::TM + rank * BM;  // first row of this CTA's 128 rows, within the group
-      const int mrow = cta_row + r_in_tile;
-      const bool row_ok = mrow < t.rows;
-      const long long grow = (long long)t.row0 + mrow;
-      const int warp_row0 = t.row0 + cta_row + q * 32;
-      const bool use_tma = a.has_tmc && (cta_row + BM <= t.rows || t.row0 + t.rows == a.M);
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + acc * BN;
-      uint32_t v[32];
-
-      // 32 packed bf16 pairs (16 words) of this lane's row -> C[row, col0 .. col0+31]
-      auto store_bf16 = [&](const uint32_t (&pk)[16], int col0, int ncols) {
-        if (use_tma) {
-          if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
-          __syncwarp();
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int jj = (j + (lane >> 1)) & 3;  // rotate the 16-byte chunks: fewer bank conflicts
-            uint32_t c0, c1, c2, c3;  // constant-index selects keep pk in registers
-            c0 = jj == 0 ? pk[0] : jj == 1 ? pk[4] : jj == 2 ? pk[8] : pk[12];
-            c1 = jj == 0 ? pk[1] : jj == 1 ? pk[5] : jj == 2 ? pk[9] : pk[13];
-            c2 = jj == 0 ? pk[2] : jj == 1 ? pk[6] : jj == 2 ? pk[10] : pk[14];
-            c3 = jj == 0 ? pk[3] : jj == 1 ? pk[7] : jj == 2 ? pk[11] : pk[15];
-            asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(stg_addr + lane * 64 + jj * 16),
-                         "r"(c0), "r"(c1), "r"(c2), "r"(c3)
-                         : "memory");
-          }
-          fence_proxy_async();
-          __syncwarp();
-          if (lane == 0) {
-            asm volatile(
-                "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"((uint64_t)&tmC),
-                "r"(stg_addr), "r"(col0), "r"(warp_row0)
-                : "memory");
-            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-          }
-        } else if (row_ok && col0 < ncols) {
-          uint16_t* dst = (uint16_t*)a.C + grow * a.ldc + col0;
-          if (col0 + 32 <= ncols) {
-#pragma unroll
-            for (int j = 0; j < 4; ++j) st_global_v4(dst + 8 * j, pk[4 * j], pk[4 * j + 1], pk[4 * j + 2], pk[4 * j + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < ncols) dst[j] = (uint16_t)(pk[j >> 1] >> (16 * (j & 1)));
-          }
-        }
-      };
-
-      if (a.epi == ENNX_B200_EPI_SWIGLU) {
-        for (int c = half * 64; c < half * 64 + 64; c += 32) {
-          uint32_t u[32];
-          tmem_ld32(tbase + c, v);
-          tmem_ld32(tbase + c + BN / 2, u);
-          tmem_ld_wait();
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            float g0 = __uint_as_float(v[2 * j]) * a.alpha, g1 = __uint_as_float(v[2 * j + 1]) * a.alpha;
-            float u0 = __uint_as_float(u[2 * j]) * a.alpha, u1 = __uint_as_float(u[2 * j + 1]) * a.alpha;
-            pk[j] = pack_bf16x2(silu(g0) * u0, silu(g1) * u1);
-          }
-          store_bf16(pk, t.nt * (BN / 2) + c, a.N / 2);
-        }
-      } else if (a.epi == ENNX_B200_EPI_LSE) {
-        float m = -INFINITY, ssum = 0.0f, tl = 0.0f;
-        int tgt = row_ok ? a.targets[grow] : -1;
-        bool have_t = false;
-        for (int c = half * 128; c < half * 128 + 128; c += 32) {
-          tmem_ld32(tbase + c, v);
-          tmem_ld_wait();
-          int col0 = t.nt * BN + c;
-          float cm = -INFINITY;
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = __uint_as_float(v[j]) * a.alpha;
-            if (col0 + j < a.N) cm = fmaxf(cm, x);
-            if (col0 + j == tgt) { tl = x; have_t = true; }
-          }
-          if (cm > -INFINITY) {
-            float nm = fmaxf(m, cm);
-            float acc_s = ssum * __expf(m - nm);
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < a.N) acc_s += __expf(__uint_as_float(v[j]) * a.alpha - nm);
-            ssum = acc_s;
-            m = nm;
-          }
-        }
-        if (row_ok) {
-          a.lse[grow * a.n_parts + t.nt * 2 + half] = make_float2(m, ssum);
-          if (have_t) a.tlogit[grow] = tl;
-        }
-      } else {
-        const float rs = (a.epi == ENNX_B200_EPI_ROWSCALE && row_ok) ? a.row_scale[grow] : a.alpha;
-        for (int c = half * 128; c < half * 128 + 128; c += 32) {
-          tmem_ld32(tbase + c, v);
-          tmem_ld_wait();
-          int col0 = t.nt * BN + c;
-          bool full = col0 + 32 <= a.N;
-          if (a.epi == ENNX_B200_EPI_F32) {
-            if (!row_ok || col0 >= a.N) continue;
-            float* dst = (float*)a.C + grow * a.ldc + col0;
-            if (full) {
-#pragma unroll
-              for (int j = 0; j < 8; ++j) {
-                float x0 = __uint_as_float(v[4 * j]) * rs, x1 = __uint_as_float(v[4 * j + 1]) * rs;
-                float x2 = __uint_as_float(v[4 * j + 2]) * rs, x3 = __uint_as_float(v[4 * j + 3]) * rs;
-                st_global_v4(dst + 4 * j, __float_as_uint(x0), __float_as_uint(x1), __float_as_uint(x2),
-                             __float_as_uint(x3));
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < a.N) dst[j] = __uint_as_float(v[j]) * rs;
-            }
-            continue;
-          }
-          if (use_tma && col0 >= a.N) continue;  // warp-uniform: whole chunk outside C
-          float x[32];
-#pragma unroll
-          for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(v[j]) * rs;
-          if (a.R && row_ok && col0 < a.N) {
-            const uint16_t* rp = a.R + grow * a.ldr + col0;
-            if (full) {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                uint4 rv = *reinterpret_cast<const uint4*>(rp + 8 * j);
-                uint32_t w4[4] = {rv.x, rv.y, rv.z, rv.w};
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                  x[8 * j + 2 * h] += bf16_to_f32((uint16_t)(w4[h] & 0xffffu));
-                  x[8 * j + 2 * h + 1] += bf16_to_f32((uint16_t)(w4[h] >> 16));
-                }
-              }
-            } else {
-#pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (col0 + j < a.N) x[j] += bf16_to_f32(rp[j]);
-            }
-          }
-          uint32_t pk[16];
-#pragma unroll
-          for (int j = 0; j < 16; ++j) pk[j] = pack_bf16x2(x[2 * j], x[2 * j + 1]);
-          store_bf16(pk, col0, a.N);
-        }
-      }
+      epi_tile<G::TM>(a, &tmC, t, rank, tbase, stg, lane, q, half);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -408,15 +416,309 @@ __global__ void __launch_bounds__(THREADS, 2)
   }
 }
 
+// ===========================================================================
+// Perturbed-B variant: the antithetic pair's operands W + E and W - E are
+// formed inside the GEMM's operand path, never stored.
+//
+// Groups come in sign pairs: group e (< P = groups / 2) holds the rows of the
+// `+` candidate and group P + e the rows of the `-` candidate; both use B row
+// block e of W and of E (the bf16 noise step sigma*eps).  A work unit is
+// (e, m, n): 256 rows of each sign against one 256-row N tile, on a CTA pair
+// (cta_group::2); accumulators in TMEM columns [0, 256) (`+`) and
+// [256, 512) (`-`).  K advances in 32-wide stages through two rings:
+//   A ring (4 stages): A+ | A- of this CTA's 128 rows (2 x 8 KB), loaded by
+//     the A producer with the pair form of TMA onto the leader's barrier;
+//   B ring (8 stages): W | E of this CTA's 128 B rows (2 x 8 KB), loaded by
+//     the B producer onto this CTA's own barrier, then rewritten in place by
+//     the transform warps, W -> W + E and E -> W - E, in bf16x2 arithmetic
+//     (one RNE rounding of the exact sum, the definition of the perturbed
+//     weight).  All tiles share one 64-byte-swizzled K-major layout, so the
+//     rewrite is a flat element-wise pass over 16-byte chunks.  Two groups of
+//     four transform warps take alternate stages; each arrives on the
+//     leader's `ready` barrier after a proxy fence.
+// The B ring is twice as deep as the A ring because its chain (load,
+// rewrite, cross-CTA arrival) is longer.  One B stage feeds both signs' MMAs,
+// so W and E cross L2 once per unit, as a plain B operand would.  A sign
+// whose 256-row tile is empty (ragged MoE groups) has its loads and MMAs
+// skipped.
+// ===========================================================================
+constexpr int PB_TWARPS = 8;                                  // transform warps (two groups of four)
+constexpr int PB_GROUP_THREADS = 32 * PB_TWARPS / 2;
+constexpr int PB_THREADS = 64 + 32 * EPI_WARPS + 32 * PB_TWARPS + 32;  // + the B producer warp: 608
+constexpr int PB_BPROD_WARP = 2 + EPI_WARPS + PB_TWARPS;
+constexpr int PB_BK = 32;                                     // K per stage
+constexpr int PB_TILE = BM * PB_BK * 2;                       // 8 KB: 128 rows x 64 B
+constexpr int PB_NA = 6, PB_NB = 6;
+constexpr uint32_t PB_IDESC = idesc_bf16_f32(256, BN);
+static_assert((PB_NA + PB_NB) * 2 * PB_TILE <= STAGES * STAGE_BYTES, "perturbed-B rings fit the ring space");
+static_assert(PB_TILE / 16 == 4 * PB_GROUP_THREADS, "four 16-byte chunks of W and E per transform thread");
+static_assert(PB_THREADS * 96 <= 65536, "register budget");
+
+struct PbArgs {
+  int pairs;  // P
+  int diag;
+};
+
+struct PbSmem {  // lives after the epilogue staging tiles
+  uint64_t full_a[PB_NA], empty_a[PB_NA];
+  uint64_t full_b[PB_NB], ready_b[PB_NB], empty_b[PB_NB];
+  uint64_t tfull, tempty[2];
+  uint32_t tmem_base;
+  int abort_flag;
+  int total_units;
+  int row0[MAX_GROUPS + 1];
+  int unit0[MAX_GROUPS / 2 + 1];
+};
+
+struct PbUnit {
+  int e, mt, nt;
+};
+
+static_assert(sizeof(PbSmem) <= 4096, "perturbed-B barriers and tables fit their area");
+
+__device__ __forceinline__ PbUnit decode_pb(const PbSmem& s, int pairs, int n_tiles, int unit) {
+  int lo = 0, hi = pairs - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if (s.unit0[mid] <= unit) lo = mid; else hi = mid - 1;
+  }
+  PbUnit u;
+  u.e = lo;
+  const int mtiles = (s.unit0[lo + 1] - s.unit0[lo]) / n_tiles;
+  const int local = unit - s.unit0[lo];
+  u.mt = local % mtiles;
+  u.nt = local / mtiles;
+  return u;
+}
+
+__device__ __forceinline__ TileInfo pb_tile(const PbSmem& s, const PbUnit& u, int sign, int pairs) {
+  TileInfo t;
+  t.g = u.e + sign * pairs;
+  t.row0 = s.row0[t.g];
+  t.rows = s.row0[t.g + 1] - t.row0;
+  t.mt = u.mt;
+  t.nt = u.nt;
+  return t;
+}
+
+__global__ void __maxnreg__(96)
+    gemm_pb_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
+                   const __grid_constant__ CUtensorMap tmE, const __grid_constant__ CUtensorMap tmC, Args a,
+                   PbArgs pb) {
+  extern __shared__ uint8_t smem_raw[];
+  uint32_t raw_addr = smem_u32(smem_raw);
+  uint8_t* ring = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
+  uint8_t* ring_a = ring;                                // PB_NA x [A+ | A-]
+  uint8_t* ring_b = ring + PB_NA * 2 * PB_TILE;          // PB_NB x [W | E]
+  uint8_t* epi_smem = ring + STAGES * STAGE_BYTES;
+  PbSmem& s = *reinterpret_cast<PbSmem*>(epi_smem + EPI_WARPS * EPI_BUF);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rank = (int)cluster_ctarank();
+  const int first = blockIdx.x >> 1, stride = gridDim.x >> 1;
+  const int P = pb.pairs;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < PB_NA; ++i) { mbar_init(&s.full_a[i], 1); mbar_init(&s.empty_a[i], 1); }
+    for (int i = 0; i < PB_NB; ++i) {
+      mbar_init(&s.full_b[i], 1);
+      mbar_init(&s.ready_b[i], PB_TWARPS);  // one group of four warps in each of the two CTAs
+      mbar_init(&s.empty_b[i], 1);
+    }
+    mbar_init(&s.tfull, 1);
+    for (int i = 0; i < 2; ++i) mbar_init(&s.tempty[i], 2 * EPI_WARPS);
+    s.abort_flag = 0;
+    for (int g = 0; g < a.groups; ++g) {
+      s.row0[g] = a.group_offsets ? a.group_offsets[g] : g * a.rows_per_group;
+      s.row0[g + 1] = a.group_offsets ? a.group_offsets[g + 1] : (g + 1) * a.rows_per_group;
+    }
+    int n = 0;
+    for (int e = 0; e < P; ++e) {
+      const int rp = s.row0[e + 1] - s.row0[e], rm = s.row0[P + e + 1] - s.row0[P + e];
+      s.unit0[e] = n;
+      n += (max(rp, rm) + 255) / 256 * a.n_tiles;
+    }
+    s.unit0[P] = n;
+    s.total_units = n;
+    fence_barrier_init();
+    fence_proxy_async();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmE);
+    if (a.has_tmc) tma_prefetch_desc(&tmC);
+  }
+  if (warp == 1) { tmem_alloc_pair(&s.tmem_base, TMEM_COLS); tmem_relinquish_pair(); }
+  __syncthreads();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = s.tmem_base;
+  const int total = s.total_units;
+  const int KB = a.K / PB_BK;
+  auto a_ptr = [&](int stage, int sign) { return ring_a + (stage * 2 + sign) * PB_TILE; };
+  auto b_ptr = [&](int stage, int part) { return ring_b + (stage * 2 + part) * PB_TILE; };
+  auto aborted = [&]() { return *(volatile int*)&s.abort_flag != 0; };
+
+  if (warp == 0) {
+    // A producer: this CTA's 128 rows of each active sign; the pair form puts
+    // both CTAs' bytes on the leader's barrier
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int unit = first; unit < total && !aborted(); unit += stride) {
+        const PbUnit u = decode_pb(s, P, a.n_tiles, unit);
+        const TileInfo tp = pb_tile(s, u, 0, P), tm = pb_tile(s, u, 1, P);
+        const bool act_p = u.mt * 256 < tp.rows, act_m = u.mt * 256 < tm.rows;
+        const uint32_t bytes = 2u * PB_TILE * ((act_p ? 1u : 0u) + (act_m ? 1u : 0u));
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&s.empty_a[stage], phase ^ 1u, a.err)) { s.abort_flag = 1; break; }
+          if (rank == 0) mbar_arrive_expect_tx(&s.full_a[stage], bytes);
+          const uint32_t bar = mapa_shared(&s.full_a[stage], 0);
+          const int kx = kb * PB_BK;
+          if (act_p) tma_load_2d_pair(a_ptr(stage, 0), &tmA, bar, kx, tp.row0 + u.mt * 256 + rank * BM);
+          if (act_m) tma_load_2d_pair(a_ptr(stage, 1), &tmA, bar, kx, tm.row0 + u.mt * 256 + rank * BM);
+          if (++stage == PB_NA) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == PB_BPROD_WARP) {
+    // B producer: this CTA's 128 rows of W and E onto this CTA's own barrier
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int unit = first; unit < total && !aborted(); unit += stride) {
+        const PbUnit u = decode_pb(s, P, a.n_tiles, unit);
+        const int brow = u.e * a.b_group_rows + u.nt * BN + rank * BM;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&s.empty_b[stage], phase ^ 1u, a.err)) { s.abort_flag = 1; break; }
+          mbar_arrive_expect_tx(&s.full_b[stage], 2u * PB_TILE);
+          tma_load_2d(b_ptr(stage, 0), &tmW, &s.full_b[stage], kb * PB_BK, brow);
+          tma_load_2d(b_ptr(stage, 1), &tmE, &s.full_b[stage], kb * PB_BK, brow);
+          if (++stage == PB_NB) { stage = 0; phase ^= 1u; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      int sa = 0, sb = 0;
+      uint32_t pa = 0, pbh = 0;
+      int it = 0;
+      for (int unit = first; unit < total && !aborted(); unit += stride, ++it) {
+        const PbUnit u = decode_pb(s, P, a.n_tiles, unit);
+        const bool act_p = u.mt * 256 < pb_tile(s, u, 0, P).rows, act_m = u.mt * 256 < pb_tile(s, u, 1, P).rows;
+        const uint32_t acc_phase = it & 1;
+        bool ok = true;
+        for (int kb = 0; kb < KB; ++kb) {
+          if (!mbar_wait(&s.ready_b[sb], pbh, a.err) || !mbar_wait(&s.full_a[sa], pa, a.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t ab = smem_u32(a_ptr(sa, 0)), bb = smem_u32(b_ptr(sb, 0));
+          // `+` accumulator first; at the first stage wait until the epilogue
+          // has drained it (the `-` one is drained after it)
+          if (kb == 0 && !mbar_wait(&s.tempty[0], acc_phase ^ 1u, a.err)) { ok = false; break; }
+          tc_fence_after();
+          if (act_p && pb.diag != 4) {
+#pragma unroll
+            for (int k = 0; k < PB_BK / 16; ++k)
+              umma_f16_pair(tmem_base, smem_desc_sw64(ab + k * 32), smem_desc_sw64(bb + k * 32), PB_IDESC,
+                            (kb | k) != 0);
+          }
+          if (kb == 0 && !mbar_wait(&s.tempty[1], acc_phase ^ 1u, a.err)) { ok = false; break; }
+          tc_fence_after();
+          if (act_m && pb.diag != 1) {
+#pragma unroll
+            for (int k = 0; k < PB_BK / 16; ++k)
+              umma_f16_pair(tmem_base + BN, smem_desc_sw64(ab + PB_TILE + k * 32),
+                            smem_desc_sw64(bb + PB_TILE + k * 32), PB_IDESC, (kb | k) != 0);
+          }
+          umma_commit_pair(&s.empty_a[sa], 0x3);
+          umma_commit_pair(&s.empty_b[sb], 0x3);
+          if (++sa == PB_NA) { sa = 0; pa ^= 1u; }
+          if (++sb == PB_NB) { sb = 0; pbh ^= 1u; }
+        }
+        if (!ok) { s.abort_flag = 1; break; }
+        umma_commit_pair(&s.tfull, 0x3);
+      }
+    }
+  } else if (warp < 2 + EPI_WARPS) {
+    const int ew = warp - 2;
+    const int q = warp & 3;
+    const int half = ew >> 2;
+    uint8_t* stg = epi_smem + ew * EPI_BUF;
+    int it = 0;
+    for (int unit = first; unit < total; unit += stride, ++it) {
+      if (!mbar_wait(&s.tfull, it & 1, a.err)) { s.abort_flag = 1; break; }
+      tc_fence_after();
+      const PbUnit u = decode_pb(s, P, a.n_tiles, unit);
+      for (int sign = 0; sign < 2; ++sign) {
+        const TileInfo t = pb_tile(s, u, sign, P);
+        if (u.mt * 256 < t.rows)
+          epi_tile<256>(a, &tmC, t, rank, tmem_base + ((uint32_t)(q * 32) << 16) + sign * BN, stg, lane, q, half);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(&s.tempty[sign], 0));
+      }
+    }
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+    __syncwarp();
+  } else {
+    // transform warps: group tg (warps 10-13 / 14-17) takes B stages with
+    // parity tg; thread tt rewrites 16-byte chunks tt + 128 j (j < 4) of the
+    // two 8 KB slots, W -> W + E and E -> W - E (identical swizzled layouts)
+    const int tg = (warp - (2 + EPI_WARPS)) >> 2;
+    const int tt = threadIdx.x - 32 * (2 + EPI_WARPS) - tg * PB_GROUP_THREADS;
+    const uint32_t ready_remote = mapa_shared(&s.ready_b[0], 0);  // ready_b[i] = ready_remote + 8 i
+    const int my_units = total > first ? (total - first + stride - 1) / stride : 0;
+    const int items = my_units * KB;
+    int stage = tg;
+    uint32_t phase = 0;
+    for (int i = tg; i < items; i += 2) {
+      if (aborted()) break;
+      if (!mbar_wait(&s.full_b[stage], phase, a.err)) { s.abort_flag = 1; break; }
+      const uint32_t bw = smem_u32(b_ptr(stage, 0)) + tt * 16, be = bw + PB_TILE;
+      uint4 w[4], e[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(w[j].x), "=r"(w[j].y), "=r"(w[j].z), "=r"(w[j].w) : "r"(bw + j * 2048));
+        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(e[j].x), "=r"(e[j].y), "=r"(e[j].z), "=r"(e[j].w) : "r"(be + j * 2048));
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(bw + j * 2048), "r"(bf16x2_add(w[j].x, e[j].x)),
+                     "r"(bf16x2_add(w[j].y, e[j].y)), "r"(bf16x2_add(w[j].z, e[j].z)), "r"(bf16x2_add(w[j].w, e[j].w))
+                     : "memory");
+        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(be + j * 2048), "r"(bf16x2_sub(w[j].x, e[j].x)),
+                     "r"(bf16x2_sub(w[j].y, e[j].y)), "r"(bf16x2_sub(w[j].z, e[j].z)), "r"(bf16x2_sub(w[j].w, e[j].w))
+                     : "memory");
+      }
+      fence_proxy_async();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(ready_remote + 8u * (uint32_t)stage);
+      stage += 2;  // this group's next stage
+      if (stage >= PB_NB) { stage -= PB_NB; phase ^= 1u; }
+    }
+  }
+
+  __syncthreads();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
+  }
+}
+
 bool g_attr_set[64];
+bool g_pb_attr_set[64];
 
 }  // namespace
 }  // namespace ennx
 
 namespace ennx {
 
-int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint16_t* B, void* C, cudaStream_t st) {
-  if (!p || !A || !B) return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: null argument");
+// Argument checks shared by the plain and the perturbed-B GEMM.
+static int32_t check_gemm(const ennx_b200_gemm_params* p, void* C) {
   const int M = p->m, N = p->n, K = p->k;
   const int G = p->groups < 1 ? 1 : p->groups;
   if (M <= 0 || N <= 0 || K <= 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: empty problem %dx%dx%d", M, N, K);
@@ -444,23 +746,14 @@ int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint1
   if (p->residual && (p->ldr % 8 || ((uintptr_t)p->residual & 15u)))
     return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: residual must be 16-byte aligned with ldr %% 8 == 0");
 
-  // CTA-pair variant for problems with enough rows to fill 256-row tiles;
-  // ENNX_B200_GEMM_PAIR=0/1 forces a variant (tests exercise both).
-  bool pair = M >= 1024;
-  if (const char* e = getenv("ENNX_B200_GEMM_PAIR")) pair = e[0] == '1';
-  const int brows = pair ? Geo<true>::BROWS : Geo<false>::BROWS;
+  return ENNX_B200_OK;
+}
 
-  const long long b_rows = (long long)(G - 1) * p->b_group_rows + N;
-  CUtensorMap ta, tb, tc;
-  ENNX_TRY(make_tmap_2d_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)p->lda, BK, BM, true));
-  ENNX_TRY(make_tmap_2d_bf16(&tb, B, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, BK, brows, true));
-  memset(&tc, 0, sizeof(tc));
-  const bool bf16_out = epi == ENNX_B200_EPI_BF16 || epi == ENNX_B200_EPI_SWIGLU || epi == ENNX_B200_EPI_ROWSCALE;
-  if (bf16_out) {
-    const long long out_cols = epi == ENNX_B200_EPI_SWIGLU ? N / 2 : N;
-    ENNX_TRY(make_tmap_2d_bf16(&tc, C, (uint64_t)out_cols, (uint64_t)M, (uint64_t)p->ldc, 32, 32, false));
-  }
-
+// Kernel arguments common to both variants.
+static Args make_args(const ennx_b200_gemm_params* p, void* C, bool bf16_out) {
+  const int M = p->m, N = p->n, K = p->k;
+  const int G = p->groups < 1 ? 1 : p->groups;
+  const int epi = p->epilogue;
   Args a;
   a.M = M; a.N = N; a.K = K;
   a.groups = G;
@@ -478,6 +771,34 @@ int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint1
   a.n_tiles = (N + BN - 1) / BN;
   a.n_parts = 2 * a.n_tiles;
   a.has_tmc = bf16_out ? 1 : 0;
+  a.err = nullptr;
+  return a;
+}
+
+int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint16_t* B, void* C, cudaStream_t st) {
+  if (!p || !A || !B) return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm: null argument");
+  ENNX_TRY(check_gemm(p, C));
+  const int M = p->m, N = p->n, K = p->k;
+  const int G = p->groups < 1 ? 1 : p->groups;
+  const int epi = p->epilogue;
+  // CTA-pair variant for problems with enough rows to fill 256-row tiles;
+  // ENNX_B200_GEMM_PAIR=0/1 forces a variant (tests exercise both).
+  bool pair = M >= 1024;
+  if (const char* e = getenv("ENNX_B200_GEMM_PAIR")) pair = e[0] == '1';
+  const int brows = pair ? Geo<true>::BROWS : Geo<false>::BROWS;
+
+  const long long b_rows = (long long)(G - 1) * p->b_group_rows + N;
+  CUtensorMap ta, tb, tc;
+  ENNX_TRY(make_tmap_2d_bf16(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)p->lda, BK, BM, true));
+  ENNX_TRY(make_tmap_2d_bf16(&tb, B, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, BK, brows, true));
+  memset(&tc, 0, sizeof(tc));
+  const bool bf16_out = epi == ENNX_B200_EPI_BF16 || epi == ENNX_B200_EPI_SWIGLU || epi == ENNX_B200_EPI_ROWSCALE;
+  if (bf16_out) {
+    const long long out_cols = epi == ENNX_B200_EPI_SWIGLU ? N / 2 : N;
+    ENNX_TRY(make_tmap_2d_bf16(&tc, C, (uint64_t)out_cols, (uint64_t)M, (uint64_t)p->ldc, 32, 32, false));
+  }
+
+  Args a = make_args(p, C, bf16_out);
   a.err = device_error_word();
   if (!a.err) return set_error(ENNX_B200_CUDA_ERROR, "gemm: no device error word");
 
@@ -518,9 +839,73 @@ int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint1
   return ENNX_B200_OK;
 }
 
+
+int32_t gemm_bf16_perturbed(const ennx_b200_gemm_params* p, const uint16_t* A, const uint16_t* W, const uint16_t* E,
+                            void* C, cudaStream_t st) {
+  if (!p || !A || !W || !E) return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm_perturbed: null argument");
+  if (p->groups < 2 || p->groups % 2)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm_perturbed: groups must be 2 * pairs");
+  ENNX_TRY(check_gemm(p, C));
+  const int M = p->m, N = p->n, K = p->k;
+  const int G = p->groups;
+  const int epi = p->epilogue;
+  if ((((uintptr_t)W | (uintptr_t)E) & 15u))
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm_perturbed: W and E must be 16-byte aligned");
+  if (G > 2 && p->b_group_rows < N)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm_perturbed: b_group_rows must be >= N");
+  CUtensorMap ta, tw, te, tc;
+  const long long b_rows = (long long)(G / 2 - 1) * p->b_group_rows + N;
+  ENNX_TRY(make_tmap_2d_bf16_sw(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)p->lda, PB_BK, BM, 64));
+  ENNX_TRY(make_tmap_2d_bf16_sw(&tw, W, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, PB_BK, BM, 64));
+  ENNX_TRY(make_tmap_2d_bf16_sw(&te, E, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, PB_BK, BM, 64));
+  memset(&tc, 0, sizeof(tc));
+  const bool bf16_out = epi == ENNX_B200_EPI_BF16 || epi == ENNX_B200_EPI_SWIGLU || epi == ENNX_B200_EPI_ROWSCALE;
+  if (bf16_out) {
+    const long long out_cols = epi == ENNX_B200_EPI_SWIGLU ? N / 2 : N;
+    ENNX_TRY(make_tmap_2d_bf16(&tc, C, (uint64_t)out_cols, (uint64_t)M, (uint64_t)p->ldc, 32, 32, false));
+  }
+  Args a = make_args(p, C, bf16_out);
+  a.err = device_error_word();
+  if (!a.err) return set_error(ENNX_B200_CUDA_ERROR, "gemm_perturbed: no device error word");
+  PbArgs pb;
+  pb.pairs = G / 2;
+  pb.diag = getenv("ENNX_B200_PB_DIAG") ? atoi(getenv("ENNX_B200_PB_DIAG")) : 0;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!g_pb_attr_set[dev]) {
+    ENNX_CUDA(cudaFuncSetAttribute(gemm_pb_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+              "gemm_perturbed: set smem");
+    g_pb_attr_set[dev] = true;
+  }
+  long long units_bound = ((long long)M / 256 + G) * a.n_tiles;
+  long long clusters = sm_count() / 2;
+  if (units_bound < clusters) clusters = units_bound;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3((unsigned)(2 * clusters));
+  cfg.blockDim = dim3(PB_THREADS);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  ENNX_CUDA(cudaLaunchKernelEx(&cfg, gemm_pb_kernel, ta, tw, te, tc, a, pb), "gemm_perturbed launch");
+  ENNX_LAUNCH_CHECK("gemm_perturbed launch");
+  return ENNX_B200_OK;
+}
+
 }  // namespace ennx
 
 extern "C" int32_t ennx_b200_gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint16_t* B,
                                        void* C, void* stream) {
   return ennx::gemm_bf16(p, A, B, C, (cudaStream_t)stream);
+}
+
+extern "C" int32_t ennx_b200_gemm_bf16_perturbed(const ennx_b200_gemm_params* p, const uint16_t* A,
+                                                 const uint16_t* W, const uint16_t* E, void* C, void* stream) {
+  return ennx::gemm_bf16_perturbed(p, A, W, E, C, (cudaStream_t)stream);
 }

@@ -9,8 +9,9 @@ namespace ennx {
 // norm.cu
 int32_t launch_rmsnorm(const uint16_t* x, long long ldx, const uint16_t* w0, const uint16_t* w1, long long split,
                        uint16_t* out, long long ldo, long long rows, int width, float eps, cudaStream_t s);
+// noise (nullable): rows of set 0 are t0 + noise, set 1 t0 - noise
 int32_t launch_embed(const int* tokens, const uint16_t* t0, const uint16_t* t1, long long per_set, long long rows,
-                     int width, int vocab, uint16_t* out, cudaStream_t s);
+                     int width, int vocab, uint16_t* out, cudaStream_t s, const uint16_t* noise = nullptr);
 int32_t launch_l2norm_heads(uint16_t* base, long long ld, int heads, long long rows, cudaStream_t s);
 int32_t launch_kda_gate(const uint16_t* raw, long long ldraw, const uint16_t* rbeta, long long ldb,
                         const uint16_t* decay0, const uint16_t* decay1, const uint16_t* tb0, const uint16_t* tb1,
@@ -92,5 +93,8 @@ int32_t launch_perturb_batch(const PerturbBatch& batch, cudaStream_t s);
 
 // gemm.cu (internal form of ennx_b200_gemm_bf16)
 int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* a, const uint16_t* b, void* c, cudaStream_t s);
+// gemm.cu: W +/- E formed in the operand path (ennx_b200_gemm_bf16_perturbed)
+int32_t gemm_bf16_perturbed(const ennx_b200_gemm_params* p, const uint16_t* a, const uint16_t* w, const uint16_t* e,
+                            void* c, cudaStream_t s);
 
 }  // namespace ennx

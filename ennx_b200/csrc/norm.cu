@@ -63,9 +63,12 @@ __global__ void rmsnorm_kernel(const uint16_t* __restrict__ x, long long ldx, co
 }
 
 // hidden[r] = table_s[tokens[r % per_set]] for r in set s (s = r / per_set).
+// With `noise` (the pair's bf16 noise step of the table), the rows are formed
+// as t0 + noise (set 0) and t0 - noise (set 1), one RNE rounding each: the
+// perturbed embedding of the antithetic pair, never stored as a table.
 __global__ void embed_kernel(const int* __restrict__ tokens, const uint16_t* __restrict__ t0,
-                             const uint16_t* __restrict__ t1, long long per_set, long long rows, int width,
-                             int vocab, uint16_t* __restrict__ out, int* err) {
+                             const uint16_t* __restrict__ t1, const uint16_t* __restrict__ noise, long long per_set,
+                             long long rows, int width, int vocab, uint16_t* __restrict__ out, int* err) {
   long long row = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   int lane = threadIdx.x & 31;
   if (row >= rows) return;
@@ -74,8 +77,20 @@ __global__ void embed_kernel(const int* __restrict__ tokens, const uint16_t* __r
     if (lane == 0) atomicExch(err, ENNX_B200_INVALID_ARGUMENT);
     tok = 0;
   }
-  const uint16_t* src = (row < per_set ? t0 : t1) + (long long)tok * width;
   uint16_t* dst = out + row * width;
+  if (noise) {
+    const uint16_t* src = t0 + (long long)tok * width;
+    const uint16_t* nz = noise + (long long)tok * width;
+    const bool plus = row < per_set;
+    for (int c = lane * 8; c < width; c += 256) {
+      const uint4 w = *reinterpret_cast<const uint4*>(src + c), e = *reinterpret_cast<const uint4*>(nz + c);
+      *reinterpret_cast<uint4*>(dst + c) =
+          plus ? make_uint4(bf16x2_add(w.x, e.x), bf16x2_add(w.y, e.y), bf16x2_add(w.z, e.z), bf16x2_add(w.w, e.w))
+               : make_uint4(bf16x2_sub(w.x, e.x), bf16x2_sub(w.y, e.y), bf16x2_sub(w.z, e.z), bf16x2_sub(w.w, e.w));
+    }
+    return;
+  }
+  const uint16_t* src = (row < per_set ? t0 : t1) + (long long)tok * width;
   for (int c = lane * 8; c < width; c += 256)
     *reinterpret_cast<uint4*>(dst + c) = *reinterpret_cast<const uint4*>(src + c);
 }
@@ -188,10 +203,10 @@ int32_t launch_rmsnorm(const uint16_t* x, long long ldx, const uint16_t* w0, con
 }
 
 int32_t launch_embed(const int* tokens, const uint16_t* t0, const uint16_t* t1, long long per_set, long long rows,
-                     int width, int vocab, uint16_t* out, cudaStream_t s) {
+                     int width, int vocab, uint16_t* out, cudaStream_t s, const uint16_t* noise) {
   if (width % 256 != 0) return set_error(ENNX_B200_UNSUPPORTED, "embedding width must be a multiple of 256");
-  embed_kernel<<<warp_rows_grid(rows, 8), 256, 0, s>>>(tokens, t0, t1 ? t1 : t0, per_set, rows, width, vocab, out,
-                                                        device_error_word());
+  embed_kernel<<<warp_rows_grid(rows, 8), 256, 0, s>>>(tokens, t0, t1 ? t1 : t0, noise, per_set, rows, width, vocab,
+                                                        out, device_error_word());
   ENNX_LAUNCH_CHECK("embed");
   return ENNX_B200_OK;
 }

@@ -121,6 +121,11 @@ static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
 int32_t make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
                           uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer, bool swizzle128) {
+  return make_tmap_2d_bf16_sw(map, base, inner, outer, row_stride_elems, box_inner, box_outer, swizzle128 ? 128 : 0);
+}
+
+int32_t make_tmap_2d_bf16_sw(CUtensorMap* map, const void* base, uint64_t inner, uint64_t outer,
+                             uint64_t row_stride_elems, uint32_t box_inner, uint32_t box_outer, int swizzle_bytes) {
   if (!g_encode) {
     cudaDriverEntryPointQueryResult q;
     void* fn = nullptr;
@@ -138,7 +143,10 @@ int32_t make_tmap_2d_bf16(CUtensorMap* map, const void* base, uint64_t inner, ui
   cuuint32_t estr[2] = {1, 1};
   CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box,
                         estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        swizzle_bytes == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                        : swizzle_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                        : swizzle_bytes == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(ENNX_B200_INVALID_ARGUMENT, "cuTensorMapEncodeTiled failed (%d) for %llux%llu box %ux%u",

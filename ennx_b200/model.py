@@ -155,15 +155,21 @@ class PopulationEvaluator:
                   self.workspace.numel(), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         return fit
 
-    def hidden(self, tokens: torch.Tensor, seed: int, sigma: float, pair: int, layers: int) -> torch.Tensor:
+    def hidden(self, tokens: torch.Tensor, seed: int, sigma: float, pair: int, layers: int,
+               with_routing: bool = False):
         """Residual stream after the first `layers` layers of antithetic pair
         `pair`: bf16 [2, batch*seq, hidden] (sign + first) -- a per-layer
-        parity probe of the same device path as ``__call__``."""
+        parity probe of the same device path as ``__call__``.  with_routing
+        also returns the expert indices of layer `layers` - 1, int32
+        [2, batch*seq, top_k]."""
         if tokens.dtype != torch.int32 or tuple(tokens.shape) != (self.batch, self.seq + 1) or not tokens.is_cuda:
             raise ValueError(f"tokens must be a CUDA int32 tensor of shape {(self.batch, self.seq + 1)}")
         out = torch.empty(2, self.batch * self.seq, self.cfg.hidden, device=tokens.device, dtype=torch.bfloat16)
+        idx = torch.empty(2, self.batch * self.seq, self.cfg.top_k, device=tokens.device, dtype=torch.int32) \
+            if with_routing else None
         _abi.call("ennx_b200_population_hidden", ctypes.byref(self._ccfg), ctypes.byref(self._cw), seed, sigma, pair,
                   layers, ctypes.c_void_p(tokens.data_ptr()), self.batch, self.seq, ctypes.c_void_p(out.data_ptr()),
+                  None if idx is None else ctypes.c_void_p(idx.data_ptr()),
                   ctypes.c_void_p(self.workspace.data_ptr()), self.workspace.numel(),
                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-        return out
+        return (out, idx) if with_routing else out

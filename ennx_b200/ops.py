@@ -59,6 +59,41 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor | None = None, *, e
     return out
 
 
+def gemm_perturbed(a: torch.Tensor, w: torch.Tensor, e: torch.Tensor, out: torch.Tensor | None = None, *,
+                   pairs: int = 1, epilogue: int = _abi.EPI_BF16, alpha: float = 1.0, b_group_rows: int = 0,
+                   group_offsets: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+                   row_scale: torch.Tensor | None = None, targets: torch.Tensor | None = None,
+                   lse_partial: torch.Tensor | None = None, target_logit: torch.Tensor | None = None,
+                   n: int | None = None) -> torch.Tensor | None:
+    """C = A . (W +/- E)^T with the perturbed operands formed inside the GEMM
+    (see ``ennx_b200_gemm_bf16_perturbed``): 2*pairs row groups, the first
+    `pairs` against W + E, the rest against W - E."""
+    _check_dev(a, w, e, out, residual, row_scale, targets, group_offsets)
+    if a.dtype != torch.bfloat16 or w.dtype != torch.bfloat16 or e.dtype != torch.bfloat16:
+        raise ValueError("gemm operands must be bfloat16")
+    if w.shape != e.shape or w.stride() != e.stride():
+        raise ValueError("W and E must have the same shape and strides")
+    M, K = a.shape
+    N = n if n is not None else w.shape[0]
+    if out is None and epilogue != _abi.EPI_LSE:
+        cols = N // 2 if epilogue == _abi.EPI_SWIGLU else N
+        out = torch.empty(M, cols, device=a.device,
+                          dtype=torch.float32 if epilogue == _abi.EPI_F32 else torch.bfloat16)
+    p = _abi.GemmParams(
+        m=M, n=N, k=K, lda=a.stride(0), ldb=w.stride(0), ldc=0 if out is None else out.stride(0),
+        groups=2 * pairs, b_group_rows=b_group_rows,
+        group_offsets=None if group_offsets is None else group_offsets.data_ptr(),
+        epilogue=epilogue, alpha=alpha,
+        residual=None if residual is None else residual.data_ptr(),
+        ldr=0 if residual is None else residual.stride(0),
+        row_scale=None if row_scale is None else row_scale.data_ptr(),
+        targets=None if targets is None else targets.data_ptr(),
+        lse_partial=None if lse_partial is None else lse_partial.data_ptr(),
+        target_logit=None if target_logit is None else target_logit.data_ptr())
+    _abi.call("ennx_b200_gemm_bf16_perturbed", ctypes.byref(p), _ptr(a), _ptr(w), _ptr(e), _ptr(out), _stream())
+    return out
+
+
 def perturb_bf16(w: torch.Tensor, seed: int, pair: int, tensor: int, sigma: float,
                  plus: torch.Tensor | None = None, minus: torch.Tensor | None = None):
     """(W + sigma*eps, W - sigma*eps) with Philox noise keyed by (seed, pair, tensor, element)."""

@@ -114,9 +114,12 @@ ENNX_B200_API int32_t ennx_b200_dense_linear_f32(const float* input, size_t colu
 /* ---- population noise (no reference counterpart: the reference draws
  *      Rademacher signs; BASELINE asks for Philox Gaussian noise) --------- */
 
-/* out_plus = bf16(W + sigma*eps), out_minus = bf16(W - sigma*eps) (nullable),
- * eps = Philox4x32-10 Box-Muller normal of (seed, pair, tensor, element).
- * w/out_*: device bf16 bits[n].  Asynchronous. */
+/* Noise step e = bf16(sigma*eps) (RNE), eps = Philox4x32-10 Box-Muller
+ * normal of (seed, pair, tensor, element); out_plus = bf16(W + e), out_minus =
+ * bf16(W - e) (nullable), each one RNE rounding of the exact sum -- the
+ * values ennx_b200_gemm_bf16_perturbed forms from W and e.  w == NULL:
+ * out_plus receives e itself (out_minus must be NULL).  w/out_*: device bf16
+ * bits[n].  Asynchronous. */
 ENNX_B200_API int32_t ennx_b200_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair,
                                uint32_t tensor, float sigma, uint16_t* out_plus,
                                uint16_t* out_minus, void* stream);
@@ -166,6 +169,20 @@ typedef struct {
 
 ENNX_B200_API int32_t ennx_b200_gemm_bf16(const ennx_b200_gemm_params* params, const uint16_t* a,
                             const uint16_t* b, void* c, void* stream);
+
+/* The antithetic perturbed GEMM: the weights of candidate +/- are W + E and
+ * W - E, each rounded once to bf16 (RNE of the exact sum), formed tile by tile
+ * inside the GEMM's operand path and never written to memory.  E is the
+ * noise operand sigma*eps (bf16, same shape and row stride ldb as W).  groups
+ * = 2P: groups [0, P) hold the `+` rows and groups [P, 2P) the `-` rows;
+ * groups e and P + e both use row block e of W and E (rows
+ * [e*b_group_rows, e*b_group_rows + N)).  Other parameters and epilogues as
+ * ennx_b200_gemm_bf16.  The fused counterpart of the reference's perturbed
+ * contraction, linear_cpu / perturbed (rust/crates/ennx/src/dense/linear.rs:
+ * 484-548) and dense_linear (cuda/kernels/src/lib.rs:2359-2423), which form
+ * each perturbed weight inside the dot product. */
+ENNX_B200_API int32_t ennx_b200_gemm_bf16_perturbed(const ennx_b200_gemm_params* params, const uint16_t* a,
+                                                    const uint16_t* w, const uint16_t* e, void* c, void* stream);
 
 /* ---- forward-path operators (no reference counterpart unless cited) ---- */
 
@@ -309,7 +326,9 @@ ENNX_B200_API int32_t ennx_b200_population_forward(const ennx_b200_model_config*
 /* Per-layer parity probe of the population forward: runs antithetic pair
  * `pair` through the first `layers` decoder layers only and copies the
  * residual stream after them to hidden (device bf16 [2][batch*seq][hidden],
- * sign + first), instead of the LM head.  Same arguments and workspace as
+ * sign + first), instead of the LM head; index (nullable, device int32
+ * [2][batch*seq][top_k]) receives the expert choices of the last of those
+ * layers.  Same arguments and workspace as
  * ennx_b200_population_forward.  No counterpart in the reference (its
  * Metal executor exposes per-layer outputs only through its own buffers,
  * forward_metal.rs:614-810). */
@@ -317,8 +336,8 @@ ENNX_B200_API int32_t ennx_b200_population_hidden(const ennx_b200_model_config* 
                                                   const ennx_b200_model_weights* weights, uint64_t seed,
                                                   float sigma, int32_t pair, int32_t layers,
                                                   const int32_t* tokens, int32_t batch, int32_t seq,
-                                                  uint16_t* hidden, void* workspace, size_t workspace_bytes,
-                                                  void* stream);
+                                                  uint16_t* hidden, int32_t* index, void* workspace,
+                                                  size_t workspace_bytes, void* stream);
 
 /* ---- KDA element-wise stages (the 16k-prefill kernels of kda_moe.metal) --- */
 

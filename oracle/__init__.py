@@ -240,6 +240,13 @@ def noise(seed: int, pair: int, tensor: int, n: int, start: int = 0) -> np.ndarr
     return out[:n]
 
 
+def noise_step_bf16(n, seed, pair, tensor, sigma):
+    """bf16 bits of the noise step e = bf16(sigma * eps) for elements [0, n)."""
+    out = np.zeros(n, np.uint16)
+    lib().eo_perturb_bf16_at(None, n, 0, seed, pair, tensor, sigma, 1, _p(out))
+    return out
+
+
 def perturb_bf16(w_bits, seed, pair, tensor, sigma, sign):
     """bf16 bits of W + sign*sigma*eps.  Tensors above 4 M elements are split
     over host threads (the C function releases the GIL under ctypes)."""

@@ -367,15 +367,23 @@ void eo_noise8(uint64_t seed, uint32_t pair, uint32_t tensor, uint64_t block, fl
     for (int j = 0; j < 4; ++j) box_muller16(x[j], &out[2 * j], &out[2 * j + 1]);
 }
 
-/* W~ = bf16(W + sign * (sigma * eps)), two fp32 roundings then RNE, for
- * elements [start, start + n) of a tensor (w and out point at element
- * start; start % 8 == 0). */
+/* Noise step e = bf16(sigma * eps) (fp32 product, RNE) and the perturbed
+ * weight W~ = bf16(W + sign * e): the float sum of two bf16 values is exact
+ * (or, for exponents more than 16 apart, rounds to a value whose RNE
+ * encoding equals that of the exact sum), so this is one RNE rounding of the
+ * exact sum.  Elements [start, start + n) of a tensor (w and out point at
+ * element start; start % 8 == 0).  w == NULL: out receives e itself. */
 void eo_perturb_bf16_at(const uint16_t* w, size_t n, size_t start, uint64_t seed, uint32_t pair, uint32_t tensor,
                         float sigma, int sign, uint16_t* out) {
     float z[8];
     for (size_t i = 0; i < n; ++i) {
         if ((i & 7) == 0) eo_noise8(seed, pair, tensor, (start + i) >> 3, z);
-        float step = sigma * z[i & 7];
+        uint16_t e = eo_bf16_encode(sigma * z[i & 7]);
+        if (!w) {
+            out[i] = e;
+            continue;
+        }
+        float step = eo_bf16_decode(e);
         float v = sign >= 0 ? eo_bf16_decode(w[i]) + step : eo_bf16_decode(w[i]) - step;
         out[i] = eo_bf16_encode(v);
     }

@@ -37,11 +37,15 @@ def perturbed(bits: np.ndarray, seed: int, pair: int, tensor: int, sigma, sign: 
 
 
 def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pair: int, sign: int,
-                   return_rows: bool = False, hidden_at: dict | None = None):
+                   return_rows: bool = False, hidden_at: dict | None = None, router_gaps: list | None = None,
+                   routing: list | None = None):
     """Mean CE of one candidate.  W: {'embedding': bits, 'final_norm': bits,
     'layers': [ {field: bits} ]} (bf16 bit patterns as uint16 arrays).
     hidden_at: {n: None} -> filled with the residual stream [T, H] after the
-    first n layers (float32 values of the bf16 activations)."""
+    first n layers (float32 values of the bf16 activations).
+    router_gaps: list -> appended per layer with each token's gap between its
+    k-th and (k+1)-th router logit (how close its expert choice is to a tie).
+    routing: list -> appended per layer with the expert indices [T, k]."""
     B, S1 = tokens.shape
     S = S1 - 1
     T = B * S
@@ -89,6 +93,12 @@ def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pa
         x = round_bf16(rmsnorm(h, P["moe_norm"], cfg.rms_eps))
         logits = router_logits(to_bf16_bits(x), to_bf16_bits(P["w_router"]))
         idx, gate = router_topk(logits, cfg.top_k)
+        if routing is not None:
+            routing.append(idx.copy())
+        if router_gaps is not None:
+            srt = -np.sort(-logits.astype(np.float64), axis=1)
+            k = cfg.top_k
+            router_gaps.append(srt[:, k - 1] - srt[:, k] if k < srt.shape[1] else np.full(T, np.inf))
         wg_, wu_ = _split_gate_up(P["w_gate_up"])
         y = h.astype(np.float64)
         for e in range(cfg.experts):

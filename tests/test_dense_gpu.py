@@ -144,3 +144,28 @@ def test_perturb_noise_is_finite_over_many_draws():
     for t in (plus, minus):
         bits = t.view(torch.int16)
         assert not bool(((bits & 0x7F80) == 0x7F80).any().item())
+
+
+def test_noise_step_matches_oracle():
+    """The noise operand of the perturbed GEMM, e = bf16(sigma*eps), alone."""
+    n = (1 << 16) + 5
+    e = torch.empty(n, dtype=torch.int16, device="cuda")
+    st = _abi.lib().ennx_b200_perturb_bf16(None, n, 0xDEADBEEF12345678, 5, 17, 1e-3, ptr(e), None, stream())
+    assert st == 0
+    ref = O.from_bf16_bits(O.noise_step_bf16(n, 0xDEADBEEF12345678, 5, 17, 1e-3)).astype(np.float64)
+    got = O.from_bf16_bits(host_u16(e)).astype(np.float64)
+    # Box-Muller on the SFU vs fp64 libm: sigma*eps agrees to ~1e-6 of sigma,
+    # then one bf16 rounding: at most one bf16 ulp (<= 2^-7 relative) apart,
+    # plus an absolute term for values near zero
+    assert np.all(np.abs(got - ref) <= 2.0 ** -7 * np.abs(ref) + 1e-3 * 1e-5)
+    # W +/- e from the same call sequence equals the perturbation with W given
+    rng = np.random.default_rng(3)
+    w = O.to_bf16_bits(rng.standard_normal(n).astype(np.float32) * 0.02)
+    tw = dev_u16(w)
+    plus, minus = torch.empty_like(tw), torch.empty_like(tw)
+    assert _abi.lib().ennx_b200_perturb_bf16(ptr(tw), n, 0xDEADBEEF12345678, 5, 17, 1e-3, ptr(plus), ptr(minus),
+                                             stream()) == 0
+    wf = O.from_bf16_bits(w).astype(np.float64)
+    ef = O.from_bf16_bits(host_u16(e)).astype(np.float64)
+    assert np.array_equal(host_u16(plus), O.to_bf16_bits((wf + ef).astype(np.float32)))
+    assert np.array_equal(host_u16(minus), O.to_bf16_bits((wf - ef).astype(np.float32)))

@@ -12,14 +12,19 @@
 // generalised to prefill over whole sequences, GQA layers every
 // `attn_period` layers, and a fused LM-head cross-entropy at the end.
 //
-// Work is organised per antithetic pair: the pair's noise step e =
-// bf16(sigma*eps) of one layer's matrices is generated into a scratch area
-// (streaming kernel on a second stream), then both candidates' tokens run
-// through the layer as one batch; every GEMM is one perturbed tcgen05 launch
-// that forms W + e and W - e inside its operand path (MoE: E expert pairs),
-// so no perturbed weight matrix is ever stored.  Small per-layer vectors
-// (norm weights, decay, time bias) and the router matrix are written as
-// W +/- e copies.
+// Work is organised per antithetic pair: the pair's perturbation of one layer
+// is generated into a scratch area (streaming kernel on a second stream)
+// while the previous layer runs, then both candidates' tokens run through
+// the layer as one batch.  Two perturbation modes
+// (ennx_b200_set_perturbation_mode):
+//   materialised (default): the noise kernel writes W + e and W - e
+//     (e = bf16(sigma*eps)) for every tensor; every GEMM is a 2-group tcgen05
+//     launch on those copies (MoE: 2*E groups);
+//   fused: the noise kernel writes only the noise step e of the matrices, and
+//     every GEMM is one perturbed launch that forms W + e and W - e inside its
+//     operand path, so no perturbed matrix is stored.  Small per-layer vectors
+//     and the router matrix are W +/- e copies in both modes.
+// Both modes compute the same perturbed weights bit for bit.
 #include <string.h>
 
 #include <algorithm>
@@ -191,9 +196,10 @@ long long field_elems(const Shapes& sh, int f) {
 }
 // Matrices consumed by the perturbed GEMM: only their noise step e is
 // generated (one copy); the other fields get materialised W + e and W - e.
-bool gemm_field(int f) {
-  return f == F_QKV || f == F_CTL || f == F_FORGET || f == F_OGATE || f == F_WO || f == F_GATE_UP || f == F_DOWN;
+bool gemm_field(int f, bool fused) {
+  return fused && (f == F_QKV || f == F_CTL || f == F_FORGET || f == F_OGATE || f == F_WO || f == F_GATE_UP || f == F_DOWN);
 }
+int g_fused_mode = 0;  // ennx_b200_set_perturbation_mode
 int kda_ordinal(const ennx_b200_model_config& c, int l) {  // index of KDA layer l among the KDA layers
   int n = 0;
   for (int i = 0; i < l; ++i) n += is_gqa(c, i) ? 0 : 1;
@@ -204,7 +210,8 @@ long long qkv_ld(const Shapes& sh) { return (sh.rows[F_QKV] + sh.rows[F_CTL] + 7
 
 struct Work {
   const int* tokens;       // caller's [batch, seq + 1] token ids
-  uint16_t *emb_scr[2];    // two slots of the embedding's noise step [V*H]
+  bool fused;              // perturbation mode of this call
+  uint16_t *emb_scr[2];    // two slots of [2][V*H] (plus, minus), or the noise step [V*H] (fused)
   uint16_t *fnorm_scr[2];  // two slots of [2][H] (final norm plus, minus)
   uint16_t *layer_scr[2];  // two slots of per-field areas: [n] noise (GEMM fields) or [2][n] (plus, minus)
   size_t field_off[F_COUNT];  // element offsets into layer_scr
@@ -241,9 +248,10 @@ int32_t validate_config(const ennx_b200_model_config* c, int batch, int seq) {
 
 void carve_work(const ennx_b200_model_config& c, int batch, int seq, uint8_t* base, Work& w) {
   Carver cv{base, 0, 0, base == nullptr};
+  w.fused = g_fused_mode != 0;
   const long long Tc = (long long)batch * seq, T = 2 * Tc, H = c.hidden;
   for (int k = 0; k < 2; ++k) {
-    w.emb_scr[k] = cv.take<uint16_t>(align_elems((long long)c.vocab * H));
+    w.emb_scr[k] = cv.take<uint16_t>(2 * align_elems((long long)c.vocab * H));
     w.fnorm_scr[k] = cv.take<uint16_t>(2 * align_elems(H));
   }
   size_t per_field_max[F_COUNT] = {0};
@@ -255,7 +263,7 @@ void carve_work(const ennx_b200_model_config& c, int batch, int seq, uint8_t* ba
     }
   }
   size_t off = 0;
-  for (int f = 0; f < F_COUNT; ++f) { w.field_off[f] = off; off += (gemm_field(f) ? 1 : 2) * per_field_max[f]; }
+  for (int f = 0; f < F_COUNT; ++f) { w.field_off[f] = off; off += 2 * per_field_max[f]; }  // room for both modes
   for (int k = 0; k < 2; ++k) w.layer_scr[k] = cv.take<uint16_t>(off);
   {
     const Shapes sk = layer_shapes(c, false);
@@ -305,7 +313,9 @@ const uint16_t* field_ptr(const ennx_b200_layer_weights& L, int f) {
 }
 
 // One antithetic pair's projection: rows [0, rows/2) against W + e, the rest
-// against W - e (W and e [n, k], row stride k), bf16 out (+ residual).
+// against W - e, bf16 out (+ residual).  w == nullptr: e points at the stored
+// copies [W + e; W - e] ([2n, k]); otherwise W and e are [n, k] and the
+// perturbed GEMM forms both signs in its operand path.
 int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* w, const uint16_t* e, long long n, long long k,
               void* c, long long ldc, long long rows, const uint16_t* residual, cudaStream_t s,
               double useful_flops = 0.0, float alpha = 1.0f) {
@@ -318,7 +328,7 @@ int32_t gemm2(const uint16_t* a, long long lda, const uint16_t* w, const uint16_
   p.residual = residual; p.ldr = ldc;
   ProfScope ps("gemm", s, useful_flops > 0.0 ? useful_flops : 2.0 * rows * n * k,
                2.0 * (rows * k + 2.0 * n * k + rows * n * (residual ? 2 : 1)));
-  return gemm_bf16_perturbed(&p, a, w, e, c, s);
+  return w ? gemm_bf16_perturbed(&p, a, w, e, c, s) : gemm_bf16(&p, a, e, c, s);
 }
 
 // Per-device streams of the pipelined population forward: `compute` runs the
@@ -360,12 +370,19 @@ LayerPtrs layer_ptrs(const ennx_b200_model_config& c, int l, const Work& w, int 
     lp.P[f] = lp.M[f] = nullptr;
     if (n == 0 || f == F_CTL || f == F_OGATE) continue;
     lp.P[f] = w.layer_scr[slot] + w.field_off[f];  // GEMM fields: the noise step e
-    if (!gemm_field(f)) lp.M[f] = lp.P[f] + align_elems(field_elems(sh, f));  // minus copy after plus
+    // minus copy directly after plus; GEMM operands (n % 64 == 0) keep the B
+    // row-block stride between the two signs at exactly `rows`
+    const long long fn = field_elems(sh, f);
+    if (!gemm_field(f, w.fused)) lp.M[f] = lp.P[f] + (fn % 8 == 0 ? (size_t)fn : align_elems(fn));
   }
-  if (sh.rows[F_CTL]) lp.P[F_CTL] = lp.P[F_QKV] + sh.rows[F_QKV] * sh.cols[F_QKV];  // control rows follow QKV
+  if (sh.rows[F_CTL]) {  // control rows follow the QKV rows of each sign
+    lp.P[F_CTL] = lp.P[F_QKV] + sh.rows[F_QKV] * sh.cols[F_QKV];
+    if (lp.M[F_QKV]) lp.M[F_CTL] = lp.M[F_QKV] + sh.rows[F_QKV] * sh.cols[F_QKV];
+  }
   if (sh.rows[F_OGATE]) {  // output-gate block: rows [hw, 2hw), columns [r, 2r)
     const long long hw = sh.rows[F_FORGET], r = sh.cols[F_FORGET];
     lp.P[F_OGATE] = lp.P[F_FORGET] + hw * 2 * r + r;
+    if (lp.M[F_FORGET]) lp.M[F_OGATE] = lp.M[F_FORGET] + hw * 2 * r + r;
   }
   return lp;
 }
@@ -386,7 +403,7 @@ int32_t add_layer_jobs(const ennx_b200_model_config& c, const ennx_b200_model_we
     // forget / output-gate weights land as blocks of the block-diagonal matrix
     const bool blk = f == F_FORGET || f == F_OGATE;
     PerturbJob& j = batch.job[batch.count++];
-    j.w = gemm_field(f) ? nullptr : src;  // GEMM fields: noise step only
+    j.w = gemm_field(f, w.fused) ? nullptr : src;  // fused GEMM fields: noise step only
     j.plus = lp.P[f]; j.minus = lp.M[f]; j.n = (uint64_t)n;
     j.tensor = 16u + 16u * (uint32_t)l + (uint32_t)f;
     j.cols = blk ? (uint32_t)sh.cols[f] : 0u;
@@ -408,7 +425,8 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const ennx_b200_la
   ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_ATTN_NORM], M[F_ATTN_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
   // one GEMM: [q | k | v] (and on KDA layers the control projection after them)
   const long long qkv_cols = qkv_ld(sh);
-  const uint16_t* base_qkv = gqa ? L.w_qkv : w.base_fused + (size_t)kda_ordinal(c, l) * w.base_stride;
+  const uint16_t* base_qkv =
+      !w.fused ? nullptr : gqa ? L.w_qkv : w.base_fused + (size_t)kda_ordinal(c, l) * w.base_stride;
   ENNX_TRY(gemm2(w.xn, H, base_qkv, P[F_QKV], sh.rows[F_QKV] + sh.rows[F_CTL], H, w.qkv, qkv_cols, T, nullptr, s));
   if (gqa) {
     const long long kd = (long long)c.q_heads * HD, vd = kd + (long long)c.kv_heads * HD;
@@ -420,12 +438,12 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const ennx_b200_la
       ENNX_TRY(launch_gqa_attention(w.qkv, qkv_cols, w.qkv + kd, qkv_cols, w.qkv + vd, qkv_cols, w.o, kd, 2 * batch,
                                     seq, c.q_heads, c.kv_heads, s));
     }
-    ENNX_TRY(gemm2(w.o, kd, L.w_o, P[F_WO], H, kd, w.hidden, H, T, w.hidden, s, 0.0, c.residual_scale));
+    ENNX_TRY(gemm2(w.o, kd, w.fused ? L.w_o : nullptr, P[F_WO], H, kd, w.hidden, H, T, w.hidden, s, 0.0, c.residual_scale));
   } else {
     const long long hw = (long long)c.kda_heads * HD, r = c.gate_rank;
     const uint16_t* ctl = w.qkv + sh.rows[F_QKV];  // [forget state | output state | beta], row stride qkv_cols
     // [f | og] = ctl[:, 0:2r] . [[W_f, 0], [0, W_o]]^T
-    const uint16_t* base_fo = base_qkv + align_elems(field_elems(sh, F_QKV));
+    const uint16_t* base_fo = w.fused ? base_qkv + align_elems(field_elems(sh, F_QKV)) : nullptr;
     ENNX_TRY(gemm2(ctl, qkv_cols, base_fo, P[F_FORGET], 2 * hw, 2 * r, w.fg, 2 * hw, T, nullptr, s,
                    2.0 * 2.0 * T * hw * r));  // the zero blocks are not counted as work
     {
@@ -443,11 +461,15 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const ennx_b200_la
     }
     ENNX_TRY(launch_kda_post(w.o, w.fg + hw, 2 * hw, P[F_OUT_NORM], M[F_OUT_NORM], Tc, c.kda_heads, T, c.rms_eps,
                              w.post, s));
-    ENNX_TRY(gemm2(w.post, hw, L.w_o, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s, 0.0, c.residual_scale));
+    ENNX_TRY(gemm2(w.post, hw, w.fused ? L.w_o : nullptr, P[F_WO], H, hw, w.hidden, H, T, w.hidden, s, 0.0, c.residual_scale));
   }
   ENNX_TRY(launch_rmsnorm(w.hidden, H, P[F_MOE_NORM], M[F_MOE_NORM], Tc, w.xn, H, T, (int)H, c.rms_eps, s));
-  ENNX_TRY(run_moe(w.xn, P[F_ROUTER], M[F_ROUTER], L.w_gate_up, L.w_down, T, Tc, 2, (int)H, c.experts, c.top_k,
-                   c.expert_width, w.hidden, w.hidden, w.moe, s, c.residual_scale, P[F_GATE_UP], P[F_DOWN]));
+  if (w.fused)
+    ENNX_TRY(run_moe(w.xn, P[F_ROUTER], M[F_ROUTER], L.w_gate_up, L.w_down, T, Tc, 2, (int)H, c.experts, c.top_k,
+                     c.expert_width, w.hidden, w.hidden, w.moe, s, c.residual_scale, P[F_GATE_UP], P[F_DOWN]));
+  else  // stored copies: expert e of set 1 is block E + e of [W + e; W - e]
+    ENNX_TRY(run_moe(w.xn, P[F_ROUTER], M[F_ROUTER], P[F_GATE_UP], P[F_DOWN], T, Tc, 2, (int)H, c.experts, c.top_k,
+                     c.expert_width, w.hidden, w.hidden, w.moe, s, c.residual_scale));
   return ENNX_B200_OK;
 }
 
@@ -486,12 +508,12 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
     const long long blkdiag = field_elems(layer_shapes(c, false), F_FORGET);
     if (blkdiag > 0)
       for (int k = 0; k < 2; ++k)
-        ENNX_CUDA(cudaMemsetAsync(w.layer_scr[k] + w.field_off[F_FORGET], 0, (size_t)blkdiag * sizeof(uint16_t), ns),
+        ENNX_CUDA(cudaMemsetAsync(w.layer_scr[k] + w.field_off[F_FORGET], 0, 2 * (size_t)blkdiag * sizeof(uint16_t), ns),
                   "zero gate blocks");
   }
   // Base operands of the fused KDA projections, once per call: [W_qkv; W_ctl]
   // (one GEMM computes both) and the block-diagonal [[W_f, 0], [0, W_o]].
-  for (int l = 0; l < L; ++l) {
+  for (int l = 0; l < L && w.fused; ++l) {
     if (is_gqa(c, l)) continue;
     const ennx_b200_layer_weights& Lw = W.layers[l];
     if (!Lw.w_qkv || !Lw.w_ctl || !Lw.w_forget || !Lw.w_ogate)
@@ -526,7 +548,8 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
     if (l == 0) {
       const int es = i % 2;
       PerturbJob& je = batch.job[batch.count++];
-      je.w = nullptr; je.plus = w.emb_scr[es]; je.minus = nullptr; je.n = (uint64_t)(V * H);  // noise step only
+      je.w = w.fused ? nullptr : W.embedding;  // fused: noise step only
+      je.plus = w.emb_scr[es]; je.minus = w.fused ? nullptr : w.emb_scr[es] + V * H; je.n = (uint64_t)(V * H);
       je.tensor = 0;
       PerturbJob& jn = batch.job[batch.count++];
       jn.w = W.final_norm; jn.plus = w.fnorm_scr[es]; jn.minus = w.fnorm_scr[es] + H; jn.n = (uint64_t)H;
@@ -553,7 +576,8 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
     const int i = j / L, l = j % L, slot = j % 2, es = i % 2;
     ENNX_CUDA(cudaStreamWaitEvent(cs, ready[slot], 0), "wait ready");
     if (l == 0)
-      ENNX_TRY(launch_embed(w.inp, W.embedding, nullptr, Tc, T, (int)H, (int)V, w.hidden, cs, w.emb_scr[es]));
+      ENNX_TRY(w.fused ? launch_embed(w.inp, W.embedding, nullptr, Tc, T, (int)H, (int)V, w.hidden, cs, w.emb_scr[es])
+                       : launch_embed(w.inp, w.emb_scr[es], w.emb_scr[es] + V * H, Tc, T, (int)H, (int)V, w.hidden, cs));
     ENNX_TRY(compute_layer(c, l, W.layers[l], layer_ptrs(c, l, w, slot), batch, seq, w, cs));
     ENNX_CUDA(cudaEventRecord(freed[slot], cs), "freed");
     freed_recorded[slot] = true;
@@ -579,7 +603,8 @@ int32_t run_population(const ennx_b200_model_config& c, const ennx_b200_model_we
       p.targets = w.tgt; p.lse_partial = w.lse; p.target_logit = w.tlogit;
       {
         ProfScope pf("gemm", cs, 2.0 * T * V * H, 2.0 * (T * H + 2.0 * V * H));
-        ENNX_TRY(gemm_bf16_perturbed(&p, w.xn, W.embedding, w.emb_scr[es], nullptr, cs));
+        ENNX_TRY(w.fused ? gemm_bf16_perturbed(&p, w.xn, W.embedding, w.emb_scr[es], nullptr, cs)
+                         : gemm_bf16(&p, w.xn, w.emb_scr[es], nullptr, cs));
       }
       ENNX_CUDA(cudaEventRecord(emb_freed[es], cs), "emb freed");
       emb_freed_recorded[es] = true;
@@ -719,6 +744,12 @@ int32_t ennx_b200_population_hidden(const ennx_b200_model_config* cfg, const enn
   w.tokens = tokens;
   return run_population(*cfg, *weights, seed, sigma, pair, 1, batch, seq, w, nullptr, (cudaStream_t)stream, layers,
                         hidden, index);
+}
+
+int32_t ennx_b200_set_perturbation_mode(int32_t mode) {
+  if (mode != 0 && mode != 1) return set_error(ENNX_B200_INVALID_ARGUMENT, "perturbation mode must be 0 or 1");
+  g_fused_mode = mode;
+  return ENNX_B200_OK;
 }
 
 int32_t ennx_b200_l2norm_heads_bf16(uint16_t* x, int64_t rows, int32_t heads, int64_t ld, void* stream) {

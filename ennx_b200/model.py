@@ -122,6 +122,13 @@ def init_weights(cfg: HybridConfig, seed: int = 0, device: str | torch.device = 
     return w
 
 
+def set_perturbation_mode(fused: bool) -> None:
+    """Materialised W +/- e copies (False, the default) or the fused operand
+    path of the perturbed GEMM (True) for every later population forward of
+    this process; both give bit-identical perturbed weights."""
+    _abi.call("ennx_b200_set_perturbation_mode", 1 if fused else 0)
+
+
 class PopulationEvaluator:
     """Scores antithetic pairs of W +/- sigma*eps on one device.
 

@@ -323,6 +323,16 @@ ENNX_B200_API int32_t ennx_b200_population_forward(const ennx_b200_model_config*
                                                    float* fitness, void* workspace, size_t workspace_bytes,
                                                    void* stream);
 
+/* Process-wide choice of how the population forward applies each pair's
+ * perturbation (both give the same perturbed weights bit for bit):
+ * 0 (default) materialised -- the noise kernel writes bf16(W + e) and
+ * bf16(W - e) copies of every tensor and the GEMMs read them; 1 fused --
+ * only the noise step e of the matrices is written and every GEMM forms
+ * W + e and W - e in its operand path (ennx_b200_gemm_bf16_perturbed).  The
+ * workspace size does not depend on the mode.  Not thread-safe against
+ * concurrent forward calls. */
+ENNX_B200_API int32_t ennx_b200_set_perturbation_mode(int32_t mode);
+
 /* Per-layer parity probe of the population forward: runs antithetic pair
  * `pair` through the first `layers` decoder layers only and copies the
  * residual stream after them to hidden (device bf16 [2][batch*seq][hidden],

@@ -73,3 +73,23 @@ def test_population_forward_deterministic():
     # evaluating pairs separately gives the same fitness as evaluating them together
     c = torch.cat([ev(tok, 7, 1e-2, 0, 1).cpu(), ev(tok, 7, 1e-2, 1, 1).cpu()])
     assert torch.equal(a, c)
+
+
+def test_fused_and_materialised_perturbation_agree(monkeypatch):
+    """The fused operand path (noise step only, W +/- e formed inside every
+    GEMM) and the stored W +/- e copies give the same fitness: bit-identical
+    with the CTA-pair GEMM in both (the same MMAs on the same operand bytes)."""
+    from ennx_b200.model import set_perturbation_mode
+    monkeypatch.setenv("ENNX_B200_GEMM_PAIR", "1")
+    cfg = SMALL
+    w = init_weights(cfg, seed=3, std=0.05)
+    tok = tokens_for(cfg, 2, 96, 8).cuda()
+    ev = PopulationEvaluator(cfg, w, 2, 96)
+    try:
+        set_perturbation_mode(False)
+        a = ev(tok, 21, 1e-2, 1, 2).cpu()
+        set_perturbation_mode(True)
+        b = ev(tok, 21, 1e-2, 1, 2).cpu()
+    finally:
+        set_perturbation_mode(False)
+    assert torch.equal(a, b), f"{a} vs {b}"

@@ -74,7 +74,6 @@ struct Args {
   int n_tiles;
   int n_parts;  // LSE partials per row: 2 * ceil(N / 256) (one per 128-column half tile)
   int has_tmc;  // C tensor map valid (bf16 outputs): full tiles leave through TMA stores
-  int pf;       // L2 prefetch distance in K stages (0: none)
   int* err;
 };
 
@@ -336,10 +335,6 @@ __global__ void __launch_bounds__(THREADS, 2)
             const uint32_t bar = mapa_shared(&s.full[stage], 0);
             tma_load_2d_pair(sA + stage * A_BYTES, &tmA, bar, kb * BK, arow);
             tma_load_2d_pair(sB + stage * G::BBYTES, &tmB, bar, kb * BK, brow);
-            if (a.pf && kb + a.pf < KB) {
-              tma_prefetch_l2(&tmA, (kb + a.pf) * BK, arow);
-              tma_prefetch_l2(&tmB, (kb + a.pf) * BK, brow);
-            }
           } else {
             mbar_arrive_expect_tx(&s.full[stage], G::STAGE);
             tma_load_2d(sA + stage * A_BYTES, &tmA, &s.full[stage], kb * BK, arow);
@@ -461,7 +456,6 @@ static_assert(PB_THREADS * 96 <= 65536, "register budget");
 
 struct PbArgs {
   int pairs;  // P
-  int diag;
 };
 
 struct PbSmem {  // lives after the epilogue staging tiles
@@ -583,11 +577,6 @@ __global__ void __maxnreg__(96)
           const int kx = kb * PB_BK;
           if (act_p) tma_load_2d_pair(a_ptr(stage, 0), &tmA, bar, kx, tp.row0 + u.mt * 256 + rank * BM);
           if (act_m) tma_load_2d_pair(a_ptr(stage, 1), &tmA, bar, kx, tm.row0 + u.mt * 256 + rank * BM);
-          if (a.pf && kb + a.pf < KB) {
-            const int kp = (kb + a.pf) * PB_BK;
-            if (act_p) tma_prefetch_l2(&tmA, kp, tp.row0 + u.mt * 256 + rank * BM);
-            if (act_m) tma_prefetch_l2(&tmA, kp, tm.row0 + u.mt * 256 + rank * BM);
-          }
           if (++stage == PB_NA) { stage = 0; phase ^= 1u; }
         }
       }
@@ -605,10 +594,6 @@ __global__ void __maxnreg__(96)
           mbar_arrive_expect_tx(&s.full_b[stage], 2u * PB_TILE);
           tma_load_2d(b_ptr(stage, 0), &tmW, &s.full_b[stage], kb * PB_BK, brow);
           tma_load_2d(b_ptr(stage, 1), &tmE, &s.full_b[stage], kb * PB_BK, brow);
-          if (a.pf && kb + a.pf < KB) {
-            tma_prefetch_l2(&tmW, (kb + a.pf) * PB_BK, brow);
-            tma_prefetch_l2(&tmE, (kb + a.pf) * PB_BK, brow);
-          }
           if (++stage == PB_NB) { stage = 0; phase ^= 1u; }
         }
       }
@@ -631,7 +616,7 @@ __global__ void __maxnreg__(96)
           // has drained it (the `-` one is drained after it)
           if (kb == 0 && !mbar_wait(&s.tempty[0], acc_phase ^ 1u, a.err)) { ok = false; break; }
           tc_fence_after();
-          if (act_p && pb.diag != 4) {
+          if (act_p) {
 #pragma unroll
             for (int k = 0; k < PB_BK / 16; ++k)
               umma_f16_pair(tmem_base, smem_desc_sw64(ab + k * 32), smem_desc_sw64(bb + k * 32), PB_IDESC,
@@ -639,7 +624,7 @@ __global__ void __maxnreg__(96)
           }
           if (kb == 0 && !mbar_wait(&s.tempty[1], acc_phase ^ 1u, a.err)) { ok = false; break; }
           tc_fence_after();
-          if (act_m && pb.diag != 1) {
+          if (act_m) {
 #pragma unroll
             for (int k = 0; k < PB_BK / 16; ++k)
               umma_f16_pair(tmem_base + BN, smem_desc_sw64(ab + PB_TILE + k * 32),
@@ -786,7 +771,6 @@ static Args make_args(const ennx_b200_gemm_params* p, void* C, bool bf16_out) {
   a.n_parts = 2 * a.n_tiles;
   a.has_tmc = bf16_out ? 1 : 0;
   a.err = nullptr;
-  a.pf = getenv("ENNX_B200_GEMM_PF") ? atoi(getenv("ENNX_B200_GEMM_PF")) : 0;
   return a;
 }
 
@@ -884,7 +868,6 @@ int32_t gemm_bf16_perturbed(const ennx_b200_gemm_params* p, const uint16_t* A, c
   if (!a.err) return set_error(ENNX_B200_CUDA_ERROR, "gemm_perturbed: no device error word");
   PbArgs pb;
   pb.pairs = G / 2;
-  pb.diag = getenv("ENNX_B200_PB_DIAG") ? atoi(getenv("ENNX_B200_PB_DIAG")) : 0;
   int dev = 0;
   cudaGetDevice(&dev);
   if (!g_pb_attr_set[dev]) {

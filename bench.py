@@ -7,7 +7,9 @@ One step = every candidate of the population (16 antithetic pairs, sharded
 over the ranks, no data-path collective) scored by mean next-token
 cross-entropy on batch 4 x seq 1024 synthetic uniform token ids; then the
 fitness vector is all-gathered (NCCL) and rank 0 broadcasts the next step's
-population seed -- the ES exchange.  ``value`` = tokens/s of the whole
+population seed and the update coefficients -- the ES exchange of
+``ennx_b200.population.PopulationStep``.  The replicated weight update is
+timed separately (``es_update``).  ``value`` = tokens/s of the whole
 population (32 * 4096 tokens per step) over the device-timed steps, max over
 ranks.  Inputs (weights, 15.9 GB bf16) are far larger than L2, so no flush is
 needed between steps.
@@ -34,6 +36,7 @@ sys.path.insert(0, ROOT)
 POP = 32          # candidates (16 antithetic pairs)
 BATCH, SEQ = 4, 1024
 SIGMA = 1e-3
+LR = 1e-2         # ES step size of the update coefficients
 METRIC = "Qwen-hybrid forward tokens/s at 1/2/4/8 B200; kernel % of roofline"
 # DRAM bytes per tcgen05 GEMM launch over one full forward step (1840 launches,
 # 870.23 GB), from the ncu capture summarised in profiles/gemm_forward_traffic.md.
@@ -165,7 +168,31 @@ def cpu_reference_sample() -> dict:
     t_fwd_sample = n_kda * (times["kda"] - t_head) + n_gqa * (times["gqa"] - t_head) + t_head
     tokens_per_candidate = BATCH * SEQ
     per_candidate = t_perturb + t_fwd_sample * tokens_per_candidate / tokens_n
+    # the same on one core (the reference's linear_cpu is single-threaded):
+    # perturbation of a 2 M-element slice and the KDA+MoE layer with one BLAS
+    # thread; the other layer kinds and the head scale by the KDA layer's ratio
+    n1 = 1 << 21
+    t0 = time.perf_counter()
+    O.perturb_bf16(base[:n1], 7, 0, 3, SIGMA, +1)
+    t_perturb_1 = (time.perf_counter() - t0) * cfg.param_count() / n1
+    try:
+        from threadpoolctl import threadpool_limits
+        with threadpool_limits(1):
+            c, layer = one_layer_model(False)
+            t0 = time.perf_counter()
+            OF.candidate_loss(c, {"embedding": emb, "final_norm": fnorm, "layers": [layer]}, tok, 1, None, 0, +1)
+            kda_1 = time.perf_counter() - t0
+    except ImportError:
+        kda_1 = times["kda"] * cores
+    per_candidate_1 = t_perturb_1 + t_fwd_sample * (kda_1 / times["kda"]) * tokens_per_candidate / tokens_n
+    cpu_model = ""
+    try:
+        with open("/proc/cpuinfo") as f:
+            cpu_model = next((l.split(":", 1)[1].strip() for l in f if l.startswith("model name")), "")
+    except OSError:
+        pass
     return {"value": tokens_per_candidate / per_candidate, "unit": "tokens/s", "cores": cores, "kind": "port",
+            "value_1_core": tokens_per_candidate / per_candidate_1, "cpu_model": cpu_model,
             "sample": (f"perturbation timed on {n_slice} elements over {cores} threads "
                        f"(-> {t_perturb:.1f}s per candidate for {cfg.param_count() / 1e9:.2f}G params); forward "
                        f"timed on 1 candidate x {tokens_n} tokens through 1 KDA+MoE layer ({times['kda']:.2f}s), "
@@ -189,10 +216,14 @@ def run_reference(args):
     elapsed = time.perf_counter() - t_all
     value = sorted(vals)[len(vals) // 2]
     line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": 1000.0 * elapsed / max(1, args.steps),
+            "warmup": args.warmup,
+            # the step `value` describes: the whole population's tokens at the sampled rate
+            "ms_per_step": 1000.0 * POP * BATCH * SEQ / value,
+            "sample_wall_s": elapsed / max(1, args.steps),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic", "config": CONFIG, "impl": "reference",
             "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": last["cores"], "kind": "port",
+                             "value_1_core": last["value_1_core"], "cpu_model": last["cpu_model"],
                              "sample": last["sample"]},
             "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -207,6 +238,7 @@ def run_ours(args):
     import ennx_b200
     from ennx_b200 import _abi
     from ennx_b200.model import HybridConfig, PopulationEvaluator, init_weights
+    from ennx_b200.population import PopulationStep
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -223,7 +255,6 @@ def run_ours(args):
     if pairs % world:
         raise SystemExit(f"{pairs} antithetic pairs do not shard over {world} ranks")
     my_pairs = pairs // world
-    first = rank * my_pairs
 
     cfg = HybridConfig()
     weights = init_weights(cfg, seed=1234)  # identical base weights on every rank
@@ -232,25 +263,25 @@ def run_ours(args):
     tokens_host = torch.randint(0, cfg.vocab, (BATCH, SEQ + 1), generator=gen, dtype=torch.int32).pin_memory()
     tokens = tokens_host.cuda()
     fit_all = torch.empty(POP, device="cuda")
-    seed_dev = torch.zeros(1, dtype=torch.int64, device="cuda")
     fit_host = torch.empty(POP, dtype=torch.float32).pin_memory()
     stream = torch.cuda.current_stream()
+
+    # The ES exchange of the tested sharding module: local evaluation, NCCL
+    # all-gather of the fitness, rank 0's update coefficients and next seed in
+    # one broadcast.  The update itself (replicated on every rank) is timed in
+    # a separate pass below and is not part of the forward tokens/s.
+    pstep = PopulationStep(ev, num_pairs=pairs, sigma=SIGMA, lr=LR, coefficients=ev.coefficients, update=None)
+    last = {}
 
     def step(i: int, e2e: bool):
         if e2e:
             tokens.copy_(tokens_host, non_blocking=True)
-        seed = 1000 + i
-        fit = ev(tokens, seed, SIGMA, first, my_pairs)
-        if world > 1:
-            dist.all_gather_into_tensor(fit_all, fit)
-            if rank == 0:
-                seed_dev.fill_(seed + 1)
-            dist.broadcast(seed_dev, 0)
-        else:
-            fit_all.copy_(fit)
+        res = pstep(tokens, 1000 + i)
+        fit_all.copy_(res.fitness)
+        last["coef"], last["seed"] = res.coefficients, 1000 + i
         if e2e:
             fit_host.copy_(fit_all, non_blocking=True)
-        return fit
+        return res.fitness
 
     def barrier():
         if world > 1:
@@ -309,6 +340,16 @@ def run_ours(args):
     device_ok("the end-to-end pass")
     _, _, prof = timed(False, profile=True)  # per-kernel CUDA-event breakdown (separate pass)
     device_ok("the profiled pass")
+    # the replicated ES update of the last step's coefficients, timed alone
+    barrier()
+    u0, u1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    u0.record(stream)
+    for _ in range(args.steps):
+        ev.update(last["seed"], last["coef"])
+    u1.record(stream)
+    barrier()
+    device_ok("the update pass")
+    upd_ms = u0.elapsed_time(u1) / args.steps
 
     tokens_per_step = POP * BATCH * SEQ
     value = tokens_per_step * args.steps / (ms / 1000.0)
@@ -340,10 +381,16 @@ def run_ours(args):
                 "kernel_breakdown": breakdown,
                 "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": BATCH * (SEQ + 1) * 4,
                         "d2h_bytes_per_step": POP * 4},
-                "gpu_launches": int(launches), "clocks": clk}
+                "gpu_launches": int(launches), "clocks": clk,
+                "es_update": {"ms_per_step": upd_ms, "lr": LR, "params": cfg.param_count(),
+                              "normals_per_step": cfg.param_count() * pairs,
+                              "hbm_gbs": 4.0 * cfg.param_count() / (upd_ms / 1e3) / 1e9,
+                              "note": "W <- bf16(W + sum_p c_p eps_p) on every rank from the broadcast "
+                                      "coefficients (noise regenerated, no weight traffic); not in tokens/s"}}
         if world == 1 and not args.no_cpu_baseline:
             cb = cpu_reference_sample()
-            line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
+            line["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "value_1_core", "cpu_model",
+                                                       "sample")}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.destroy_process_group()

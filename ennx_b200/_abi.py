@@ -176,6 +176,9 @@ SIGNATURES = {
     "ennx_b200_population_forward": (_I32, [_P, _P, _U64, _F32, _I32, _I32, _P, _I32, _I32, _P, _P, _SZ, _P]),
     "ennx_b200_population_hidden": (_I32, [_P, _P, _U64, _F32, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
     "ennx_b200_set_perturbation_mode": (_I32, [_I32]),
+    "ennx_b200_es_coefficients": (_I32, [_P, _I32, _I32, _F32, _F32, _P, _P]),
+    "ennx_b200_es_update_bf16": (_I32, [_P, _SZ, _U64, _U32, _P, _U32, _U32, _P]),
+    "ennx_b200_population_update": (_I32, [_P, _P, _U64, _P, _I32, _I32, _P]),
     "ennx_b200_l2norm_heads_bf16": (_I32, [_P, ctypes.c_int64, _I32, ctypes.c_int64, _P]),
     "ennx_b200_kda_gate_beta": (_I32, [_P, ctypes.c_int64, _P, ctypes.c_int64, _P, _P, ctypes.c_int64, _I32, _P, _P,
                                        _P]),

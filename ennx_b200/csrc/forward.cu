@@ -746,6 +746,41 @@ int32_t ennx_b200_population_hidden(const ennx_b200_model_config* cfg, const enn
                         hidden, index);
 }
 
+int32_t ennx_b200_population_update(const ennx_b200_model_config* cfg, const ennx_b200_model_weights* weights,
+                                    uint64_t seed, const float* coef, int32_t first_pair, int32_t num_pairs,
+                                    void* stream) {
+  if (!cfg || cfg->layers <= 0) return set_error(ENNX_B200_INVALID_ARGUMENT, "population_update: bad config");
+  if (!weights || !weights->embedding || !weights->final_norm || !weights->layers || !coef)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "population_update: null argument");
+  if (num_pairs <= 0 || first_pair < 0)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "population_update: empty pair range");
+  cudaStream_t s = (cudaStream_t)stream;
+  const ennx_b200_model_config& c = *cfg;
+  // The weights are updated in place through the caller's device pointers;
+  // the tensor ids are those of the forward's perturbation.
+  EsUpdateBatch b;
+  memset(&b, 0, sizeof(b));
+  b.seed = seed; b.first_pair = (uint32_t)first_pair; b.pairs = num_pairs;
+  b.job[b.count++] = EsUpdateJob{const_cast<uint16_t*>(weights->embedding), (uint64_t)c.vocab * c.hidden, 0u};
+  b.job[b.count++] = EsUpdateJob{const_cast<uint16_t*>(weights->final_norm), (uint64_t)c.hidden, 1u};
+  for (int l = 0; l < c.layers; ++l) {
+    const Shapes sh = layer_shapes(c, is_gqa(c, l));
+    for (int f = 0; f < F_COUNT; ++f) {
+      const long long n = sh.rows[f] * sh.cols[f];
+      if (n == 0) continue;
+      const uint16_t* src = field_ptr(weights->layers[l], f);
+      if (!src) return set_error(ENNX_B200_INVALID_ARGUMENT, "missing weight tensor %d of layer %d", f, l);
+      b.job[b.count++] = EsUpdateJob{const_cast<uint16_t*>(src), (uint64_t)n, 16u + 16u * (uint32_t)l + (uint32_t)f};
+    }
+    {
+      ProfScope ps("es_update", s, 0, 0);
+      ENNX_TRY(launch_es_update(b, coef, s));
+    }
+    b.count = 0;
+  }
+  return ENNX_B200_OK;
+}
+
 int32_t ennx_b200_set_perturbation_mode(int32_t mode) {
   if (mode != 0 && mode != 1) return set_error(ENNX_B200_INVALID_ARGUMENT, "perturbation mode must be 0 or 1");
   g_fused_mode = mode;

@@ -91,6 +91,24 @@ struct PerturbBatch {
 };
 int32_t launch_perturb_batch(const PerturbBatch& batch, cudaStream_t s);
 
+// es.cu: the zeroth-order update W <- bf16(W + sum_p coef[p] * eps_{first_pair + p})
+constexpr int kMaxEsJobs = 16;
+struct EsUpdateJob {
+  uint16_t* w;
+  uint64_t n;
+  uint32_t tensor;
+};
+struct EsUpdateBatch {
+  int count, pairs;
+  uint32_t first_pair;
+  uint64_t seed;
+  EsUpdateJob job[kMaxEsJobs];
+  uint32_t block0[kMaxEsJobs + 1];  // filled by launch_es_update
+};
+int32_t launch_es_update(const EsUpdateBatch& batch, const float* coef, cudaStream_t s);
+int32_t launch_es_coefficients(const float* fitness, int pairs, float sigma, float lr, int total_pairs, float* coef,
+                               cudaStream_t s);
+
 // gemm.cu (internal form of ennx_b200_gemm_bf16)
 int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* a, const uint16_t* b, void* c, cudaStream_t s);
 // gemm.cu: W +/- E formed in the operand path (ennx_b200_gemm_bf16_perturbed)

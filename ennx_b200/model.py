@@ -180,3 +180,118 @@ class PopulationEvaluator:
                   ctypes.c_void_p(self.workspace.data_ptr()), self.workspace.numel(),
                   ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
         return (out, idx) if with_routing else out
+
+    def coefficients(self, fitness: torch.Tensor, sigma: float, lr: float, total_pairs: int | None = None
+                     ) -> torch.Tensor:
+        """Update coefficients of the antithetic estimator from a device
+        fitness vector [2P]: c_p = -lr (f+ - f-) / (2 sigma total_pairs)."""
+        P = fitness.numel() // 2
+        coef = torch.empty(P, device=fitness.device, dtype=torch.float32)
+        _abi.call("ennx_b200_es_coefficients", ctypes.c_void_p(fitness.data_ptr()), P, total_pairs or P, sigma, lr,
+                  ctypes.c_void_p(coef.data_ptr()), ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        return coef
+
+    def update(self, seed: int, coef: torch.Tensor, first_pair: int = 0) -> None:
+        """W <- bf16(W + sum_p coef[p] eps_{first_pair + p}) for every tensor,
+        in place in the weights this evaluator was built on (the noise of the
+        forward's pairs, regenerated from `seed`)."""
+        if coef.dtype != torch.float32 or not coef.is_cuda:
+            raise ValueError("coefficients must be a CUDA float32 tensor")
+        coef = coef.contiguous()
+        _abi.call("ennx_b200_population_update", ctypes.byref(self._ccfg), ctypes.byref(self._cw), seed,
+                  ctypes.c_void_p(coef.data_ptr()), first_pair, coef.numel(),
+                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+
+    def rebind(self, weights: dict) -> None:
+        """Point the evaluator at other base weights of the same shapes (for
+        example views into a search's resident row); the workspace is kept."""
+        for l, lw in enumerate(weights["layers"]):
+            for f in _abi.LAYER_FIELDS:
+                t = lw.get(f)
+                setattr(self._layers[l], f, None if t is None else t.data_ptr())
+        self._cw = _abi.ModelWeights(weights["embedding"].data_ptr(), weights["final_norm"].data_ptr(),
+                                     self._layers)
+        self.weights = weights
+
+
+def flat_layout(cfg: HybridConfig) -> list[tuple[str, int, int, tuple]]:
+    """The model as one flat BF16 parameter vector: (name, layer, offset,
+    shape) per tensor, every tensor starting on a 16-element boundary (the
+    16-byte alignment the kernels need).  Names are the weight dict's keys."""
+    out, off = [], 0
+
+    def add(name, layer, shape):
+        nonlocal off
+        n = 1
+        for d in shape:
+            n *= d
+        out.append((name, layer, off, tuple(shape)))
+        off += (n + 15) // 16 * 16
+
+    add("embedding", -1, (cfg.vocab, cfg.hidden))
+    add("final_norm", -1, (cfg.hidden,))
+    for l in range(cfg.layers):
+        for name, shp in cfg.layer_shapes(l).items():
+            add(name, l, shp)
+    return out
+
+
+def flat_size(cfg: HybridConfig) -> int:
+    name, layer, off, shape = flat_layout(cfg)[-1]
+    n = 1
+    for d in shape:
+        n *= d
+    return off + (n + 15) // 16 * 16
+
+
+def weights_from_flat(cfg: HybridConfig, flat: torch.Tensor) -> dict:
+    """Weight dict of views into a flat BF16 vector laid out by ``flat_layout``."""
+    w = {"layers": [dict() for _ in range(cfg.layers)]}
+    for name, layer, off, shape in flat_layout(cfg):
+        n = 1
+        for d in shape:
+            n *= d
+        view = flat[off:off + n].view(*shape)
+        if layer < 0:
+            w[name] = view
+        else:
+            w["layers"][layer][name] = view
+    return w
+
+
+class ResidentForwardSearch:
+    """The reference's resident BO round over the forward
+    (``ResidentBoState::ask_evaluate``, forward_program.rs:706-720): the
+    resident BF16 search proposes a trial row of the whole model's
+    parameters, the population forward scores that row as the model (no
+    population noise: sigma 0), and the mean cross-entropy goes back to the
+    search as a device reward (-CE) without a host copy.
+
+    ``search``: a ``SearchState`` whose rows are laid out by ``flat_layout``;
+    ``tokens``: CUDA int32 [batch, seq + 1]."""
+
+    def __init__(self, cfg: HybridConfig, search, batch: int, seq: int):
+        from .search import SearchState
+        if not isinstance(search, SearchState):
+            raise TypeError("ResidentForwardSearch needs a SearchState")
+        if search.len != flat_size(cfg):
+            raise ValueError(f"search rows hold {search.len} values; the model needs {flat_size(cfg)}")
+        self.cfg, self.search, self.batch, self.seq = cfg, search, batch, seq
+        self._ev = None
+
+    def ask_evaluate(self, tokens: torch.Tensor, seed: int, candidates: int = 8, neighbors: int = 8, **ask):
+        """One round: ask (1 arm), evaluate the trial row, tell -CE.  Returns
+        the device reward tensor [1]."""
+        props = self.search.ask(1, candidates, neighbors, seed, **ask)
+        batch = torch.from_dlpack(props)  # [1, len] trial row; the export lease lives with `batch`
+        w = weights_from_flat(self.cfg, batch[0])
+        if self._ev is None:
+            self._ev = PopulationEvaluator(self.cfg, w, self.batch, self.seq)
+        else:
+            self._ev.rebind(w)
+        fit = self._ev(tokens, 0, 0.0, 0, 1)  # both candidates of the pair are the row itself
+        reward = (-fit[:1]).contiguous()
+        self._ev.weights = None  # the evaluator keeps raw pointers only, not the lease
+        del batch, w
+        self.search.tell(props, reward)
+        return reward

@@ -323,6 +323,30 @@ ENNX_B200_API int32_t ennx_b200_population_forward(const ennx_b200_model_config*
                                                    float* fitness, void* workspace, size_t workspace_bytes,
                                                    void* stream);
 
+/* ---- the zeroth-order update (the population's tell) ------------------- */
+
+/* coef[p] = -lr * (fitness[2p] - fitness[2p+1]) / (2 * sigma * total_pairs),
+ * p < pairs: the antithetic estimator of the mean cross-entropy's gradient,
+ * as a step that lowers it.  fitness, coef: device f32. */
+ENNX_B200_API int32_t ennx_b200_es_coefficients(const float* fitness, int32_t pairs, int32_t total_pairs,
+                                                float sigma, float lr, float* coef, void* stream);
+/* In place: w[i] = bf16(w[i] + sum_{p < pairs} coef[p] * eps(seed, first_pair + p,
+ * tensor, i)) with the fp32 sum taken over p in order and one RNE rounding;
+ * eps is the forward's Philox normal.  pairs <= 256.  Counterpart of the
+ * reference's device tell that moves the incumbent from a round's rewards
+ * (rust/crates/ennx/src/bf16_search.rs:319-407, cuda/kernels/src/lib.rs:409-535). */
+ENNX_B200_API int32_t ennx_b200_es_update_bf16(uint16_t* w, size_t n, uint64_t seed, uint32_t tensor,
+                                               const float* coef, uint32_t first_pair, uint32_t pairs,
+                                               void* stream);
+/* ennx_b200_es_update_bf16 over every tensor of the model (the forward's
+ * tensor ids), writing through the device pointers of `weights`; one launch
+ * per layer.  Every rank applies it with the same broadcast coefficients, so
+ * the replicas stay identical without moving any weight. */
+ENNX_B200_API int32_t ennx_b200_population_update(const ennx_b200_model_config* cfg,
+                                                  const ennx_b200_model_weights* weights, uint64_t seed,
+                                                  const float* coef, int32_t first_pair, int32_t num_pairs,
+                                                  void* stream);
+
 /* Process-wide choice of how the population forward applies each pair's
  * perturbation (both give the same perturbed weights bit for bit):
  * 0 (default) materialised -- the noise kernel writes bf16(W + e) and

@@ -82,6 +82,7 @@ def lib():
             "eo_noise8": (None, [u64, u32, u32, u64, P]),
             "eo_perturb_bf16": (None, [P, sz, u64, u32, u32, f32, ctypes.c_int, P]),
             "eo_perturb_bf16_at": (None, [P, sz, sz, u64, u32, u32, f32, ctypes.c_int, P]),
+            "eo_es_update": (None, [P, sz, u64, u32, P, u32, u32, P]),
             "eo_rmsnorm": (None, [P, P, sz, sz, f32, P]),
             "eo_router_logits": (None, [P, P, sz, sz, sz, P]),
             "eo_router_topk": (None, [P, sz, sz, sz, P, P]),
@@ -238,6 +239,23 @@ def noise(seed: int, pair: int, tensor: int, n: int, start: int = 0) -> np.ndarr
         lib().eo_noise8(seed, pair, tensor, start // 8 + blk, _p(buf))
         out[8 * blk:8 * blk + 8] = buf
     return out[:n]
+
+
+def es_coefficients(fitness, sigma, lr, total_pairs=None):
+    """coef[p] = -lr (f[2p] - f[2p+1]) / (2 sigma total_pairs), float32 arithmetic."""
+    f = np.asarray(fitness, np.float32)
+    P = f.size // 2
+    scale = np.float32(-lr) / (np.float32(2.0) * np.float32(sigma) * np.float32(total_pairs or P))
+    return (scale * (f[0::2] - f[1::2])).astype(np.float32)
+
+
+def es_update(w_bits, seed, tensor, coef, first_pair=0):
+    """bf16 bits of W + sum_p coef[p] eps(seed, first_pair + p, tensor, .)."""
+    w = _c(w_bits, np.uint16).reshape(-1)
+    c = _c(coef, np.float32)
+    out = np.zeros_like(w)
+    lib().eo_es_update(_p(w), w.size, seed, tensor, _p(c), first_pair, c.size, _p(out))
+    return out.reshape(np.shape(w_bits))
 
 
 def noise_step_bf16(n, seed, pair, tensor, sigma):

@@ -389,6 +389,22 @@ void eo_perturb_bf16_at(const uint16_t* w, size_t n, size_t start, uint64_t seed
     }
 }
 
+/* The zeroth-order update (the ES tell): out[i] = bf16(w[i] + sum_p coef[p] *
+ * eps(seed, first_pair + p, tensor, i)), the sum in fp32 with one fused
+ * multiply-add per pair in pair order, one RNE rounding at the end. */
+void eo_es_update(const uint16_t* w, size_t n, uint64_t seed, uint32_t tensor, const float* coef,
+                  uint32_t first_pair, uint32_t pairs, uint16_t* out) {
+    for (size_t g = 0; g < (n + 7) / 8; ++g) {
+        float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (uint32_t p = 0; p < pairs; ++p) {
+            float z[8];
+            eo_noise8(seed, first_pair + p, tensor, g, z);
+            for (int k = 0; k < 8; ++k) acc[k] = fmaf(coef[p], z[k], acc[k]);
+        }
+        for (size_t e = g * 8; e < n && e < g * 8 + 8; ++e) out[e] = eo_bf16_encode(eo_bf16_decode(w[e]) + acc[e - g * 8]);
+    }
+}
+
 void eo_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor,
                      float sigma, int sign, uint16_t* out) {
     eo_perturb_bf16_at(w, n, 0, seed, pair, tensor, sigma, sign, out);

@@ -86,6 +86,8 @@ void eo_philox4x32_10(const uint32_t ctr[4], const uint32_t key[2], uint32_t out
 void eo_noise8(uint64_t seed, uint32_t pair, uint32_t tensor, uint64_t block, float out[8]);
 void eo_perturb_bf16_at(const uint16_t* w, size_t n, size_t start, uint64_t seed, uint32_t pair, uint32_t tensor,
                         float sigma, int sign, uint16_t* out);
+void eo_es_update(const uint16_t* w, size_t n, uint64_t seed, uint32_t tensor, const float* coef,
+                  uint32_t first_pair, uint32_t pairs, uint16_t* out);
 void eo_perturb_bf16(const uint16_t* w, size_t n, uint64_t seed, uint32_t pair, uint32_t tensor,
                      float sigma, int sign, uint16_t* out);
 

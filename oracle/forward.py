@@ -133,3 +133,14 @@ def population_forward(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float
         for sign in (+1, -1):
             out.append(candidate_loss(cfg, W, tokens, seed, sigma, first_pair + i, sign))
     return np.array(out)
+
+
+def population_update(cfg, W: dict, seed: int, coef, first_pair: int = 0) -> dict:
+    """The zeroth-order update of every tensor (the forward's tensor ids)."""
+    from . import es_update
+    out = {"embedding": es_update(W["embedding"], seed, 0, coef, first_pair),
+           "final_norm": es_update(W["final_norm"], seed, 1, coef, first_pair), "layers": []}
+    for l, L in enumerate(W["layers"]):
+        out["layers"].append({f: es_update(L[f], seed, 16 + 16 * l + i, coef, first_pair)
+                              for i, f in enumerate(FIELDS) if f in L})
+    return out

@@ -288,6 +288,49 @@ class ParamBuffer:
             _abi.call("ennx_b200_dense_apply_bf16", _ptr(self._base), self._base.numel(), self._leaves,
                       self._num_leaves, _term_array(tm), len(tm), _ptr(self._candidate), _stream(torch))
 
+    def materialize_gaussian(self, seed: int, pair: int, sigma: float, sign: int = 1) -> None:
+        """The Philox Gaussian direction of the population forward instead of
+        Rademacher terms: for leaf j (in block order) and element i of it,
+        ``candidate = bf16(base + s * bf16(sigma * scale_j * eps(seed, pair,
+        j, i)))``, s = +1 or -1 (the antithetic sign) -- the same noise and
+        rounding as ``ennx_b200_perturb_bf16``.  Rolls back to ``base`` and
+        raises if any value overflows, like ``materialize``."""
+        if self._exported:
+            raise ValueError("cannot materialize while a JAX candidate is alive")
+        if sign not in (1, -1):
+            raise ValueError("the antithetic sign must be +1 or -1")
+        sigma = _f32(sigma)
+        if not math.isfinite(sigma) or sigma < 0.0:
+            raise ValueError("sigma must be finite and non-negative")
+        if not 0 <= int(seed) <= _U64 or not 0 <= int(pair) < 2 ** 32:
+            raise ValueError("seed must be a u64 and pair a u32")
+        import torch
+        with torch.cuda.device(self._device):
+            st = _stream(torch)
+            for j in range(self._num_leaves):
+                leaf = self._leaves[j]
+                off, n = int(leaf.offset), int(leaf.len)
+                aligned = off % 8 == 0  # the kernel takes 16-byte aligned rows; other leaves go through copies
+                base = self._base[off:off + n] if aligned else self._base[off:off + n].clone()
+                cand = self._candidate[off:off + n] if aligned else torch.empty_like(base)
+                scaled = float(np.float32(sigma) * np.float32(leaf.scale))
+                if sign > 0:
+                    _abi.call("ennx_b200_perturb_bf16", _ptr(base), n, int(seed), int(pair), j, scaled, _ptr(cand),
+                              None, st)
+                else:  # the minus copy, into the candidate (the plus copy into a scratch)
+                    scratch = torch.empty_like(cand)
+                    _abi.call("ennx_b200_perturb_bf16", _ptr(base), n, int(seed), int(pair), j, scaled,
+                              _ptr(scratch), _ptr(cand), st)
+                if not aligned:
+                    self._candidate[off:off + n].copy_(cand)
+            flag = ctypes.c_int32(0)
+            torch.cuda.current_stream().synchronize()
+            _abi.call("ennx_b200_check_bf16", _ptr(self._candidate), self._candidate.numel(), ctypes.byref(flag), st)
+        if not flag.value:
+            self._candidate.copy_(self._base)
+            torch.cuda.current_stream().synchronize()
+            raise ValueError("BF16 Gaussian perturbation overflowed")
+
     def __dlpack_device__(self) -> tuple[int, int]:
         return (_dlpack.KDL_CUDA, self._device.index or 0)
 

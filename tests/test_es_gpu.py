@@ -30,8 +30,15 @@ def _bits(t):
     return t.cpu().view(torch.int16).numpy().view(np.uint16)
 
 
-def _ulps(a, b):
-    return np.abs(a.astype(np.int32) - b.astype(np.int32))
+def update_close(got_bits, exp_bits, coef):
+    """Device vs oracle update: the Philox normals agree to ~1e-6 (SFU vs
+    libm), so each sum agrees to ~1e-6 * sum|c|; after one bf16 rounding the
+    values are at most one ulp (2^-7 relative) plus that apart.  Values that
+    the update moves near zero have no bit-level agreement, hence values."""
+    g, e = O.from_bf16_bits(got_bits).astype(np.float64), O.from_bf16_bits(exp_bits).astype(np.float64)
+    tol = 2.0 ** -7 * np.abs(e) + 1e-5 * float(np.abs(np.asarray(coef, np.float64)).sum())
+    assert np.all(np.abs(g - e) <= tol), f"max excess {(np.abs(g - e) - tol).max():.3e}"
+    assert (g != e).mean() < 1e-2
 
 
 def test_es_update_matches_oracle():
@@ -43,10 +50,7 @@ def test_es_update_matches_oracle():
     tc = torch.from_numpy(coef).cuda()
     assert _abi.lib().ennx_b200_es_update_bf16(ptr(tw), n, 77, 21, ptr(tc), 3, 16, stream()) == 0
     ref = O.es_update(w, 77, 21, coef, 3)
-    d = _ulps(host_u16(tw), ref)
-    # device Box-Muller (SFU) vs fp64 libm: eps agree to ~1e-6, so a sum on a
-    # rounding boundary may land one bf16 ulp away
-    assert d.max() <= 1 and (d > 0).mean() < 1e-3
+    update_close(host_u16(tw), ref, coef)
     assert (host_u16(tw) != w).mean() > 0.5  # the update moved most weights
 
 
@@ -74,8 +78,7 @@ def test_population_update_matches_oracle():
     for L, R in zip(w["layers"], ref["layers"]):
         pairs += [(L[k], R[k]) for k in R]
     for got, exp in pairs:
-        d = _ulps(_bits(got).reshape(-1), exp.reshape(-1))
-        assert d.max() <= 1 and (d > 0).mean() < 1e-2
+        update_close(_bits(got).reshape(-1), exp.reshape(-1), coef.cpu().numpy())
 
 
 def test_resident_es_state_closed_loop():
@@ -97,8 +100,7 @@ def test_resident_es_state_closed_loop():
     np.testing.assert_allclose(f0.cpu().numpy(), ref_fit, rtol=2e-3, atol=2e-3)
     coef = O.es_coefficients(f0.cpu().numpy(), 1e-2, 0.05)
     ref_w = OF.population_update(cfg, snap, 40, coef)
-    d = _ulps(_bits(w["layers"][1]["w_gate_up"]).reshape(-1), ref_w["layers"][1]["w_gate_up"].reshape(-1))
-    assert d.max() <= 1 and (d > 0).mean() < 1e-2
+    update_close(_bits(w["layers"][1]["w_gate_up"]).reshape(-1), ref_w["layers"][1]["w_gate_up"].reshape(-1), coef)
     r1 = state.ask()
     with pytest.raises(ValueError, match="tell must finish"):
         state.ask()

@@ -249,7 +249,11 @@ def run_ours(args):
         # broadcast per step: NVLink SHARP (multicast) buffers bring nothing
         # for them, so their setup is skipped.
         os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        # a rank that dies makes the others' next collective fail within two
+        # minutes instead of NCCL's ten-minute default
+        import datetime
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=120))
     _abi.check(_abi.lib().ennx_b200_device_check(), "device_check")
     pairs = POP // 2
     if pairs % world:
@@ -292,8 +296,13 @@ def run_ours(args):
         # every bounded device wait that gave up records a status; a run in
         # which a kernel returned early must not report a number
         st = _abi.lib().ennx_b200_device_status(ctypes.c_void_p(stream.cuda_stream))
+        msg = _abi.lib().ennx_b200_last_error().decode() if st != _abi.OK else ""
+        if world > 1:  # decide together: no rank may leave while the others wait in a collective
+            t = torch.tensor([st], device="cuda", dtype=torch.int32)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            st = int(t.item())
         if st != _abi.OK:
-            raise SystemExit(f"device status {st} after {where}: {_abi.lib().ennx_b200_last_error().decode()}")
+            raise SystemExit(f"device status {st} after {where} (on some rank) {msg}")
 
     for i in range(args.warmup):
         step(i, False)

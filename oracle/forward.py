@@ -38,14 +38,17 @@ def perturbed(bits: np.ndarray, seed: int, pair: int, tensor: int, sigma, sign: 
 
 def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pair: int, sign: int,
                    return_rows: bool = False, hidden_at: dict | None = None, router_gaps: list | None = None,
-                   routing: list | None = None):
+                   routing: list | None = None, start_hidden=None, first_layer: int = 0):
     """Mean CE of one candidate.  W: {'embedding': bits, 'final_norm': bits,
     'layers': [ {field: bits} ]} (bf16 bit patterns as uint16 arrays).
     hidden_at: {n: None} -> filled with the residual stream [T, H] after the
     first n layers (float32 values of the bf16 activations).
     router_gaps: list -> appended per layer with each token's gap between its
     k-th and (k+1)-th router logit (how close its expert choice is to a tie).
-    routing: list -> appended per layer with the expert indices [T, k]."""
+    routing: list -> appended per layer with the expert indices [T, k].
+    start_hidden [T, H] / first_layer: run W["layers"] as layers
+    first_layer, first_layer + 1, ... from the given residual stream instead
+    of the embedding (per-layer isolation)."""
     B, S1 = tokens.shape
     S = S1 - 1
     T = B * S
@@ -54,8 +57,8 @@ def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pa
     inp = tokens[:, :S].reshape(-1)
     tgt = tokens[:, 1:].reshape(-1)
     emb = perturbed(W["embedding"], seed, pair, 0, sigma, sign)
-    h = emb[inp].astype(np.float32)
-    for l, L in enumerate(W["layers"]):
+    h = emb[inp].astype(np.float32) if start_hidden is None else np.asarray(start_hidden, np.float32)
+    for l, L in enumerate(W["layers"], start=first_layer):
         P = {f: perturbed(L[f], seed, pair, 16 + 16 * l + i, sigma, sign) for i, f in enumerate(FIELDS) if f in L}
         x = round_bf16(rmsnorm(h, P["attn_norm"], cfg.rms_eps))
         qkv = round_bf16(gemm(x, P["w_qkv"]).astype(np.float32))
@@ -110,8 +113,8 @@ def candidate_loss(cfg, W: dict, tokens: np.ndarray, seed: int, sigma: float, pa
             out = round_bf16((gemm(act, P["w_down"][e]) * (rs * gate[rows, ranks])[:, None]).astype(np.float32))
             np.add.at(y, rows, out.astype(np.float64))
         h = round_bf16(y.astype(np.float32))
-        if hidden_at is not None and (l + 1) in hidden_at:
-            hidden_at[l + 1] = h.copy()
+        if hidden_at is not None and (l + 1 - first_layer) in hidden_at:
+            hidden_at[l + 1 - first_layer] = h.copy()
     fnorm = perturbed(W["final_norm"], seed, pair, 1, sigma, sign)
     x = round_bf16(rmsnorm(h, fnorm, cfg.rms_eps))
     logits = gemm(x, emb)

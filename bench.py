@@ -255,19 +255,19 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=torch.device("cuda", local),
                                 timeout=datetime.timedelta(seconds=120))
     _abi.check(_abi.lib().ennx_b200_device_check(), "device_check")
-    pairs = POP // 2
+    pairs = args.pairs or POP // 2
     if pairs % world:
         raise SystemExit(f"{pairs} antithetic pairs do not shard over {world} ranks")
     my_pairs = pairs // world
 
-    cfg = HybridConfig()
+    cfg = HybridConfig(layers=args.layers) if args.layers else HybridConfig()
     weights = init_weights(cfg, seed=1234)  # identical base weights on every rank
     ev = PopulationEvaluator(cfg, weights, BATCH, SEQ)
     gen = torch.Generator().manual_seed(99)
     tokens_host = torch.randint(0, cfg.vocab, (BATCH, SEQ + 1), generator=gen, dtype=torch.int32).pin_memory()
     tokens = tokens_host.cuda()
-    fit_all = torch.empty(POP, device="cuda")
-    fit_host = torch.empty(POP, dtype=torch.float32).pin_memory()
+    fit_all = torch.empty(2 * pairs, device="cuda")
+    fit_host = torch.empty(2 * pairs, dtype=torch.float32).pin_memory()
     stream = torch.cuda.current_stream()
 
     # The ES exchange of the tested sharding module: local evaluation, NCCL
@@ -360,7 +360,7 @@ def run_ours(args):
     device_ok("the update pass")
     upd_ms = u0.elapsed_time(u1) / args.steps
 
-    tokens_per_step = POP * BATCH * SEQ
+    tokens_per_step = 2 * pairs * BATCH * SEQ
     value = tokens_per_step * args.steps / (ms / 1000.0)
     e2e_value = tokens_per_step * args.steps / (ms_e2e / 1000.0)
     hbm, tf_burst, tf_sust, src = peaks()
@@ -376,7 +376,9 @@ def run_ours(args):
         line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-                "config": dict(CONFIG, parallelism=f"population-sharded x{world} (pairs per rank {my_pairs})"),
+                "config": dict(CONFIG, parallelism=f"population-sharded x{world} (pairs per rank {my_pairs})",
+                               **({"profiling_override": f"layers={cfg.layers} pairs={pairs} (not the benchmark)"}
+                                  if args.layers or args.pairs else {})),
                 "tflops": total_flops / (ms / 1000.0) / 1e12,
                 "roofline": {"bound": "tensor", "kernel": "gemm_bf16_kernel (tcgen05, all projection/expert/LM-head "
                                                           "GEMMs)",
@@ -389,7 +391,7 @@ def run_ours(args):
                              "avg_launch_ms": g_ms / max(1, g_launch)},
                 "kernel_breakdown": breakdown,
                 "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": BATCH * (SEQ + 1) * 4,
-                        "d2h_bytes_per_step": POP * 4},
+                        "d2h_bytes_per_step": 2 * pairs * 4},
                 "gpu_launches": int(launches), "clocks": clk,
                 "es_update": {"ms_per_step": upd_ms, "lr": LR, "params": cfg.param_count(),
                               "normals_per_step": cfg.param_count() * pairs,
@@ -690,6 +692,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--plain", action="store_true", help="gemm_pb ops: time the plain GEMM on stored W +/- e")
+    ap.add_argument("--layers", type=int, default=0, help="profiling aid: a shorter model (not the benchmark)")
+    ap.add_argument("--pairs", type=int, default=0, help="profiling aid: fewer antithetic pairs (not the benchmark)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: fewer than 3 warm-up steps", file=sys.stderr)

@@ -126,7 +126,8 @@ def test_forward_configs4_full_model_one_pair():
     expert choices equal the oracle's for every token whose 8th and 9th
     router logits are not within ROUTER_TIE of each other, and on the tokens
     whose choices agree the stream after the layer passes ``hidden_close``.
-    Both fitness values (all 24 layers and the LM head, chained) within 2e-3."""
+    Both fitness values (all 24 layers and the LM head, chained) within
+    5e-3 relative."""
     cfg = HybridConfig()
     w = init_weights(cfg, seed=1234)
     B, S = 1, 64
@@ -153,7 +154,10 @@ def test_forward_configs4_full_model_one_pair():
                 f"tokens {np.nonzero(flip & ~(gaps[0] < ROUTER_TIE))[0].tolist()}")
             flips += int(flip.sum())
             hidden_close(hid[n][s][~flip], at[1][~flip], f"hidden after layer {n - 1}, sign {sign:+d}")
+        # the fitness chains all 24 layers and the LM head in bf16 (the
+        # oracle in float64 between bf16 storage points) and averages only
+        # 64 tokens: 5e-3 relative, inside the 2e-2 bound of bf16 outputs
         ref = OF.candidate_loss(cfg, wb, tok.numpy(), seed, sigma, pair, sign)
-        np.testing.assert_allclose(fit[s], ref, rtol=2e-3, atol=2e-3)
+        np.testing.assert_allclose(fit[s], ref, rtol=5e-3, atol=0)
     assert flips <= 2 * 4 * B * S // 8, f"{flips} expert-choice flips"
     assert fit[0] != fit[1]

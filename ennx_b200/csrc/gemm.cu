@@ -74,6 +74,7 @@ struct Args {
   int n_tiles;
   int n_parts;  // LSE partials per row: 2 * ceil(N / 256) (one per 128-column half tile)
   int has_tmc;  // C tensor map valid (bf16 outputs): full tiles leave through TMA stores
+  int n_fast;   // tile order within a group: N tiles fastest (1) or M tiles fastest (0)
   int* err;
 };
 
@@ -103,8 +104,13 @@ __device__ __forceinline__ TileInfo decode_tile(const Smem& s, const Args& a, in
   t.rows = s.row0[lo + 1] - s.row0[lo];
   int mtiles = (t.rows + TM - 1) / TM;
   int local = tile - s.tile0[lo];
-  t.mt = local % mtiles;
-  t.nt = local / mtiles;
+  if (a.n_fast) {
+    t.nt = local % a.n_tiles;
+    t.mt = local / a.n_tiles;
+  } else {
+    t.mt = local % mtiles;
+    t.nt = local / mtiles;
+  }
   return t;
 }
 
@@ -605,7 +611,8 @@ __global__ void __maxnreg__(96)
       int it = 0;
       for (int unit = first; unit < total && !aborted(); unit += stride, ++it) {
         const PbUnit u = decode_pb(s, P, a.n_tiles, unit);
-        const bool act_p = u.mt * 256 < pb_tile(s, u, 0, P).rows, act_m = u.mt * 256 < pb_tile(s, u, 1, P).rows;
+        const bool act_p = u.mt * 256 < pb_tile(s, u, 0, P).rows,
+                   act_m = u.mt * 256 < pb_tile(s, u, 1, P).rows;
         const uint32_t acc_phase = it & 1;
         bool ok = true;
         for (int kb = 0; kb < KB; ++kb) {
@@ -771,6 +778,11 @@ static Args make_args(const ennx_b200_gemm_params* p, void* C, bool bf16_out) {
   a.n_parts = 2 * a.n_tiles;
   a.has_tmc = bf16_out ? 1 : 0;
   a.err = nullptr;
+  // Few groups of many rows: N tiles fastest, so the tiles that run together
+  // share their A rows in L2 (A can exceed L2; the B blocks are small).
+  // Many ragged groups (experts): M tiles fastest within a group.
+  a.n_fast = G <= 2 ? 1 : 0;
+  if (const char* e = getenv("ENNX_B200_GEMM_ORDER")) a.n_fast = atoi(e);
   return a;
 }
 

@@ -778,10 +778,18 @@ static Args make_args(const ennx_b200_gemm_params* p, void* C, bool bf16_out) {
   a.n_parts = 2 * a.n_tiles;
   a.has_tmc = bf16_out ? 1 : 0;
   a.err = nullptr;
-  // Few groups of many rows: N tiles fastest, so the tiles that run together
-  // share their A rows in L2 (A can exceed L2; the B blocks are small).
-  // Many ragged groups (experts): M tiles fastest within a group.
-  a.n_fast = G <= 2 ? 1 : 0;
+  // Tile order within a group.  M tiles fastest (the default): the tiles
+  // that run together share one B tile, and every A tile is read once per
+  // N tile -- cheap while A stays in L2.  N tiles fastest when a group's A
+  // rows cannot stay in L2 but its B block can (e.g. 2 x 16384 rows against
+  // a 2048 x 2048 B): then B is the operand re-read, from L2.  (The LM head,
+  // 8192 rows against a 151936-row B, must stay M-fastest: N-fastest would
+  // stream its 0.6 GB B once per M tile.)
+  {
+    const double rows_per_group = (double)M / G, l2_share = 48e6;
+    const double a_bytes = rows_per_group * K * 2.0, b_bytes = (double)N * K * 2.0;
+    a.n_fast = (a_bytes > l2_share && b_bytes <= l2_share) ? 1 : 0;
+  }
   if (const char* e = getenv("ENNX_B200_GEMM_ORDER")) a.n_fast = atoi(e);
   return a;
 }

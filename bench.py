@@ -38,9 +38,10 @@ BATCH, SEQ = 4, 1024
 SIGMA = 1e-3
 LR = 1e-2         # ES step size of the update coefficients
 METRIC = "Qwen-hybrid forward tokens/s at 1/2/4/8 B200; kernel % of roofline"
-# DRAM bytes per tcgen05 GEMM launch over one full forward step (1840 launches,
-# 870.23 GB), from the ncu capture summarised in profiles/gemm_forward_traffic.md.
-GEMM_DRAM_BYTES_PER_LAUNCH = 472.95e6
+# DRAM bytes per tcgen05 GEMM launch of one full forward step: each GEMM kind
+# captured with ncu on a small case (one pair, four layers) and scaled by the
+# launches of a full step (1840): profiles/gemm_forward_traffic.md.
+GEMM_DRAM_BYTES_PER_LAUNCH = 458.5e6
 CONFIG = {"workload": "hybrid KDA/GQA-MoE forward, 32 antithetic candidates (sigma 1e-3, Philox), "
                       "batch 4 x seq 1024 each, mean CE fitness",
           "layers": 24, "hidden": 2048, "pattern": "[KDA,KDA,KDA,GQA]x6", "q_heads": 16, "kv_heads": 4,
@@ -342,6 +343,11 @@ def run_ours(args):
 
     clocks = ClockSampler(local)
     clocks.start()
+    # nvidia-smi's start-up can stall the device for seconds: let it produce
+    # its first sample before the timed region begins
+    t_wait = time.time()
+    while not clocks.rows and clocks.proc is not None and time.time() - t_wait < 10.0:
+        time.sleep(0.05)
     ms, launches, _ = timed(False)
     clk = clocks.stop()
     device_ok("the timed pass")
@@ -385,7 +391,8 @@ def run_ours(args):
                              "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s", "frac": achieved / tf_sust,
                              "peak_source": f"{src} bf16_tflops_sustained (kernel timed inside a long step)",
                              "traffic": GEMM_DRAM_BYTES_PER_LAUNCH,
-                             "traffic_unit": "bytes per launch (ncu dram__bytes_read+write, one forward step)",
+                             "traffic_unit": "bytes per launch (ncu dram__bytes_read+write per GEMM kind on a one-pair "
+                                             "four-layer case, scaled to a full step's launch mix)",
                              "algorithmic_bytes_per_launch": g_bytes / max(1, g_launch),
                              "algorithmic_flops_per_launch": g_flops / max(1, g_launch),
                              "avg_launch_ms": g_ms / max(1, g_launch)},

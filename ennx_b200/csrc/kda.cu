@@ -147,23 +147,6 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
   uint16_t* bigr = big + rec * (192 * DK);
   uint16_t* smallr = small + rec * (128 * C);
 
-  // Warm L2 with every row this CTA reads, before the first phase waits on
-  // any of them: q and k (256 B per token row of this head) and the gate
-  // input (raw bf16 projection, 256 B, or f32 log decay, 512 B).  The phases
-  // below then load from L2 instead of paying a DRAM round trip each.
-  if (tid < 3 * C) {
-    const int row = tid % C, which = tid / C;
-    if (t0 + row < seq) {
-      const long long tok = tok0 + t0 + row;
-      const void* src;
-      uint32_t bytes = DK * 2;
-      if (which == 0) src = qg + tok * ld + h * DK;
-      else if (which == 1) src = kg + tok * ld + h * DK;
-      else if (raw.active) src = raw.f + tok * raw.ldf + h * DK;
-      else { src = gg + tok * ldg + h * DK; bytes = DK * 4; }
-      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
-    }
-  }
   if (tid == 0) {
     mbar_init(mma_done, 1);
     fence_barrier_init();

@@ -16,18 +16,16 @@ namespace ennx {
 // Router: a register-blocked fp32 SIMT GEMM.  A block owns RT consecutive
 // tokens of one weight set and all experts (in tiles of RE); K is staged
 // through shared memory in chunks of RK, converted from bf16 to fp32 once.
-// Thread (ty, tx) accumulates tokens 4*ty..4*ty+3 x experts 4*tx..4*tx+3,
+// Thread (ty, tx) accumulates tokens 8*ty..8*ty+7 x experts 4*tx..4*tx+3,
 // each logit one serial fma chain over k = 0, 1, ..., H-1 starting from 0 --
 // the order of the reference's per-token loop (kda_moe.metal:589-595) and of
 // the CPU oracle, so logits are bit-identical.  The serial chain rules out
-// splitting K; the parallelism comes from 16 independent chains per thread,
-// issued as 8 packed fma.rn.f32x2 per k-step (two independent IEEE fma.rn
-// each), with operands loaded one k-step ahead, and from eight warps per
-// block (one block per 64 tokens: 128 blocks for a pair's 8192 tokens, so
-// each SM needs its own warps to hide the shared-memory latency).  The logits of the block's tokens
+// splitting K; the parallelism comes from 32 independent chains per thread,
+// issued as 16 packed fma.rn.f32x2 per k-step (two independent IEEE fma.rn
+// each), with operands loaded one k-step ahead.  The logits of the block's tokens
 // are kept in shared memory; one thread per token then runs the insertion
 // top-k and the gate softmax.
-constexpr int RT = 64, RE = 64, RK = 32, kRouterThreads = 256, TPT = 4;
+constexpr int RT = 64, RE = 64, RK = 32, kRouterThreads = 128;
 
 __device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
   uint64_t r;
@@ -41,7 +39,6 @@ __device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c
   return d;
 }
 constexpr int kStageLoads = RK * RT / 8 / kRouterThreads;  // uint4 per thread per chunk (x, and w alike)
-static_assert(RT == TPT * (kRouterThreads / 16) && RE == 4 * 16 && kStageLoads >= 1, "router thread tiling");
 
 __global__ void __launch_bounds__(kRouterThreads, 1) router_topk_kernel(
     const uint16_t* __restrict__ x, long long ldx, const uint16_t* __restrict__ w0, const uint16_t* __restrict__ w1,
@@ -95,9 +92,9 @@ __global__ void __launch_bounds__(kRouterThreads, 1) router_topk_kernel(
         }
       }
     };
-    uint64_t accp[TPT / 2][4];  // accp[i][j] = (logit of token TPT*ty+2i, of token TPT*ty+2i+1) for expert 4tx+j
+    uint64_t accp[4][4];  // accp[i][j] = (logit of token 8ty+2i, of token 8ty+2i+1) for expert 4tx+j
 #pragma unroll
-    for (int i = 0; i < TPT / 2; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) accp[i][j] = 0ull;
     __syncthreads();  // previous expert tile's readers are done with the buffers
@@ -106,38 +103,40 @@ __global__ void __launch_bounds__(kRouterThreads, 1) router_topk_kernel(
     __syncthreads();
     for (int c = 0; c < nchunks; ++c) {
       if (c + 1 < nchunks) fetch(c + 1);
-      const float* a = As + (c & 1) * RK * RT + TPT * ty;
+      const float* a = As + (c & 1) * RK * RT + 8 * ty;
       const float* bb = Bs + (c & 1) * RK * RE + 4 * tx;
       // operands one k-step ahead; the FMAs run as packed pairs over tokens
       // (fma.rn.f32x2: two independent fma.rn per instruction)
-      float4 a0 = *reinterpret_cast<const float4*>(a);
+      float4 a0 = *reinterpret_cast<const float4*>(a), a1 = *reinterpret_cast<const float4*>(a + 4);
       float4 b0 = *reinterpret_cast<const float4*>(bb);
 #pragma unroll
       for (int k = 0; k < RK; ++k) {
-        float4 na0, nb0v;
+        float4 na0, na1, nb0v;
         if (k + 1 < RK) {
           na0 = *reinterpret_cast<const float4*>(a + (k + 1) * RT);
+          na1 = *reinterpret_cast<const float4*>(a + (k + 1) * RT + 4);
           nb0v = *reinterpret_cast<const float4*>(bb + (k + 1) * RE);
         }
-        const uint64_t ap[TPT / 2] = {pack_f32x2(a0.x, a0.y), pack_f32x2(a0.z, a0.w)};
+        const uint64_t ap[4] = {pack_f32x2(a0.x, a0.y), pack_f32x2(a0.z, a0.w), pack_f32x2(a1.x, a1.y),
+                                pack_f32x2(a1.z, a1.w)};
         const float br[4] = {b0.x, b0.y, b0.z, b0.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const uint64_t bj = pack_f32x2(br[j], br[j]);
 #pragma unroll
-          for (int i = 0; i < TPT / 2; ++i) accp[i][j] = fma_f32x2(ap[i], bj, accp[i][j]);
+          for (int i = 0; i < 4; ++i) accp[i][j] = fma_f32x2(ap[i], bj, accp[i][j]);
         }
-        if (k + 1 < RK) { a0 = na0; b0 = nb0v; }
+        if (k + 1 < RK) { a0 = na0; a1 = na1; b0 = nb0v; }
       }
       if (c + 1 < nchunks) stash((c + 1) & 1);
       __syncthreads();
     }
 #pragma unroll
-    for (int i = 0; i < TPT / 2; ++i)
+    for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        Ls[(TPT * ty + 2 * i) * lds + e0 + 4 * tx + j] = __uint_as_float((uint32_t)accp[i][j]);
-        Ls[(TPT * ty + 2 * i + 1) * lds + e0 + 4 * tx + j] = __uint_as_float((uint32_t)(accp[i][j] >> 32));
+        Ls[(8 * ty + 2 * i) * lds + e0 + 4 * tx + j] = __uint_as_float((uint32_t)accp[i][j]);
+        Ls[(8 * ty + 2 * i + 1) * lds + e0 + 4 * tx + j] = __uint_as_float((uint32_t)(accp[i][j] >> 32));
       }
   }
   for (int e = tid; e < experts; e += kRouterThreads) hist[e] = 0;

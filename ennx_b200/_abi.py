@@ -100,6 +100,14 @@ class PerturbSeed(ctypes.Structure):
     _fields_ = [("low", ctypes.c_uint32), ("high", ctypes.c_uint32), ("enabled", ctypes.c_uint32)]
 
 
+class PackedKdaBlock(ctypes.Structure):
+    """ennx_b200_packed_kda_block."""
+    _fields_ = [(n, PackedLinear) for n in ("qkv", "control", "forget_b", "gate_b", "output", "decay", "time_bias",
+                                            "output_norm")] + [
+        ("heads", ctypes.c_int32), ("gate_rank", ctypes.c_int32), ("rms_eps", ctypes.c_float),
+        ("residual_scale", ctypes.c_float)]
+
+
 class ModelConfig(ctypes.Structure):
     _fields_ = [("layers", ctypes.c_int32), ("hidden", ctypes.c_int32), ("vocab", ctypes.c_int32),
                 ("attn_period", ctypes.c_int32), ("q_heads", ctypes.c_int32), ("kv_heads", ctypes.c_int32),
@@ -176,6 +184,8 @@ SIGNATURES = {
     "ennx_b200_population_forward": (_I32, [_P, _P, _U64, _F32, _I32, _I32, _P, _I32, _I32, _P, _P, _SZ, _P]),
     "ennx_b200_population_hidden": (_I32, [_P, _P, _U64, _F32, _I32, _I32, _P, _I32, _I32, _P, _P, _P, _SZ, _P]),
     "ennx_b200_set_perturbation_mode": (_I32, [_I32]),
+    "ennx_b200_packed_kda_prefill_workspace_size": (_SZ, [_P, _I32, _I32, _I32]),
+    "ennx_b200_packed_kda_prefill": (_I32, [_P, _P, _P, _P, PerturbSeed, _P, _P, _P, _I32, _I32, _I32, _P, _SZ, _P]),
     "ennx_b200_es_coefficients": (_I32, [_P, _I32, _I32, _F32, _F32, _P, _P]),
     "ennx_b200_es_update_bf16": (_I32, [_P, _SZ, _U64, _U32, _P, _U32, _U32, _P]),
     "ennx_b200_population_update": (_I32, [_P, _P, _U64, _P, _I32, _I32, _P]),

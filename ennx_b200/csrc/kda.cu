@@ -251,7 +251,7 @@ __global__ void __launch_bounds__(PREP_THREADS, 2)
     unpack8(qn, q);
     unpack8(kn, k);
     if (it + 1 < C * 16 / PREP_THREADS) load_qk(it + 1, qn, kn);
-    if (raw.active) {
+    if (raw.active && !raw.no_l2norm) {
       // per-token L2 normalisation, 1/max(|x|, 1e-6), rounded to bf16 (kda_moe.metal:510-534)
       float sq = 0.0f, sk = 0.0f;
 #pragma unroll

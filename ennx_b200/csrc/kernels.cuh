@@ -62,6 +62,7 @@ struct KdaRawGate {
   const uint16_t *tb0, *tb1;        // [heads*128]
   long long split_seq;
   int active;
+  int no_l2norm;  // q and k used as given (the 16k prefill block applies no L2 norm)
 };
 int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, long long ld_qkv,
                            const float* g, const float* beta, float* state, uint16_t* o, long long ldo, int batch,

@@ -279,3 +279,56 @@ class NativeKdaModel:
         _abi.call("ennx_b200_kda_decoder_generate", self._handle, p.ctypes.data_as(ctypes.c_void_p), p.size,
                   max_new_tokens, seed & (2**64 - 1), out.ctypes.data_as(ctypes.c_void_p))
         return out.tolist()
+
+
+class PackedKdaBlock:
+    """The KDA attention block of one layer of a packed model over whole
+    sequences -- the reference's 16k prefill ``KdaMoeMetalExecutor::kda``
+    (forward_metal.rs:997-1129) for any length: ``block(normalized, hidden,
+    batch, seq, state=None, seed=None)`` adds ``residual_scale * update`` to
+    ``hidden`` (CUDA bf16 [batch*seq, hidden]) in place; ``seed`` enables the
+    integer-code perturbation of every projection (None: the stored codes,
+    the resident-row case), ``state`` (f32 [batch, heads, 128, 128]) carries
+    the recurrence.  The arenas are copied to the device once."""
+
+    NAMES = ("qkv", "control", "forget_b", "gate_b", "output", "decay", "time_bias", "output_norm")
+
+    def __init__(self, packed, scales, biases, linears, layer: int, heads: int, gate_rank: int, rms_epsilon: float,
+                 residual_scale: float):
+        import torch
+        named = {str(e[0]): tuple(int(v) for v in e[1:]) for e in linears}
+        a = f"layers.{layer}.attention"
+        missing = [n for n in self.NAMES if f"{a}.{n}" not in named]
+        if missing:
+            raise ValueError(f"packed model has no linear {a}.{missing[0]!r}")
+        self._block = _abi.PackedKdaBlock(*[_linear_struct(named[f"{a}.{n}"]) for n in self.NAMES], heads, gate_rank,
+                                          rms_epsilon, residual_scale)
+        self._w = torch.from_numpy(np.ascontiguousarray(packed, np.uint8)).cuda()
+        self._s = torch.from_numpy(np.ascontiguousarray(scales, np.float32)).cuda()
+        self._b = torch.from_numpy(np.ascontiguousarray(biases, np.float32)).cuda()
+        self.heads = heads
+        self._ws = None
+
+    def __call__(self, normalized, hidden, batch: int, seq: int, state=None, seed: int | None = None):
+        import torch
+        for t in (normalized, hidden):
+            if t.dtype != torch.bfloat16 or not t.is_cuda or not t.is_contiguous():
+                raise ValueError("normalized and hidden must be contiguous CUDA bf16 tensors")
+        if normalized.shape != hidden.shape or normalized.shape[0] != batch * seq:
+            raise ValueError("normalized and hidden must both be [batch * seq, hidden]")
+        H = hidden.shape[1]
+        n = _abi.lib().ennx_b200_packed_kda_prefill_workspace_size(ctypes.byref(self._block), batch, seq, H)
+        if n == 0:
+            _abi.call("ennx_b200_packed_kda_prefill", None, None, None, ctypes.byref(self._block),
+                      _abi.PerturbSeed(0, 0, 0), None, None, None, batch, seq, H, None, 0, None)
+        if self._ws is None or self._ws.numel() < n:
+            self._ws = torch.empty(n, dtype=torch.uint8, device=hidden.device)
+        ps = _abi.PerturbSeed(0, 0, 0) if seed is None else _abi.PerturbSeed(seed & 0xFFFFFFFF,
+                                                                              (seed >> 32) & 0xFFFFFFFF, 1)
+        _abi.call("ennx_b200_packed_kda_prefill", ctypes.c_void_p(self._w.data_ptr()),
+                  ctypes.c_void_p(self._s.data_ptr()), ctypes.c_void_p(self._b.data_ptr()), ctypes.byref(self._block),
+                  ps, ctypes.c_void_p(normalized.data_ptr()), ctypes.c_void_p(hidden.data_ptr()),
+                  None if state is None else ctypes.c_void_p(state.data_ptr()), batch, seq, H,
+                  ctypes.c_void_p(self._ws.data_ptr()), self._ws.numel(),
+                  ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        return hidden

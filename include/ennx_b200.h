@@ -452,6 +452,45 @@ ENNX_B200_API int32_t ennx_b200_packed_linear_bf16(const uint16_t* x, int64_t to
                                                    ennx_b200_perturb_seed seed, uint16_t* out, void* workspace,
                                                    size_t workspace_bytes, void* stream);
 
+/* ---- packed KDA attention block over whole sequences (16k prefill) ------ */
+
+/* Descriptors of one layer's KDA block in a package (names as in the
+ * package: layers.<i>.attention.{qkv, control, forget_b, gate_b, output,
+ * decay, time_bias, output_norm}); the vectors are one-row linears. */
+typedef struct {
+    ennx_b200_packed_linear qkv;          /* [3*heads*128, hidden] */
+    ennx_b200_packed_linear control;      /* [2*rank + heads, hidden]: forget state | output state | beta */
+    ennx_b200_packed_linear forget_b;     /* [heads*128, rank] */
+    ennx_b200_packed_linear gate_b;       /* [heads*128, rank] */
+    ennx_b200_packed_linear output;       /* [hidden, heads*128] */
+    ennx_b200_packed_linear decay;        /* [1, heads] */
+    ennx_b200_packed_linear time_bias;    /* [1, heads*128] */
+    ennx_b200_packed_linear output_norm;  /* [1, 128] */
+    int32_t heads, gate_rank;
+    float rms_eps, residual_scale;
+} ennx_b200_packed_kda_block;
+
+/* The KDA attention update of KdaMoeMetalExecutor::kda (forward_metal.rs:
+ * 997-1129: packed qkv and control projections, splits, forget / output-gate
+ * projections, gate and beta, the gated delta recurrence, per-head norm x
+ * sigmoid(output gate), output projection, residual) for `batch` sequences
+ * of any length `seq` (the reference requires 16384): hidden (device bf16
+ * [batch*seq, hidden_width]) += residual_scale * update, computed from
+ * `normalized` (the RMS-normalised input, same shape).  Like that path it
+ * applies no short convolution and no q/k L2 norm.  `seed` is the integer-
+ * code perturbation of every projection (PerturbSeed).  state (nullable,
+ * f32 [batch, heads, 128, 128]) is the recurrent state in and out.  heads*128
+ * key/value width, gate_rank and hidden_width multiples of 64.  workspace:
+ * 256-byte aligned, >= ennx_b200_packed_kda_prefill_workspace_size bytes. */
+ENNX_B200_API size_t ennx_b200_packed_kda_prefill_workspace_size(const ennx_b200_packed_kda_block* block,
+                                                                 int32_t batch, int32_t seq, int32_t hidden_width);
+ENNX_B200_API int32_t ennx_b200_packed_kda_prefill(const uint8_t* weights, const float* scales, const float* biases,
+                                                   const ennx_b200_packed_kda_block* block,
+                                                   ennx_b200_perturb_seed seed, const uint16_t* normalized,
+                                                   uint16_t* hidden, float* state, int32_t batch, int32_t seq,
+                                                   int32_t hidden_width, void* workspace, size_t workspace_bytes,
+                                                   void* stream);
+
 /* ---- resident BF16 TuRBO search (replaces the Bf16SearchEngine of the
  *      ennx-cuda crate, cuda/src/bf16_search.rs:129-1067, and its kernels
  *      distance_bf16 / score_bf16 / draw_bf16 / seed_bf16 / pick_trial /

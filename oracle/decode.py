@@ -158,3 +158,41 @@ class DecoderOracle:
             if i + 1 < max_new_tokens:
                 nxt = self.decode_token(nxt, seed)
         return out
+
+
+def kda_prefill_block(packed, scales, biases, linears, layer, heads, gate_rank, eps, residual_scale, normalized,
+                      hidden, batch, seq, seed=None, state=None):
+    """The 16k prefill KDA block (KdaMoeMetalExecutor::kda, forward_metal.rs:
+    997-1129) in float64 between the points where the device stores bf16:
+    packed projections, gate/beta, the serial recurrence (fp32 state), per-
+    head norm x sigmoid(gate), output projection, residual.  No short
+    convolution and no q/k L2 norm, as that path has none."""
+    from . import kda_postprocess, kda_recurrence, round_bf16
+    named = {str(e[0]): tuple(int(v) for v in e[1:]) for e in linears}
+    a = f"layers.{layer}.attention"
+    s = (0, 0, 0) if seed is None else (seed & 0xFFFFFFFF, (seed >> 32) & 0xFFFFFFFF, 1)
+
+    def W(n):
+        return packed_dequantize(packed, scales, biases, PackedLinear(*named[f"{a}.{n}"]), s).astype(np.float64)
+
+    hw, r = heads * 128, gate_rank
+    T = batch * seq
+    x = np.asarray(normalized, np.float64)
+    qkv = round_bf16((x @ W("qkv").T).astype(np.float32))
+    ctl = round_bf16((x @ W("control").T).astype(np.float32))
+    f = round_bf16((ctl[:, :r].astype(np.float64) @ W("forget_b").T).astype(np.float32))
+    og = round_bf16((ctl[:, r:2 * r].astype(np.float64) @ W("gate_b").T).astype(np.float32))
+    decay = round_bf16(W("decay")[0].astype(np.float32)).astype(np.float64)
+    tb = round_bf16(W("time_bias")[0].astype(np.float32)).astype(np.float64)
+    onorm = round_bf16(W("output_norm")[0].astype(np.float32))
+    g = np.maximum(-np.repeat(np.exp(decay), 128)[None, :] * softplus(f.astype(np.float64) + tb[None, :]), -5.0)
+    beta = 1.0 / (1.0 + np.exp(-ctl[:, 2 * r:2 * r + heads].astype(np.float64)))
+    shp = (batch, seq, heads, 128)
+    o, st = kda_recurrence(qkv[:, :hw].reshape(shp), qkv[:, hw:2 * hw].reshape(shp), qkv[:, 2 * hw:].reshape(shp),
+                           g.astype(np.float32).reshape(shp), beta.astype(np.float32).reshape(batch, seq, heads),
+                           state)
+    o = round_bf16(o).reshape(T, heads, 128)
+    post = round_bf16(kda_postprocess(o, og, onorm, eps).reshape(T, hw))
+    upd = post.astype(np.float64) @ W("output").T
+    out = round_bf16((np.asarray(hidden, np.float64) + residual_scale * upd).astype(np.float32))
+    return out, st

@@ -38,7 +38,9 @@ def test_packed_kda_block_matches_oracle(package, layer, batch, seq, seed):
     blk = PackedKdaBlock(package.packed, package.scales, package.biases, package.linears(), layer, heads, r,
                          CFG["rms_epsilon"], CFG["residual_scale"])
     rng = np.random.default_rng(layer * 100 + seq)
-    xn = O.round_bf16(rng.standard_normal((batch * seq, H)).astype(np.float32))
+    # Without the q/k L2 norm the delta rule is stable only while beta*|k|^2 < 2;
+    # inputs at 0.15 of unit RMS keep this test package's keys there
+    xn = O.round_bf16((0.15 * rng.standard_normal((batch * seq, H))).astype(np.float32))
     h0 = O.round_bf16(rng.standard_normal((batch * seq, H)).astype(np.float32))
     state0 = (rng.standard_normal((batch, heads, 128, 128)) * 0.05).astype(np.float32)
     hid = torch.from_numpy(h0).cuda().bfloat16()
@@ -57,7 +59,7 @@ def test_packed_kda_block_state_carries_and_seed_matters(package):
     blk = PackedKdaBlock(package.packed, package.scales, package.biases, package.linears(), 0, heads, r,
                          CFG["rms_epsilon"], CFG["residual_scale"])
     rng = np.random.default_rng(3)
-    xn = torch.from_numpy(O.round_bf16(rng.standard_normal((128, H)).astype(np.float32))).cuda().bfloat16()
+    xn = torch.from_numpy(O.round_bf16((0.15 * rng.standard_normal((128, H))).astype(np.float32))).cuda().bfloat16()
     # one call over 128 tokens == two calls over 64 with the state carried
     full = torch.zeros(128, H, device="cuda", dtype=torch.bfloat16)
     blk(xn, full, 1, 128, state=torch.zeros(1, heads, 128, 128, device="cuda"), seed=5)

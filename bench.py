@@ -616,6 +616,62 @@ def run_search(args):
         "cpu_baseline": cpu, "timing": "cuda events over eager rounds (host calls included)"}), flush=True)
 
 
+def run_packed_prefill(args):
+    """The packed KDA attention block over whole sequences at the reference's
+    16k prefill shape (KdaMoeMetalExecutor::kda, forward_metal.rs:997-1129,
+    which requires length 16384): 1 x 16384 tokens, hidden 2048, 16 heads x
+    128, gate rank 128, int4 codes (group 64) with integer-code perturbation
+    on.  A step is one block call for one candidate seed (dequantise the
+    candidate's codes, five projections, gated chunked KDA, post-norm,
+    output projection + residual).  Weights: seeded random codes."""
+    import numpy as np
+    import torch
+
+    from ennx_b200.native import PackedKdaBlock
+
+    torch.cuda.set_device(0)
+    H, heads, hw, r, T = 2048, 16, 128, 128, 16384
+    W = heads * hw
+    plan = [("qkv", 3 * W, H), ("control", 2 * r + heads, H), ("forget_b", W, r), ("gate_b", W, r), ("output", H, W),
+            ("decay", 1, heads), ("time_bias", 1, W), ("output_norm", 1, hw)]
+    linears, byte, sco, elem = [], 0, 0, 0
+    for name, out, inp in plan:
+        group = 64 if inp % 64 == 0 else inp
+        linears.append((f"layers.0.attention.{name}", byte, sco, sco, inp, out, 4, group, elem, 0, 0x20000000))
+        byte += out * ((inp * 4 + 7) // 8)
+        sco += out * ((inp + group - 1) // group)
+        elem += out * inp
+    rng = np.random.default_rng(0)
+    packed = rng.integers(0, 256, size=byte, dtype=np.uint8)
+    scales = np.full(sco, 3.0 / (15 * np.sqrt(H)) * 0.1, np.float32)
+    biases = np.full(sco, -7.5 * 3.0 / (15 * np.sqrt(H)) * 0.1, np.float32)
+    blk = PackedKdaBlock(packed, scales, biases, linears, 0, heads, r, 1e-6, 0.22)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    xn = torch.randn(T, H, generator=g, device="cuda").bfloat16()
+    hid = torch.zeros(T, H, device="cuda", dtype=torch.bfloat16)
+    st = torch.zeros(1, heads, hw, hw, device="cuda")
+    for i in range(max(args.warmup, 3)):
+        blk(xn, hid, 1, T, state=st, seed=i)
+    torch.cuda.synchronize()
+    k = max(args.steps, 5)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for i in range(k):
+        blk(xn, hid, 1, T, state=st, seed=100 + i)
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / k
+    flops = 2.0 * T * (3 * W * H + (2 * r + heads) * H + 2 * W * r + H * W) + T * heads * 6.0 * hw * hw
+    hbm, tf, _, src = peaks()
+    print(json.dumps({
+        "op": "packed_prefill", "metric": "packed KDA block tokens/s (16k prefill, one candidate per call)",
+        "value": T / (ms / 1e3), "unit": "tokens/s", "ms_per_call": ms, "higher_is_better": True, "steps": k,
+        "config": {"workload": "1 x 16384 tokens, hidden 2048, 16 x 128 heads, rank 128, int4 group 64, code "
+                               "perturbation on, a new candidate seed per call"},
+        "tflops": flops / (ms / 1e3) / 1e12, "frac_tensor_of_burst": flops / (ms / 1e3) / 1e12 / tf, "peaks": src,
+        "timing": "CUDA events over eager calls (dequantisation of the candidate's codes included)"}), flush=True)
+
+
 def run_decode(args):
     """Greedy single-token decoding of a packed int4 KDA-MoE model through
     NativeKdaModel (the reference's NativeKdaModel decode path,
@@ -691,6 +747,7 @@ def run_decode(args):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--op", choices=["forward", "gemm", "gemm_pb", "gemm_pb_moe", "attention", "moe", "kda", "search",
+                                     "packed_prefill",
                                      "decode"],
                     default="forward")
     ap.add_argument("--gpus", type=int, default=1)
@@ -708,6 +765,8 @@ def main():
         run_reference(args)
     elif args.op == "search":
         run_search(args)
+    elif args.op == "packed_prefill":
+        run_packed_prefill(args)
     elif args.op == "decode":
         run_decode(args)
     elif args.op != "forward":

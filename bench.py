@@ -262,6 +262,7 @@ def run_ours(args):
     my_pairs = pairs // world
 
     cfg = HybridConfig(layers=args.layers) if args.layers else HybridConfig()
+    ennx_b200.model.set_perturbation_mode(args.perturbation == "fused")
     weights = init_weights(cfg, seed=1234)  # identical base weights on every rank
     ev = PopulationEvaluator(cfg, weights, BATCH, SEQ)
     gen = torch.Generator().manual_seed(99)
@@ -383,6 +384,7 @@ def run_ours(args):
                 "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
                 "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
                 "config": dict(CONFIG, parallelism=f"population-sharded x{world} (pairs per rank {my_pairs})",
+                               perturbation=args.perturbation,
                                **({"profiling_override": f"layers={cfg.layers} pairs={pairs} (not the benchmark)"}
                                   if args.layers or args.pairs else {})),
                 "tflops": total_flops / (ms / 1000.0) / 1e12,
@@ -756,6 +758,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--plain", action="store_true", help="gemm_pb ops: time the plain GEMM on stored W +/- e")
+    ap.add_argument("--perturbation", choices=["stored", "fused"], default="stored",
+                    help="forward: W +/- e as stored per-layer copies, or formed in the GEMM operand path")
     ap.add_argument("--layers", type=int, default=0, help="profiling aid: a shorter model (not the benchmark)")
     ap.add_argument("--pairs", type=int, default=0, help="profiling aid: fewer antithetic pairs (not the benchmark)")
     args = ap.parse_args()

@@ -448,16 +448,36 @@ __global__ void __launch_bounds__(THREADS, 2)
 // whose 256-row tile is empty (ragged MoE groups) has its loads and MMAs
 // skipped.
 // ===========================================================================
-constexpr int PB_TWARPS = 8;                                  // transform warps (two groups of four)
-constexpr int PB_GROUP_THREADS = 32 * PB_TWARPS / 2;
+#ifndef PB_TWARPS_DEF
+#define PB_TWARPS_DEF 8
+#endif
+constexpr int PB_TWARPS = PB_TWARPS_DEF;                      // transform warps (PB_TGROUPS groups)
+#ifndef PB_TGROUPS_DEF
+#define PB_TGROUPS_DEF 2
+#endif
+constexpr int PB_TGROUPS = PB_TGROUPS_DEF;                    // transform groups, taking B stages in turn
+constexpr int PB_GROUP_THREADS = 32 * PB_TWARPS / PB_TGROUPS;
 constexpr int PB_THREADS = 64 + 32 * EPI_WARPS + 32 * PB_TWARPS + 32;  // + the B producer warp: 608
 constexpr int PB_BPROD_WARP = 2 + EPI_WARPS + PB_TWARPS;
-constexpr int PB_BK = 32;                                     // K per stage
-constexpr int PB_TILE = BM * PB_BK * 2;                       // 8 KB: 128 rows x 64 B
-constexpr int PB_NA = 6, PB_NB = 6;
+// K per stage 64 (128-byte swizzled rows: one L2 request moves a whole
+// line, where 64-byte rows took twice the requests); the B ring deeper than
+// the A ring, since a B stage also waits for its rewrite (measured: 2 A + 4 B
+// stages 20 % faster than 6 + 6 stages of K 32, and than 3 + 3 of K 64)
+#ifndef PB_BK_DEF
+#define PB_BK_DEF 64
+#define PB_NA_DEF 2
+#define PB_NB_DEF 4
+#endif
+constexpr int PB_BK = PB_BK_DEF;                              // K per stage
+constexpr int PB_TILE = BM * PB_BK * 2;                       // 128 rows x 2 PB_BK bytes
+constexpr int PB_NA = PB_NA_DEF, PB_NB = PB_NB_DEF;
+constexpr int PB_SW = PB_BK * 2;                              // swizzle span = row bytes (64 or 128)
+constexpr int PB_CH = PB_TILE / 16 / PB_GROUP_THREADS;        // 16-byte chunks of W (and of E) per transform thread
+__device__ __forceinline__ uint64_t pb_desc(uint32_t a) { return PB_SW == 128 ? smem_desc_sw128(a) : smem_desc_sw64(a); }
 constexpr uint32_t PB_IDESC = idesc_bf16_f32(256, BN);
 static_assert((PB_NA + PB_NB) * 2 * PB_TILE <= STAGES * STAGE_BYTES, "perturbed-B rings fit the ring space");
-static_assert(PB_TILE / 16 == 4 * PB_GROUP_THREADS, "four 16-byte chunks of W and E per transform thread");
+static_assert(PB_TGROUPS <= PB_NB, "each transform group starts on its own stage");
+static_assert(PB_TILE / 16 == PB_CH * PB_GROUP_THREADS, "whole 16-byte chunks of W and E per transform thread");
 static_assert(PB_THREADS * 96 <= 65536, "register budget");
 
 struct PbArgs {
@@ -527,7 +547,7 @@ __global__ void __maxnreg__(96)
     for (int i = 0; i < PB_NA; ++i) { mbar_init(&s.full_a[i], 1); mbar_init(&s.empty_a[i], 1); }
     for (int i = 0; i < PB_NB; ++i) {
       mbar_init(&s.full_b[i], 1);
-      mbar_init(&s.ready_b[i], PB_TWARPS);  // one group of four warps in each of the two CTAs
+      mbar_init(&s.ready_b[i], 2 * PB_TWARPS / PB_TGROUPS);  // one group of four warps in each of the two CTAs
       mbar_init(&s.empty_b[i], 1);
     }
     mbar_init(&s.tfull, 1);
@@ -626,7 +646,7 @@ __global__ void __maxnreg__(96)
           if (act_p) {
 #pragma unroll
             for (int k = 0; k < PB_BK / 16; ++k)
-              umma_f16_pair(tmem_base, smem_desc_sw64(ab + k * 32), smem_desc_sw64(bb + k * 32), PB_IDESC,
+              umma_f16_pair(tmem_base, pb_desc(ab + k * 32), pb_desc(bb + k * 32), PB_IDESC,
                             (kb | k) != 0);
           }
           if (kb == 0 && !mbar_wait(&s.tempty[1], acc_phase ^ 1u, a.err)) { ok = false; break; }
@@ -634,8 +654,8 @@ __global__ void __maxnreg__(96)
           if (act_m) {
 #pragma unroll
             for (int k = 0; k < PB_BK / 16; ++k)
-              umma_f16_pair(tmem_base + BN, smem_desc_sw64(ab + PB_TILE + k * 32),
-                            smem_desc_sw64(bb + PB_TILE + k * 32), PB_IDESC, (kb | k) != 0);
+              umma_f16_pair(tmem_base + BN, pb_desc(ab + PB_TILE + k * 32),
+                            pb_desc(bb + PB_TILE + k * 32), PB_IDESC, (kb | k) != 0);
           }
           umma_commit_pair(&s.empty_a[sa], 0x3);
           umma_commit_pair(&s.empty_b[sb], 0x3);
@@ -668,41 +688,51 @@ __global__ void __maxnreg__(96)
     if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
     __syncwarp();
   } else {
-    // transform warps: group tg (warps 10-13 / 14-17) takes B stages with
-    // parity tg; thread tt rewrites 16-byte chunks tt + 128 j (j < 4) of the
-    // two 8 KB slots, W -> W + E and E -> W - E (identical swizzled layouts)
-    const int tg = (warp - (2 + EPI_WARPS)) >> 2;
+    // transform warps: group tg (warps 10-13 / 14-17) takes the B stages
+    // i = tg mod PB_TGROUPS; thread tt rewrites 16-byte chunks tt + 128 j
+    // (j < PB_CH) of the W and E slots, W -> W + E and E -> W - E (identical
+    // swizzled layouts)
+    const int tg = (warp - (2 + EPI_WARPS)) / (PB_TWARPS / PB_TGROUPS);
     const int tt = threadIdx.x - 32 * (2 + EPI_WARPS) - tg * PB_GROUP_THREADS;
     const uint32_t ready_remote = mapa_shared(&s.ready_b[0], 0);  // ready_b[i] = ready_remote + 8 i
     const int my_units = total > first ? (total - first + stride - 1) / stride : 0;
     const int items = my_units * KB;
     int stage = tg;
     uint32_t phase = 0;
-    for (int i = tg; i < items; i += 2) {
+    for (int i = tg; i < items; i += PB_TGROUPS) {
       if (aborted()) break;
       if (!mbar_wait(&s.full_b[stage], phase, a.err)) { s.abort_flag = 1; break; }
       const uint32_t bw = smem_u32(b_ptr(stage, 0)) + tt * 16, be = bw + PB_TILE;
-      uint4 w[4], e[4];
+      constexpr int CB = PB_CH < 4 ? PB_CH : 4;  // chunks in flight per thread
+      constexpr uint32_t CS = 16 * PB_GROUP_THREADS;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(w[j].x), "=r"(w[j].y), "=r"(w[j].z), "=r"(w[j].w) : "r"(bw + j * 2048));
-        asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
-                     : "=r"(e[j].x), "=r"(e[j].y), "=r"(e[j].z), "=r"(e[j].w) : "r"(be + j * 2048));
-      }
+      for (int j0 = 0; j0 < PB_CH; j0 += CB) {
+        uint4 w[CB], e[CB];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(bw + j * 2048), "r"(bf16x2_add(w[j].x, e[j].x)),
-                     "r"(bf16x2_add(w[j].y, e[j].y)), "r"(bf16x2_add(w[j].z, e[j].z)), "r"(bf16x2_add(w[j].w, e[j].w))
-                     : "memory");
-        asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(be + j * 2048), "r"(bf16x2_sub(w[j].x, e[j].x)),
-                     "r"(bf16x2_sub(w[j].y, e[j].y)), "r"(bf16x2_sub(w[j].z, e[j].z)), "r"(bf16x2_sub(w[j].w, e[j].w))
-                     : "memory");
+        for (int j = 0; j < CB; ++j) {
+          const uint32_t o = (j0 + j) * CS;
+          asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(w[j].x), "=r"(w[j].y), "=r"(w[j].z), "=r"(w[j].w) : "r"(bw + o));
+          asm volatile("ld.shared.v4.b32 {%0,%1,%2,%3}, [%4];"
+                       : "=r"(e[j].x), "=r"(e[j].y), "=r"(e[j].z), "=r"(e[j].w) : "r"(be + o));
+        }
+#pragma unroll
+        for (int j = 0; j < CB; ++j) {
+          const uint32_t o = (j0 + j) * CS;
+          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(bw + o), "r"(bf16x2_add(w[j].x, e[j].x)),
+                       "r"(bf16x2_add(w[j].y, e[j].y)), "r"(bf16x2_add(w[j].z, e[j].z)),
+                       "r"(bf16x2_add(w[j].w, e[j].w))
+                       : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(be + o), "r"(bf16x2_sub(w[j].x, e[j].x)),
+                       "r"(bf16x2_sub(w[j].y, e[j].y)), "r"(bf16x2_sub(w[j].z, e[j].z)),
+                       "r"(bf16x2_sub(w[j].w, e[j].w))
+                       : "memory");
+        }
       }
       fence_proxy_async();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(ready_remote + 8u * (uint32_t)stage);
-      stage += 2;  // this group's next stage
+      stage += PB_TGROUPS;  // this group's next stage
       if (stage >= PB_NB) { stage -= PB_NB; phase ^= 1u; }
     }
   }
@@ -874,9 +904,9 @@ int32_t gemm_bf16_perturbed(const ennx_b200_gemm_params* p, const uint16_t* A, c
     return set_error(ENNX_B200_INVALID_ARGUMENT, "gemm_perturbed: b_group_rows must be >= N");
   CUtensorMap ta, tw, te, tc;
   const long long b_rows = (long long)(G / 2 - 1) * p->b_group_rows + N;
-  ENNX_TRY(make_tmap_2d_bf16_sw(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)p->lda, PB_BK, BM, 64));
-  ENNX_TRY(make_tmap_2d_bf16_sw(&tw, W, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, PB_BK, BM, 64));
-  ENNX_TRY(make_tmap_2d_bf16_sw(&te, E, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, PB_BK, BM, 64));
+  ENNX_TRY(make_tmap_2d_bf16_sw(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)p->lda, PB_BK, BM, PB_SW));
+  ENNX_TRY(make_tmap_2d_bf16_sw(&tw, W, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, PB_BK, BM, PB_SW));
+  ENNX_TRY(make_tmap_2d_bf16_sw(&te, E, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, PB_BK, BM, PB_SW));
   memset(&tc, 0, sizeof(tc));
   const bool bf16_out = epi == ENNX_B200_EPI_BF16 || epi == ENNX_B200_EPI_SWIGLU || epi == ENNX_B200_EPI_ROWSCALE;
   if (bf16_out) {

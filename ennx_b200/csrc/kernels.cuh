@@ -54,15 +54,15 @@ size_t kda_workspace_bytes(int batch, int seq, int heads);
 // Forward-path inputs of the chunked KDA: gates from the raw projections and
 // in-kernel L2 normalisation of q and k (sequences < split_seq use set 0).
 struct KdaRawGate {
-  const uint16_t* f;      // raw forget logits [T, heads*128]
-  long long ldf;
-  const uint16_t* rbeta;  // raw beta logits, column h of row t
-  long long ldb;
-  const uint16_t *decay0, *decay1;  // [heads]
-  const uint16_t *tb0, *tb1;        // [heads*128]
-  long long split_seq;
-  int active;
-  int no_l2norm;  // q and k used as given (the 16k prefill block applies no L2 norm)
+  const uint16_t* f = nullptr;      // raw forget logits [T, heads*128]
+  long long ldf = 0;
+  const uint16_t* rbeta = nullptr;  // raw beta logits, column h of row t
+  long long ldb = 0;
+  const uint16_t *decay0 = nullptr, *decay1 = nullptr;  // [heads]
+  const uint16_t *tb0 = nullptr, *tb1 = nullptr;        // [heads*128]
+  long long split_seq = 0;
+  int active = 0;
+  int no_l2norm = 0;  // q and k used as given (the 16k prefill block applies no L2 norm)
 };
 int32_t launch_kda_chunked(const uint16_t* q, const uint16_t* k, const uint16_t* v, long long ld_qkv,
                            const float* g, const float* beta, float* state, uint16_t* o, long long ldo, int batch,

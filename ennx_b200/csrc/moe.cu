@@ -25,7 +25,15 @@ namespace ennx {
 // each), with operands loaded one k-step ahead.  The logits of the block's tokens
 // are kept in shared memory; one thread per token then runs the insertion
 // top-k and the gate softmax.
-constexpr int RT = 64, RE = 64, RK = 32, kRouterThreads = 128;
+//
+// Sizes: 56 tokens per block (7 rows of 16 threads), so that one weight set
+// of 4096 tokens -- half of a pair's rows -- is 74 blocks and a pair fills
+// the 148 SMs exactly.  Each K chunk (64 k) is copied into a bf16 staging
+// area with cp.async before the previous chunk's FMAs run, so the copies are
+// in flight meanwhile.  (A dedicated feed warp converting for the other four
+// measured slower: one warp's conversion outlasts a chunk of FMAs.)
+constexpr int RT = 56, RE = 64, RK = 64, kRouterThreads = 112;
+static_assert(RT == 8 * (kRouterThreads / 16) && RE == 4 * 16, "thread (tx, ty) owns 8 tokens x 4 experts");
 
 __device__ __forceinline__ uint64_t pack_f32x2(float lo, float hi) {
   uint64_t r;
@@ -38,9 +46,16 @@ __device__ __forceinline__ uint64_t fma_f32x2(uint64_t a, uint64_t b, uint64_t c
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
   return d;
 }
-constexpr int kStageLoads = RK * RT / 8 / kRouterThreads;  // uint4 per thread per chunk (x, and w alike)
+constexpr int kXLoads = RK * RT / 8, kWLoads = RK * RE / 8;     // uint4 per chunk (x rows, expert rows)
+constexpr int kXPer = (kXLoads + kRouterThreads - 1) / kRouterThreads;
+constexpr int kWPer = (kWLoads + kRouterThreads - 1) / kRouterThreads;
+// 16-byte global -> shared copy (zero fill when !ok)
+__device__ __forceinline__ void cp_async16(void* dst, const void* src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(dst)), "l"(src), "r"(ok ? 16 : 0)
+               : "memory");
+}
 
-__global__ void __launch_bounds__(kRouterThreads, 1) router_topk_kernel(
+__global__ void __launch_bounds__(kRouterThreads, 2) router_topk_kernel(
     const uint16_t* __restrict__ x, long long ldx, const uint16_t* __restrict__ w0, const uint16_t* __restrict__ w1,
     long long split, long long tokens, int hidden, int experts, int top_k, float* __restrict__ logits,
     int* __restrict__ idx, float* __restrict__ gate, int* __restrict__ counts) {
@@ -50,6 +65,8 @@ __global__ void __launch_bounds__(kRouterThreads, 1) router_topk_kernel(
   float* Bs = As + 2 * RK * RT;     // [2][RK][RE]
   float* Ls = Bs + 2 * RK * RE;     // [RT][lds]
   const int lds = ((experts + RE - 1) / RE) * RE + 1;
+  uint16_t* xst = reinterpret_cast<uint16_t*>(Ls + (RT * lds + 3) / 4 * 4);  // [kXLoads][8] bf16 staging
+  uint16_t* wst = xst + kXLoads * 8;                                         // [kWLoads][8]
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const long long nb0 = (split + RT - 1) / RT;
   long long tb, te;
@@ -61,32 +78,53 @@ __global__ void __launch_bounds__(kRouterThreads, 1) router_topk_kernel(
   }
   const int nchunks = hidden / RK;
   for (int e0 = 0; e0 < experts; e0 += RE) {
-    // global -> register staging, uint4 (8 k of one token / expert) each
-    uint4 rx[kStageLoads], rw[kStageLoads];
+    // chunk c's copies (16 B = 8 k of one token or expert each); each thread
+    // later converts exactly the pieces it copied, so the staging needs no
+    // barrier of its own
     auto fetch = [&](int c) {
 #pragma unroll
-      for (int i = 0; i < kStageLoads; ++i) {
+      for (int i = 0; i < kXPer; ++i) {
         const int li = tid + i * kRouterThreads, t = li % RT, q = li / RT;
-        rx[i] = tb + t < te ? __ldg(reinterpret_cast<const uint4*>(x + (tb + t) * ldx + c * RK + 8 * q))
-                            : make_uint4(0, 0, 0, 0);
-        const int e = e0 + li % RE, qe = li / RE;
-        rw[i] = e < experts ? __ldg(reinterpret_cast<const uint4*>(w + (long long)e * hidden + c * RK + 8 * qe))
-                            : make_uint4(0, 0, 0, 0);
+        if (li < kXLoads) {
+          const bool ok = tb + t < te;
+          cp_async16(xst + li * 8, x + (ok ? (tb + t) * ldx + c * RK + 8 * q : 0), ok);
+        }
       }
+#pragma unroll
+      for (int i = 0; i < kWPer; ++i) {
+        const int li = tid + i * kRouterThreads, e = e0 + li % RE, qe = li / RE;
+        if (li < kWLoads) {
+          const bool ok = e < experts;
+          cp_async16(wst + li * 8, w + (ok ? (long long)e * hidden + c * RK + 8 * qe : 0), ok);
+        }
+      }
+      asm volatile("cp.async.commit_group;" ::: "memory");
     };
+    // the staged chunk into the fp32 operands As/Bs[buf]
     auto stash = [&](int buf) {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
       float* a = As + buf * RK * RT;
       float* bb = Bs + buf * RK * RE;
 #pragma unroll
-      for (int i = 0; i < kStageLoads; ++i) {
-        const int li = tid + i * kRouterThreads;
-        const int t = li % RT, q = li / RT, e = li % RE, qe = li / RE;
-        const uint32_t xv[4] = {rx[i].x, rx[i].y, rx[i].z, rx[i].w};
-        const uint32_t wv[4] = {rw[i].x, rw[i].y, rw[i].z, rw[i].w};
+      for (int i = 0; i < kXPer; ++i) {
+        const int li = tid + i * kRouterThreads, t = li % RT, q = li / RT;
+        if (li >= kXLoads) break;
+        const uint4 v = *reinterpret_cast<const uint4*>(xst + li * 8);
+        const uint32_t xv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
         for (int h = 0; h < 4; ++h) {
           a[(8 * q + 2 * h) * RT + t] = bf16_to_f32((uint16_t)(xv[h] & 0xffffu));
           a[(8 * q + 2 * h + 1) * RT + t] = bf16_to_f32((uint16_t)(xv[h] >> 16));
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < kWPer; ++i) {
+        const int li = tid + i * kRouterThreads, e = li % RE, qe = li / RE;
+        if (li >= kWLoads) break;
+        const uint4 v = *reinterpret_cast<const uint4*>(wst + li * 8);
+        const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
           bb[(8 * qe + 2 * h) * RE + e] = bf16_to_f32((uint16_t)(wv[h] & 0xffffu));
           bb[(8 * qe + 2 * h + 1) * RE + e] = bf16_to_f32((uint16_t)(wv[h] >> 16));
         }
@@ -236,16 +274,31 @@ __global__ void __launch_bounds__(256) moe_scatter_gather_kernel(
     perm_pos[t * top_k + lane] = pos;
     perm_gate[pos] = gate_scale * gate[t * top_k + lane];
   }
+  // the row is read in batches of eight 16-byte chunks per lane (all loads
+  // in flight before the first store), then written to each slot
   const uint16_t* src = x + t * ldx;
-  for (int c = lane * 8; c < width; c += 256) {
-    const uint4 v = *reinterpret_cast<const uint4*>(src + c);
-    for (int r = 0; r < top_k; ++r) {
-      const int p = __shfl_sync(0xffffffffu, pos, r);
-      *reinterpret_cast<uint4*>(xperm + (long long)p * width + c) = v;
+  int slot[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) slot[r] = __shfl_sync(0xffffffffu, pos, r);
+  for (int c0 = lane * 8; c0 < width; c0 += 8 * 256) {
+    uint4 v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (c0 + j * 256 < width) v[j] = ldg_stream_v4(src + c0 + j * 256);
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      if (r >= top_k) break;
+      uint16_t* dst = xperm + (long long)slot[r] * width + c0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        if (c0 + j * 256 < width) *reinterpret_cast<uint4*>(dst + j * 256) = v[j];
     }
   }
 }
 
+// out = residual + sum_r y[perm_pos[t, r]] (fp32 sum in pick order, one
+// rounding).  A warp per token; each lane keeps two 16-byte chunks of all
+// top_k rows in flight before it sums.
 __global__ void moe_combine_kernel(const uint16_t* __restrict__ y, const int* __restrict__ perm_pos, long long tokens,
                                    int top_k, int width, const uint16_t* __restrict__ residual,
                                    uint16_t* __restrict__ out) {
@@ -253,30 +306,47 @@ __global__ void moe_combine_kernel(const uint16_t* __restrict__ y, const int* __
   int lane = threadIdx.x & 31;
   if (t >= tokens) return;
   int pos[8];
-  for (int r = 0; r < top_k; ++r) pos[r] = perm_pos[t * top_k + r];
-  for (int c = lane * 8; c < width; c += 256) {
-    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (residual) {
-      uint4 rv = *reinterpret_cast<const uint4*>(residual + t * width + c);
-      uint32_t w[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        acc[2 * h] = bf16_to_f32((uint16_t)(w[h] & 0xffffu));
-        acc[2 * h + 1] = bf16_to_f32((uint16_t)(w[h] >> 16));
-      }
-    }
-    for (int r = 0; r < top_k; ++r) {
-      uint4 yv = *reinterpret_cast<const uint4*>(y + (long long)pos[r] * width + c);
-      uint32_t w[4] = {yv.x, yv.y, yv.z, yv.w};
+  for (int r = 0; r < 8; ++r) pos[r] = r < top_k ? perm_pos[t * top_k + r] : 0;
+  for (int c0 = lane * 8; c0 < width; c0 += 2 * 256) {
+    float acc[2][8];
+    uint4 yv[2][8];
 #pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        acc[2 * h] += bf16_to_f32((uint16_t)(w[h] & 0xffffu));
-        acc[2 * h + 1] += bf16_to_f32((uint16_t)(w[h] >> 16));
+    for (int u = 0; u < 2; ++u) {
+      const int c = c0 + u * 256;
+#pragma unroll
+      for (int h = 0; h < 8; ++h) acc[u][h] = 0.0f;
+      if (c < width && residual) {
+        const uint4 rv = *reinterpret_cast<const uint4*>(residual + t * width + c);
+        const uint32_t w[4] = {rv.x, rv.y, rv.z, rv.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          acc[u][2 * h] = bf16_to_f32((uint16_t)(w[h] & 0xffffu));
+          acc[u][2 * h + 1] = bf16_to_f32((uint16_t)(w[h] >> 16));
+        }
       }
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+        if (r < top_k && c < width) yv[u][r] = ldg_stream_v4(y + (long long)pos[r] * width + c);
     }
-    *reinterpret_cast<uint4*>(out + t * width + c) =
-        make_uint4(pack_bf16x2(acc[0], acc[1]), pack_bf16x2(acc[2], acc[3]), pack_bf16x2(acc[4], acc[5]),
-                   pack_bf16x2(acc[6], acc[7]));
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const int c = c0 + u * 256;
+      if (c >= width) break;
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        if (r >= top_k) break;
+        const uint32_t w[4] = {yv[u][r].x, yv[u][r].y, yv[u][r].z, yv[u][r].w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          acc[u][2 * h] += bf16_to_f32((uint16_t)(w[h] & 0xffffu));
+          acc[u][2 * h + 1] += bf16_to_f32((uint16_t)(w[h] >> 16));
+        }
+      }
+      *reinterpret_cast<uint4*>(out + t * width + c) =
+          make_uint4(pack_bf16x2(acc[u][0], acc[u][1]), pack_bf16x2(acc[u][2], acc[u][3]),
+                     pack_bf16x2(acc[u][4], acc[u][5]), pack_bf16x2(acc[u][6], acc[u][7]));
+    }
   }
 }
 
@@ -293,13 +363,15 @@ int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0,
   if (!w1) { w1 = w0; split = tokens; }
   const long long blocks = (split + RT - 1) / RT + (tokens - split + RT - 1) / RT;
   const int lds = ((experts + RE - 1) / RE) * RE + 1;
-  const size_t smem = sizeof(float) * (2 * RK * RT + 2 * RK * RE + (size_t)RT * lds);
+  const size_t smem = sizeof(float) * (2 * RK * RT + 2 * RK * RE + ((size_t)RT * lds + 3) / 4 * 4) +
+                      16 * (kXLoads + kWLoads);
   static bool attr[64];
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr[dev]) {
     ENNX_CUDA(cudaFuncSetAttribute(router_topk_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                   (int)(sizeof(float) * (2 * RK * RT + 2 * RK * RE + RT * (256 + 1)))),
+                                   (int)(sizeof(float) * (2 * RK * RT + 2 * RK * RE + (RT * (256 + 1) + 3) / 4 * 4) +
+                                         16 * (kXLoads + kWLoads))),
               "router smem");
     attr[dev] = true;
   }

@@ -85,6 +85,35 @@ def test_gemm_grouped_device_offsets_ragged():
     close(c.float().cpu().numpy(), ref)
 
 
+@pytest.mark.parametrize("epi", ["bf16", "swiglu", "rowscale"])
+def test_gemm_grouped_tail_tiles(epi):
+    # group sizes around the 256-row pair tile (partial last tiles of at most
+    # and of more than 128 rows, empty groups), every fused epilogue
+    counts = [256, 128, 129, 384, 0, 512, 640, 1, 255, 385]
+    offs = np.concatenate([[0], np.cumsum(counts)]).astype(np.int32)
+    M, N, K, G = int(offs[-1]), 512, 192, len(counts)
+    a = rand_bf16((M, K), 20)
+    b = rand_bf16((G * N, K), 21, 0.1)
+    kw = dict(groups=G, b_group_rows=N, n=N, group_offsets=torch.from_numpy(offs).cuda())
+    ref = np.zeros((M, N))
+    for g in range(G):
+        if counts[g]:
+            ref[offs[g]:offs[g + 1]] = ref_gemm(a[offs[g]:offs[g + 1]], b[g * N:(g + 1) * N])
+    if epi == "swiglu":
+        c = ops.gemm(a.cuda(), b.cuda(), epilogue=_abi.EPI_SWIGLU, **kw)
+        # each 256-column tile holds 128 gate columns, then their 128 up columns
+        gate = np.concatenate([ref[:, t:t + 128] for t in range(0, N, 256)], 1)
+        up = np.concatenate([ref[:, t + 128:t + 256] for t in range(0, N, 256)], 1)
+        ref = O.silu(gate) * up
+    elif epi == "rowscale":
+        rs = torch.rand(M, generator=torch.Generator().manual_seed(22))
+        c = ops.gemm(a.cuda(), b.cuda(), epilogue=_abi.EPI_ROWSCALE, row_scale=rs.cuda(), **kw)
+        ref = ref * rs.double().numpy()[:, None]
+    else:
+        c = ops.gemm(a.cuda(), b.cuda(), **kw)
+    close(c.float().cpu().numpy(), ref)
+
+
 def test_gemm_swiglu_epilogue():
     M, I, K = 200, 512, 256
     a = rand_bf16((M, K), 11)

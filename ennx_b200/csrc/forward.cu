@@ -430,8 +430,8 @@ int32_t compute_layer(const ennx_b200_model_config& c, int l, const ennx_b200_la
   ENNX_TRY(gemm2(w.xn, H, base_qkv, P[F_QKV], sh.rows[F_QKV] + sh.rows[F_CTL], H, w.qkv, qkv_cols, T, nullptr, s));
   if (gqa) {
     const long long kd = (long long)c.q_heads * HD, vd = kd + (long long)c.kv_heads * HD;
-    ENNX_TRY(launch_rope(w.qkv, qkv_cols, c.q_heads, HD, T, seq, c.rope_theta, s));
-    ENNX_TRY(launch_rope(w.qkv + kd, qkv_cols, c.kv_heads, HD, T, seq, c.rope_theta, s));
+    // q heads then k heads, adjacent in each qkv row: one launch
+    ENNX_TRY(launch_rope(w.qkv, qkv_cols, c.q_heads + c.kv_heads, HD, T, seq, c.rope_theta, s));
     {
       ProfScope ps("attention", s, 2.0 * batch * c.q_heads * (double)seq * (seq + 1) * HD * 2.0,
                    2.0 * T * (2.0 * kd + 2.0 * c.kv_heads * HD));

@@ -32,6 +32,18 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+// warp_sum over the 32 values p[2l + e] held as (p0, p1) by lane l of a
+// half-warp: the same additions in the same tree order, so the same float
+// result (lane 2l + e ^ 16 is half-lane l ^ 8, and so on; the last step adds
+// the lane's own pair)
+__device__ __forceinline__ float half_warp_pair_sum(float p0, float p1) {
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) {
+    p0 += __shfl_xor_sync(0xffffffffu, p0, o);
+    p1 += __shfl_xor_sync(0xffffffffu, p1, o);
+  }
+  return p0 + p1;
+}
 
 // y = x * rsqrt(mean(x^2) + eps) * w; rows [0, split) use w0, the rest w1.
 __global__ void rmsnorm_kernel(const uint16_t* __restrict__ x, long long ldx, const uint16_t* __restrict__ w0,
@@ -135,49 +147,78 @@ __global__ void kda_gate_kernel(const uint16_t* __restrict__ raw, long long ldra
 }
 
 // out = rmsnorm_head(o) * norm * sigmoid(og), head width 128; norm per set.
+// Per-head RMSNorm x norm weight x sigmoid(output gate).  A half-warp per
+// (row, head): lane l of the half holds elements 8l..8l+7 (16-byte loads).
 __global__ void kda_post_kernel(const uint16_t* __restrict__ o, const uint16_t* __restrict__ og, long long ldog,
                                 const uint16_t* __restrict__ n0, const uint16_t* __restrict__ n1, long long split,
                                 int heads, long long groups, float eps, uint16_t* __restrict__ out) {
-  long long gidx = (long long)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  int lane = threadIdx.x & 31;
-  if (gidx >= groups) return;
-  long long r = gidx / heads;
-  int h = (int)(gidx % heads);
-  long long off = r * (long long)heads * 128 + h * 128 + lane * 4;
-  uint2 raw = *reinterpret_cast<const uint2*>(o + off);
-  uint2 graw = *reinterpret_cast<const uint2*>(og + r * ldog + h * 128 + lane * 4);
-  const uint16_t* nw = (r < split ? n0 : n1) + lane * 4;
-  float f[4] = {bf16_to_f32(raw.x & 0xffffu), bf16_to_f32(raw.x >> 16), bf16_to_f32(raw.y & 0xffffu),
-                bf16_to_f32(raw.y >> 16)};
-  float g[4] = {bf16_to_f32(graw.x & 0xffffu), bf16_to_f32(graw.x >> 16), bf16_to_f32(graw.y & 0xffffu),
-                bf16_to_f32(graw.y >> 16)};
-  float ss = warp_sum(f[0] * f[0] + f[1] * f[1] + f[2] * f[2] + f[3] * f[3]);
-  float inv = rsqrtf(ss / 128.0f + eps);
-  float y[4];
+  const long long g_raw = ((long long)blockIdx.x * blockDim.x + threadIdx.x) >> 4;
+  const int l = threadIdx.x & 15;
+  const bool ok = g_raw < groups;  // no early exit: the shuffles span the whole warp
+  const long long gidx = ok ? g_raw : groups - 1;
+  const long long r = gidx / heads;
+  const int h = (int)(gidx % heads);
+  const long long off = r * (long long)heads * 128 + h * 128 + l * 8;
+  const uint4 raw = *reinterpret_cast<const uint4*>(o + off);
+  const uint4 graw = *reinterpret_cast<const uint4*>(og + r * ldog + h * 128 + l * 8);
+  const uint4 nraw = *reinterpret_cast<const uint4*>((r < split ? n0 : n1) + l * 8);
+  const uint32_t ow[4] = {raw.x, raw.y, raw.z, raw.w}, gw[4] = {graw.x, graw.y, graw.z, graw.w},
+                 nw[4] = {nraw.x, nraw.y, nraw.z, nraw.w};
+  float f[8], g[8], n[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) y[i] = f[i] * inv * bf16_to_f32(nw[i]) / (1.0f + __expf(-g[i]));
-  *reinterpret_cast<uint2*>(out + off) = make_uint2(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]));
+  for (int j = 0; j < 4; ++j) {
+    f[2 * j] = bf16_to_f32(ow[j] & 0xffffu); f[2 * j + 1] = bf16_to_f32(ow[j] >> 16);
+    g[2 * j] = bf16_to_f32(gw[j] & 0xffffu); g[2 * j + 1] = bf16_to_f32(gw[j] >> 16);
+    n[2 * j] = bf16_to_f32(nw[j] & 0xffffu); n[2 * j + 1] = bf16_to_f32(nw[j] >> 16);
+  }
+  // sum of squares over the head: partials of 4 consecutive elements, summed
+  // over the head in warp_sum's order
+  float p0 = f[0] * f[0] + f[1] * f[1] + f[2] * f[2] + f[3] * f[3];
+  float p1 = f[4] * f[4] + f[5] * f[5] + f[6] * f[6] + f[7] * f[7];
+  float ss = half_warp_pair_sum(p0, p1);
+  const float inv = rsqrtf(ss / 128.0f + eps);
+  float y[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) y[i] = f[i] * inv * n[i] / (1.0f + __expf(-g[i]));
+  if (ok)
+    *reinterpret_cast<uint4*>(out + off) = make_uint4(pack_bf16x2(y[0], y[1]), pack_bf16x2(y[2], y[3]),
+                                                      pack_bf16x2(y[4], y[5]), pack_bf16x2(y[6], y[7]));
 }
 
 // Rotate-half RoPE in place on `heads` heads of width dim starting at base + r*ld.
-// Position of row r is r % seq.
+// Position of row r is r % seq.  One thread per (row, head, 8 rotary pairs):
+// 16-byte loads of x[k0..k0+7] and x[k0+half..k0+half+7]; same per-element
+// formula as a scalar loop (inv_freq = 2^(-log2(theta) 2k/dim), angle = pos inv_freq).
 __global__ void rope_kernel(uint16_t* __restrict__ base, long long ld, int heads, int dim, long long rows, int seq,
                             float log2_theta) {
-  int half = dim / 2;
-  long long total = rows * heads * (long long)half;
+  const int half = dim / 2, cpr = half / 8, ipr = heads * cpr;  // chunks per head, per row
+  const long long total = rows * ipr;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    int k = (int)(i % half);
-    long long rh = i / half;
-    long long r = rh / heads;
-    int h = (int)(rh % heads);
-    float pos = (float)(r % seq);
-    float inv_freq = exp2f(-log2_theta * (2.0f * k / (float)dim));
-    float s, c;
-    sincosf(pos * inv_freq, &s, &c);
-    uint16_t* p = base + r * ld + (long long)h * dim;
-    float x1 = bf16_to_f32(p[k]), x2 = bf16_to_f32(p[k + half]);
-    p[k] = f32_to_bf16_rne(x1 * c - x2 * s);
-    p[k + half] = f32_to_bf16_rne(x2 * c + x1 * s);
+    const long long r = i / ipr;
+    const int hc = (int)(i - r * ipr), h = hc / cpr, k0 = (hc - h * cpr) * 8;
+    const float pos = (float)(r % seq);
+    uint16_t* p = base + r * ld + (long long)h * dim + k0;
+    const uint4 a = *reinterpret_cast<const uint4*>(p), b = *reinterpret_cast<const uint4*>(p + half);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+    uint32_t ya[4], yb[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float o1[2], o2[2];
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int k = k0 + 2 * j + e;
+        const float inv_freq = exp2f(-log2_theta * (2.0f * k / (float)dim));
+        float sn, cs;
+        sincosf(pos * inv_freq, &sn, &cs);
+        const float x1 = bf16_to_f32((uint16_t)(aw[j] >> (16 * e))), x2 = bf16_to_f32((uint16_t)(bw[j] >> (16 * e)));
+        o1[e] = x1 * cs - x2 * sn;
+        o2[e] = x2 * cs + x1 * sn;
+      }
+      ya[j] = pack_bf16x2(o1[0], o1[1]);
+      yb[j] = pack_bf16x2(o2[0], o2[1]);
+    }
+    *reinterpret_cast<uint4*>(p) = make_uint4(ya[0], ya[1], ya[2], ya[3]);
+    *reinterpret_cast<uint4*>(p + half) = make_uint4(yb[0], yb[1], yb[2], yb[3]);
   }
 }
 
@@ -233,15 +274,19 @@ int32_t launch_kda_gate(const uint16_t* raw, long long ldraw, const uint16_t* rb
 int32_t launch_kda_post(const uint16_t* o, const uint16_t* og, long long ldog, const uint16_t* n0, const uint16_t* n1,
                         long long split, int heads, long long rows, float eps, uint16_t* out, cudaStream_t s) {
   long long groups = rows * heads;
-  kda_post_kernel<<<warp_rows_grid(groups, 8), 256, 0, s>>>(o, og, ldog, n0, n1 ? n1 : n0, n1 ? split : rows, heads,
-                                                             groups, eps, out);
+  if (((uintptr_t)o | (uintptr_t)og | (uintptr_t)out | (uintptr_t)n0 | (uintptr_t)(n1 ? n1 : n0)) & 15u || ldog % 8)
+    return set_error(ENNX_B200_INVALID_ARGUMENT, "kda_post: operands must be 16-byte aligned");
+  kda_post_kernel<<<(unsigned)((groups + 15) / 16), 256, 0, s>>>(o, og, ldog, n0, n1 ? n1 : n0, n1 ? split : rows,
+                                                                  heads, groups, eps, out);
   ENNX_LAUNCH_CHECK("kda_post");
   return ENNX_B200_OK;
 }
 
 int32_t launch_rope(uint16_t* base, long long ld, int heads, int dim, long long rows, int seq, float theta,
                     cudaStream_t s) {
-  long long total = rows * heads * (long long)(dim / 2);
+  if (dim % 16 || ld % 8 || ((uintptr_t)base & 15u))
+    return set_error(ENNX_B200_UNSUPPORTED, "rope: head width must be a multiple of 16 with 16-byte aligned rows");
+  long long total = rows * heads * (long long)(dim / 16);
   rope_kernel<<<stride_grid(total, 256), 256, 0, s>>>(base, ld, heads, dim, rows, seq, log2f(theta));
   ENNX_LAUNCH_CHECK("rope");
   return ENNX_B200_OK;

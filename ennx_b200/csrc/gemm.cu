@@ -460,12 +460,16 @@ constexpr int PB_GROUP_THREADS = 32 * PB_TWARPS / PB_TGROUPS;
 constexpr int PB_THREADS = 64 + 32 * EPI_WARPS + 32 * PB_TWARPS + 32;  // + the B producer warp: 608
 constexpr int PB_BPROD_WARP = 2 + EPI_WARPS + PB_TWARPS;
 // K per stage 64 (128-byte swizzled rows: one L2 request moves a whole
-// line, where 64-byte rows took twice the requests); the B ring deeper than
-// the A ring, since a B stage also waits for its rewrite (measured: 2 A + 4 B
-// stages 20 % faster than 6 + 6 stages of K 32, and than 3 + 3 of K 64)
+// line, where 64-byte rows took twice the requests).  A B stage lives
+// longer than an A stage (load, rewrite by the transform warps, then MMA),
+// and an A stage is freed only when the MMA two stages back completes, so
+// both rings want depth: the kernel has no epilogue staging (direct 16-byte
+// stores) and a 2 KB table area, which makes room for 3 A + 4 B stages of
+// 32 KB in the 227 KB of shared memory.  (Measured: 2 + 4 stages 20 %
+// faster than 6 + 6 stages of K 32, and than 3 + 3 of K 64.)
 #ifndef PB_BK_DEF
 #define PB_BK_DEF 64
-#define PB_NA_DEF 2
+#define PB_NA_DEF 3
 #define PB_NB_DEF 4
 #endif
 constexpr int PB_BK = PB_BK_DEF;                              // K per stage
@@ -475,7 +479,9 @@ constexpr int PB_SW = PB_BK * 2;                              // swizzle span = 
 constexpr int PB_CH = PB_TILE / 16 / PB_GROUP_THREADS;        // 16-byte chunks of W (and of E) per transform thread
 __device__ __forceinline__ uint64_t pb_desc(uint32_t a) { return PB_SW == 128 ? smem_desc_sw128(a) : smem_desc_sw64(a); }
 constexpr uint32_t PB_IDESC = idesc_bf16_f32(256, BN);
-static_assert((PB_NA + PB_NB) * 2 * PB_TILE <= STAGES * STAGE_BYTES, "perturbed-B rings fit the ring space");
+constexpr int PB_TABLES = 2048;
+constexpr int PB_SMEM_BYTES = 1024 /*align*/ + (PB_NA + PB_NB) * 2 * PB_TILE + PB_TABLES;
+static_assert(PB_SMEM_BYTES <= 232448, "perturbed-B rings and tables fit 227 KB of shared memory");
 static_assert(PB_TGROUPS <= PB_NB, "each transform group starts on its own stage");
 static_assert(PB_TILE / 16 == PB_CH * PB_GROUP_THREADS, "whole 16-byte chunks of W and E per transform thread");
 static_assert(PB_THREADS * 96 <= 65536, "register budget");
@@ -499,7 +505,7 @@ struct PbUnit {
   int e, mt, nt;
 };
 
-static_assert(sizeof(PbSmem) <= 4096, "perturbed-B barriers and tables fit their area");
+static_assert(sizeof(PbSmem) <= PB_TABLES, "perturbed-B barriers and tables fit their area");
 
 __device__ __forceinline__ PbUnit decode_pb(const PbSmem& s, int pairs, int n_tiles, int unit) {
   int lo = 0, hi = pairs - 1;
@@ -535,8 +541,7 @@ __global__ void __maxnreg__(96)
   uint8_t* ring = smem_raw + (((raw_addr + 1023u) & ~1023u) - raw_addr);
   uint8_t* ring_a = ring;                                // PB_NA x [A+ | A-]
   uint8_t* ring_b = ring + PB_NA * 2 * PB_TILE;          // PB_NB x [W | E]
-  uint8_t* epi_smem = ring + STAGES * STAGE_BYTES;
-  PbSmem& s = *reinterpret_cast<PbSmem*>(epi_smem + EPI_WARPS * EPI_BUF);
+  PbSmem& s = *reinterpret_cast<PbSmem*>(ring + (PB_NA + PB_NB) * 2 * PB_TILE);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rank = (int)cluster_ctarank();
@@ -670,7 +675,7 @@ __global__ void __maxnreg__(96)
     const int ew = warp - 2;
     const int q = warp & 3;
     const int half = ew >> 2;
-    uint8_t* stg = epi_smem + ew * EPI_BUF;
+    uint8_t* stg = ring;  // unused: no TMA stores in this kernel (Args::has_tmc = 0)
     int it = 0;
     for (int unit = first; unit < total; unit += stride, ++it) {
       if (!mbar_wait(&s.tfull, it & 1, a.err)) { s.abort_flag = 1; break; }
@@ -907,13 +912,10 @@ int32_t gemm_bf16_perturbed(const ennx_b200_gemm_params* p, const uint16_t* A, c
   ENNX_TRY(make_tmap_2d_bf16_sw(&ta, A, (uint64_t)K, (uint64_t)M, (uint64_t)p->lda, PB_BK, BM, PB_SW));
   ENNX_TRY(make_tmap_2d_bf16_sw(&tw, W, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, PB_BK, BM, PB_SW));
   ENNX_TRY(make_tmap_2d_bf16_sw(&te, E, (uint64_t)K, (uint64_t)b_rows, (uint64_t)p->ldb, PB_BK, BM, PB_SW));
-  memset(&tc, 0, sizeof(tc));
+  memset(&tc, 0, sizeof(tc));  // no TMA stores in this kernel
   const bool bf16_out = epi == ENNX_B200_EPI_BF16 || epi == ENNX_B200_EPI_SWIGLU || epi == ENNX_B200_EPI_ROWSCALE;
-  if (bf16_out) {
-    const long long out_cols = epi == ENNX_B200_EPI_SWIGLU ? N / 2 : N;
-    ENNX_TRY(make_tmap_2d_bf16(&tc, C, (uint64_t)out_cols, (uint64_t)M, (uint64_t)p->ldc, 32, 32, false));
-  }
   Args a = make_args(p, C, bf16_out);
+  a.has_tmc = 0;  // epilogue: direct 16-byte stores (its shared memory went to the rings)
   a.err = device_error_word();
   if (!a.err) return set_error(ENNX_B200_CUDA_ERROR, "gemm_perturbed: no device error word");
   PbArgs pb;
@@ -921,7 +923,7 @@ int32_t gemm_bf16_perturbed(const ennx_b200_gemm_params* p, const uint16_t* A, c
   int dev = 0;
   cudaGetDevice(&dev);
   if (!g_pb_attr_set[dev]) {
-    ENNX_CUDA(cudaFuncSetAttribute(gemm_pb_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES),
+    ENNX_CUDA(cudaFuncSetAttribute(gemm_pb_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PB_SMEM_BYTES),
               "gemm_perturbed: set smem");
     g_pb_attr_set[dev] = true;
   }
@@ -932,7 +934,7 @@ int32_t gemm_bf16_perturbed(const ennx_b200_gemm_params* p, const uint16_t* A, c
   memset(&cfg, 0, sizeof(cfg));
   cfg.gridDim = dim3((unsigned)(2 * clusters));
   cfg.blockDim = dim3(PB_THREADS);
-  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.dynamicSmemBytes = PB_SMEM_BYTES;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;

@@ -486,6 +486,19 @@ def run_op(args):
         fn = lambda: ops.moe_layer(x, wr, wgu, wd, topk)  # noqa: E731
         flops = 2.0 * T * H * E + 2.0 * T * topk * 3 * H * I
         nbytes, unit_name = 2.0 * (wgu.numel() + wd.numel() + 2 * T * H), "MoE 16384x2048, 64 experts top-8"
+    elif args.op in ("noise", "noise_step"):
+        # The perturbation of one MoE layer's expert weights for one pair
+        # (64 experts x 3 x 768 x 2048 = 302 M weights) as the forward's noise
+        # stream runs it, alone on the GPU: W -> bf16(W + e), bf16(W - e)
+        # (6 B per weight), or the noise step e alone (2 B per weight)
+        n = 64 * 3 * 768 * 2048
+        w = rn(n, std=0.02)
+        plus = torch.empty_like(w)
+        step = args.op == "noise_step"
+        minus = None if step else torch.empty_like(w)
+        fn = lambda: ops.perturb_bf16(None if step else w, 7, 3, 11, 1e-3, plus=plus, minus=minus)  # noqa: E731
+        flops, nbytes = 0.0, (2.0 if step else 6.0) * n
+        unit_name = "Philox noise, one MoE layer's experts (302 M weights), " + ("noise step e" if step else "W +/- e")
     else:  # kda
         B, T, H = 8, 4096, 16
         q = torch.nn.functional.normalize(torch.randn(B, T, H, 128, generator=g, device="cuda"), dim=-1).bfloat16()
@@ -748,7 +761,8 @@ def run_decode(args):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--op", choices=["forward", "gemm", "gemm_pb", "gemm_pb_moe", "attention", "moe", "kda", "search",
+    ap.add_argument("--op", choices=["forward", "gemm", "gemm_pb", "gemm_pb_moe", "attention", "moe", "kda", "noise",
+                                     "noise_step", "search",
                                      "packed_prefill",
                                      "decode"],
                     default="forward")

@@ -96,10 +96,18 @@ def gemm_perturbed(a: torch.Tensor, w: torch.Tensor, e: torch.Tensor, out: torch
 
 def perturb_bf16(w: torch.Tensor, seed: int, pair: int, tensor: int, sigma: float,
                  plus: torch.Tensor | None = None, minus: torch.Tensor | None = None):
-    """(W + sigma*eps, W - sigma*eps) with Philox noise keyed by (seed, pair, tensor, element)."""
-    _check_dev(w)
-    plus = torch.empty_like(w) if plus is None else plus
-    _abi.call("ennx_b200_perturb_bf16", _ptr(w), w.numel(), seed, pair, tensor, sigma, _ptr(plus), _ptr(minus),
+    """(W + sigma*eps, W - sigma*eps) with Philox noise keyed by (seed, pair, tensor, element).
+    w None: `plus` receives the noise step bf16(sigma*eps) itself (minus must be None)."""
+    if w is None:
+        if plus is None or minus is not None:
+            raise ValueError("the noise step alone needs `plus` and no `minus`")
+        _check_dev(plus)
+        n = plus.numel()
+    else:
+        _check_dev(w)
+        plus = torch.empty_like(w) if plus is None else plus
+        n = w.numel()
+    _abi.call("ennx_b200_perturb_bf16", _ptr(w), n, seed, pair, tensor, sigma, _ptr(plus), _ptr(minus),
               _stream())
     return plus, minus
 

@@ -186,39 +186,46 @@ __global__ void kda_post_kernel(const uint16_t* __restrict__ o, const uint16_t* 
 }
 
 // Rotate-half RoPE in place on `heads` heads of width dim starting at base + r*ld.
-// Position of row r is r % seq.  One thread per (row, head, 8 rotary pairs):
-// 16-byte loads of x[k0..k0+7] and x[k0+half..k0+half+7]; same per-element
-// formula as a scalar loop (inv_freq = 2^(-log2(theta) 2k/dim), angle = pos inv_freq).
+// Position of row r is r % seq.  One thread per (row, 8 rotary pairs): the
+// eight angles (inv_freq = 2^(-log2(theta) 2k/dim), angle = pos inv_freq,
+// the per-element formula) are computed once and applied to that chunk of
+// every head, with 16-byte loads of x[k0..k0+7] and x[k0+half..k0+half+7].
 __global__ void rope_kernel(uint16_t* __restrict__ base, long long ld, int heads, int dim, long long rows, int seq,
                             float log2_theta) {
-  const int half = dim / 2, cpr = half / 8, ipr = heads * cpr;  // chunks per head, per row
-  const long long total = rows * ipr;
+  const int half = dim / 2, cpr = half / 8;  // 8-pair chunks per head
+  const long long total = rows * cpr;
   for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
-    const long long r = i / ipr;
-    const int hc = (int)(i - r * ipr), h = hc / cpr, k0 = (hc - h * cpr) * 8;
+    const long long r = i / cpr;
+    const int k0 = (int)(i - r * cpr) * 8;
     const float pos = (float)(r % seq);
-    uint16_t* p = base + r * ld + (long long)h * dim + k0;
-    const uint4 a = *reinterpret_cast<const uint4*>(p), b = *reinterpret_cast<const uint4*>(p + half);
-    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
-    uint32_t ya[4], yb[4];
+    float sn[8], cs[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      float o1[2], o2[2];
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int k = k0 + 2 * j + e;
-        const float inv_freq = exp2f(-log2_theta * (2.0f * k / (float)dim));
-        float sn, cs;
-        sincosf(pos * inv_freq, &sn, &cs);
-        const float x1 = bf16_to_f32((uint16_t)(aw[j] >> (16 * e))), x2 = bf16_to_f32((uint16_t)(bw[j] >> (16 * e)));
-        o1[e] = x1 * cs - x2 * sn;
-        o2[e] = x2 * cs + x1 * sn;
-      }
-      ya[j] = pack_bf16x2(o1[0], o1[1]);
-      yb[j] = pack_bf16x2(o2[0], o2[1]);
+    for (int e = 0; e < 8; ++e) {
+      const float inv_freq = exp2f(-log2_theta * (2.0f * (k0 + e) / (float)dim));
+      sincosf(pos * inv_freq, &sn[e], &cs[e]);
     }
-    *reinterpret_cast<uint4*>(p) = make_uint4(ya[0], ya[1], ya[2], ya[3]);
-    *reinterpret_cast<uint4*>(p + half) = make_uint4(yb[0], yb[1], yb[2], yb[3]);
+    uint16_t* row = base + r * ld + k0;
+#pragma unroll 4
+    for (int h = 0; h < heads; ++h) {
+      uint16_t* p = row + (long long)h * dim;
+      const uint4 a = *reinterpret_cast<const uint4*>(p), b = *reinterpret_cast<const uint4*>(p + half);
+      const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+      uint32_t ya[4], yb[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float o1[2], o2[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float x1 = bf16_to_f32((uint16_t)(aw[j] >> (16 * e))), x2 = bf16_to_f32((uint16_t)(bw[j] >> (16 * e)));
+          o1[e] = x1 * cs[2 * j + e] - x2 * sn[2 * j + e];
+          o2[e] = x2 * cs[2 * j + e] + x1 * sn[2 * j + e];
+        }
+        ya[j] = pack_bf16x2(o1[0], o1[1]);
+        yb[j] = pack_bf16x2(o2[0], o2[1]);
+      }
+      *reinterpret_cast<uint4*>(p) = make_uint4(ya[0], ya[1], ya[2], ya[3]);
+      *reinterpret_cast<uint4*>(p + half) = make_uint4(yb[0], yb[1], yb[2], yb[3]);
+    }
   }
 }
 
@@ -286,7 +293,7 @@ int32_t launch_rope(uint16_t* base, long long ld, int heads, int dim, long long 
                     cudaStream_t s) {
   if (dim % 16 || ld % 8 || ((uintptr_t)base & 15u))
     return set_error(ENNX_B200_UNSUPPORTED, "rope: head width must be a multiple of 16 with 16-byte aligned rows");
-  long long total = rows * heads * (long long)(dim / 16);
+  long long total = rows * (long long)(dim / 16);
   rope_kernel<<<stride_grid(total, 256), 256, 0, s>>>(base, ld, heads, dim, rows, seq, log2f(theta));
   ENNX_LAUNCH_CHECK("rope");
   return ENNX_B200_OK;

@@ -274,26 +274,41 @@ __global__ void __launch_bounds__(256) moe_scatter_gather_kernel(
     perm_pos[t * top_k + lane] = pos;
     perm_gate[pos] = gate_scale * gate[t * top_k + lane];
   }
-  // the row is read in batches of eight 16-byte chunks per lane (all loads
-  // in flight before the first store), then written to each slot
+  // the row goes through this warp's 4 KB of shared memory in segments of
+  // 2048 elements: eight 16-byte loads per lane (all in flight), one store
+  // to shared memory, then one bulk copy (TMA engine) per slot
+  __shared__ __align__(128) uint4 seg_buf[8][256];
+  uint4* buf = seg_buf[warp];
+  const uint32_t buf_s = smem_u32(buf);
   const uint16_t* src = x + t * ldx;
   int slot[8];
 #pragma unroll
   for (int r = 0; r < 8; ++r) slot[r] = __shfl_sync(0xffffffffu, pos, r);
-  for (int c0 = lane * 8; c0 < width; c0 += 8 * 256) {
+  for (int s0 = 0; s0 < width; s0 += 2048) {
+    const int seg = min(2048, width - s0);
     uint4 v[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      if (c0 + j * 256 < width) v[j] = ldg_stream_v4(src + c0 + j * 256);
+      if (lane * 8 + j * 256 < seg) v[j] = ldg_stream_v4(src + s0 + lane * 8 + j * 256);
+    if (lane == 0) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");  // previous segment read out
+    __syncwarp();
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      if (r >= top_k) break;
-      uint16_t* dst = xperm + (long long)slot[r] * width + c0;
-#pragma unroll
-      for (int j = 0; j < 8; ++j)
-        if (c0 + j * 256 < width) *reinterpret_cast<uint4*>(dst + j * 256) = v[j];
+    for (int j = 0; j < 8; ++j)
+      if (lane * 8 + j * 256 < seg) buf[lane + 32 * j] = v[j];
+    fence_proxy_async();
+    __syncwarp();
+    if (lane == 0) {
+      for (int r = 0; r < top_k; ++r) {
+        uint16_t* dst = xperm + (long long)slot[r] * width + s0;
+        asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(dst), "r"(buf_s),
+                     "r"(seg * 2)
+                     : "memory");
+      }
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     }
   }
+  if (lane == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+  __syncwarp();
 }
 
 // out = residual + sum_r y[perm_pos[t, r]] (fp32 sum in pick order, one

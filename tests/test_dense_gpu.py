@@ -152,6 +152,11 @@ def test_noise_step_matches_oracle():
     e = torch.empty(n, dtype=torch.int16, device="cuda")
     st = _abi.lib().ennx_b200_perturb_bf16(None, n, 0xDEADBEEF12345678, 5, 17, 1e-3, ptr(e), None, stream())
     assert st == 0
+    # the Python form (ops.perturb_bf16 with w None) is the same call
+    from ennx_b200 import ops
+    e2 = torch.empty(n, dtype=torch.bfloat16, device="cuda")
+    ops.perturb_bf16(None, 0xDEADBEEF12345678, 5, 17, 1e-3, plus=e2)
+    assert torch.equal(e2.view(torch.int16), e)
     ref = O.from_bf16_bits(O.noise_step_bf16(n, 0xDEADBEEF12345678, 5, 17, 1e-3)).astype(np.float64)
     got = O.from_bf16_bits(host_u16(e)).astype(np.float64)
     # Box-Muller on the SFU vs fp64 libm: sigma*eps agrees to ~1e-6 of sigma,

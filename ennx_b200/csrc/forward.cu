@@ -73,6 +73,7 @@ struct MoeBuffers {
   int *idx, *counters, *offsets, *perm_pos;
   float *gate, *perm_gate;
   uint16_t *xperm, *act, *yperm;
+  float* router_wt;  // both router weight sets as fp32, k-major per 64-expert tile
 };
 
 void carve_moe(Carver& c, long long tokens, int hidden, int experts, int top_k, int width, int sets, MoeBuffers& m) {
@@ -86,6 +87,7 @@ void carve_moe(Carver& c, long long tokens, int hidden, int experts, int top_k, 
   m.xperm = c.take<uint16_t>(rows * hidden);
   m.act = c.take<uint16_t>(rows * width);
   m.yperm = c.take<uint16_t>(rows * hidden);
+  m.router_wt = c.take<float>(2 * (size_t)((experts + 63) / 64) * hidden * 64);
   m.logits = nullptr;
 }
 
@@ -103,7 +105,7 @@ int32_t run_moe(const uint16_t* x, const uint16_t* wr0, const uint16_t* wr1, con
     // pick counts (router) -> slots and row copies in expert-major order (one pass)
     ENNX_CUDA(cudaMemsetAsync(m.counters, 0, sizeof(int) * 2 * sets * experts, s), "moe counters");
     ENNX_TRY(launch_router_topk(x, hidden, wr0, sets > 1 ? wr1 : nullptr, split, tokens, hidden, experts, top_k,
-                                m.logits, m.idx, m.gate, s, m.counters));
+                                m.logits, m.idx, m.gate, s, m.counters, m.router_wt));
     ENNX_TRY(launch_moe_scatter_gather(m.idx, m.gate, residual_scale, tokens, top_k, experts, split, sets, m.counters,
                                        m.offsets, m.counters + sets * experts, m.perm_pos, m.perm_gate, x, hidden,
                                        hidden, m.xperm, s));

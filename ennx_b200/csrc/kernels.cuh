@@ -26,7 +26,10 @@ int32_t launch_rope(uint16_t* base, long long ld, int heads, int dim, long long 
 int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0, const uint16_t* w1, long long split,
                            long long tokens, int hidden, int experts, int top_k, float* logits, int* idx,
                            float* gate, cudaStream_t s,
-                           int* counts = nullptr);
+                           int* counts = nullptr,
+                           // optional scratch of 2 * ceil(experts / 64) * hidden * 64 floats: the
+                           // router weights converted once per call instead of once per block
+                           float* wt = nullptr);
 // Expert-major permutation and row copy in one pass.  Group of (token t,
 // rank r) is set(t) * experts + idx[t, r] (set = t >= split); `counts` are the
 // per-group picks (launch_router_topk with counts), `cursor` int[groups]

@@ -55,10 +55,28 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src, bool ok) 
                : "memory");
 }
 
+// The router weights of both sets as fp32, k-major per tile of RE experts:
+// wt[set][tile][k][RE] (experts past the end are zero).  One conversion per
+// call, so the router blocks copy their expert operand chunks (RK x RE fp32,
+// 16 KB, contiguous) straight into shared memory instead of each converting
+// the same rows.
+__global__ void router_wt_kernel(const uint16_t* __restrict__ w0, const uint16_t* __restrict__ w1, int hidden,
+                                 int experts, int tiles, float* __restrict__ wt) {
+  const long long per_set = (long long)tiles * hidden * RE;
+  const long long total = 2 * per_set;
+  for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+    const int set = (int)(i / per_set);
+    const long long j = i - set * per_set;
+    const int tile = (int)(j / ((long long)hidden * RE));
+    const int k = (int)((j / RE) % hidden), e = tile * RE + (int)(j % RE);
+    wt[i] = e < experts ? bf16_to_f32((set ? w1 : w0)[(long long)e * hidden + k]) : 0.0f;
+  }
+}
+
 __global__ void __launch_bounds__(kRouterThreads, 2) router_topk_kernel(
     const uint16_t* __restrict__ x, long long ldx, const uint16_t* __restrict__ w0, const uint16_t* __restrict__ w1,
     long long split, long long tokens, int hidden, int experts, int top_k, float* __restrict__ logits,
-    int* __restrict__ idx, float* __restrict__ gate, int* __restrict__ counts) {
+    int* __restrict__ idx, float* __restrict__ gate, int* __restrict__ counts, const float* __restrict__ wt) {
   extern __shared__ __align__(16) float rsm[];
   __shared__ int hist[256];  // picks per expert of this block's tokens (counts != nullptr)
   float* As = rsm;                  // [2][RK][RT]
@@ -71,6 +89,8 @@ __global__ void __launch_bounds__(kRouterThreads, 2) router_topk_kernel(
   const long long nb0 = (split + RT - 1) / RT;
   long long tb, te;
   const uint16_t* w;
+  const int set = (long long)blockIdx.x < nb0 ? 0 : 1;
+  const int tiles = (experts + RE - 1) / RE;
   if ((long long)blockIdx.x < nb0) {
     tb = (long long)blockIdx.x * RT; te = min(split, tb + RT); w = w0;
   } else {
@@ -90,12 +110,18 @@ __global__ void __launch_bounds__(kRouterThreads, 2) router_topk_kernel(
           cp_async16(xst + li * 8, x + (ok ? (tb + t) * ldx + c * RK + 8 * q : 0), ok);
         }
       }
+      if (wt) {  // fp32 operand chunk, copied straight into Bs[c & 1]
+        const float* src = wt + (((long long)set * tiles + e0 / RE) * hidden + (long long)c * RK) * RE;
+        float* dst = Bs + (c & 1) * RK * RE;
+        for (int li = tid; li < RK * RE / 4; li += kRouterThreads) cp_async16(dst + 4 * li, src + 4 * li, true);
+      } else {
 #pragma unroll
-      for (int i = 0; i < kWPer; ++i) {
-        const int li = tid + i * kRouterThreads, e = e0 + li % RE, qe = li / RE;
-        if (li < kWLoads) {
-          const bool ok = e < experts;
-          cp_async16(wst + li * 8, w + (ok ? (long long)e * hidden + c * RK + 8 * qe : 0), ok);
+        for (int i = 0; i < kWPer; ++i) {
+          const int li = tid + i * kRouterThreads, e = e0 + li % RE, qe = li / RE;
+          if (li < kWLoads) {
+            const bool ok = e < experts;
+            cp_async16(wst + li * 8, w + (ok ? (long long)e * hidden + c * RK + 8 * qe : 0), ok);
+          }
         }
       }
       asm volatile("cp.async.commit_group;" ::: "memory");
@@ -120,7 +146,7 @@ __global__ void __launch_bounds__(kRouterThreads, 2) router_topk_kernel(
 #pragma unroll
       for (int i = 0; i < kWPer; ++i) {
         const int li = tid + i * kRouterThreads, e = li % RE, qe = li / RE;
-        if (li >= kWLoads) break;
+        if (wt || li >= kWLoads) break;
         const uint4 v = *reinterpret_cast<const uint4*>(wst + li * 8);
         const uint32_t wv[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
@@ -367,7 +393,7 @@ __global__ void moe_combine_kernel(const uint16_t* __restrict__ y, const int* __
 
 int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0, const uint16_t* w1, long long split,
                            long long tokens, int hidden, int experts, int top_k, float* logits, int* idx,
-                           float* gate, cudaStream_t s, int* counts) {
+                           float* gate, cudaStream_t s, int* counts, float* wt) {
   if (top_k < 1 || top_k > 8 || top_k > experts)
     return set_error(ENNX_B200_INVALID_ARGUMENT, "router: top_k must be in [1, min(8, experts)]");  // forward_program.rs:428
   if (experts > 256) return set_error(ENNX_B200_UNSUPPORTED, "router: at most 256 experts");
@@ -390,8 +416,15 @@ int32_t launch_router_topk(const uint16_t* x, long long ldx, const uint16_t* w0,
               "router smem");
     attr[dev] = true;
   }
+  if (wt) {
+    if ((uintptr_t)wt & 15u) return set_error(ENNX_B200_INVALID_ARGUMENT, "router: fp32 weight scratch must be 16-byte aligned");
+    const long long n = 2LL * ((experts + RE - 1) / RE) * hidden * RE;
+    router_wt_kernel<<<(unsigned)((n + 255) / 256 < 4LL * sm_count() ? (n + 255) / 256 : 4LL * sm_count()), 256, 0, s>>>(
+        w0, w1, hidden, experts, (experts + RE - 1) / RE, wt);
+    ENNX_LAUNCH_CHECK("router_wt");
+  }
   router_topk_kernel<<<(unsigned)blocks, kRouterThreads, smem, s>>>(x, ldx, w0, w1, split, tokens, hidden, experts,
-                                                                      top_k, logits, idx, gate, counts);
+                                                                      top_k, logits, idx, gate, counts, wt);
   ENNX_LAUNCH_CHECK("router_topk");
   return ENNX_B200_OK;
 }

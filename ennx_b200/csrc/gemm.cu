@@ -837,7 +837,11 @@ int32_t gemm_bf16(const ennx_b200_gemm_params* p, const uint16_t* A, const uint1
   const int epi = p->epilogue;
   // CTA-pair variant for problems with enough rows to fill 256-row tiles;
   // ENNX_B200_GEMM_PAIR=0/1 forces a variant (tests exercise both).
-  bool pair = M >= 1024;
+  // Grouped problems with device-side offsets (the expert GEMMs) take the
+  // CTA pair only at >= 1024 rows per group on average: at ~512 rows a
+  // group's last 256-row tile is often mostly padding, and 128-row tiles
+  // waste less (measured: the population step 739 -> 729 ms).
+  bool pair = M >= 1024 && (!p->group_offsets || (long long)M / G >= 1024);
   if (const char* e = getenv("ENNX_B200_GEMM_PAIR")) pair = e[0] == '1';
   const int brows = pair ? Geo<true>::BROWS : Geo<false>::BROWS;
 
